@@ -1,0 +1,77 @@
+"""ctypes binding of libhla_s6.so (the C ABI declared in include/hla_s6.h).
+
+The shared library is built in-tree by ``build.py``.  There is no fallback: if the library
+is missing or was built for another ABI version, importing the ops raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get('HLA_S6_LIB', _PKG / 'libhla_s6.so'))
+ABI_VERSION = 1
+
+OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
+
+_c_void_p, _i32, _i64, _f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+P = _c_void_p
+
+# name -> argtypes (restype is always int32 status unless noted)
+SIGNATURES = {
+    'hla_s6_history_attention': [P, _i64, _i64, P, _i64, _i64, _i64, P, _i64, _i32, P, P, _i32, _i32, _i32, _i32,
+                                 _f32, _i32, P, _i64, P, _i64, _i64, P, P, P],
+    'hla_s6_history_partials': [P, _i64, _i64, P, _i64, _i64, _i64, P, _i64, _i32, P, _i32, _i32, _i32, _i32, _f32,
+                                _i32, P, _i64, P, P],
+    'hla_s6_history_reduce': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i64, _i64, P, P, P],
+    'hla_s6_history_plan': [_i32, _i32, _i32, _i32, _i32, _i64, P, P, P],
+}
+
+_lib = None
+
+
+def load():
+    """Load the library once; raises RuntimeError when it is absent or mismatched."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f'libhla_s6.so not found at {LIB_PATH}: build it with '
+                           f'`python {_PKG / "build.py"}` (no CPU fallback exists)')
+    lib = ctypes.CDLL(str(LIB_PATH))
+    lib.hla_s6_version.restype = ctypes.c_int
+    lib.hla_s6_last_error.restype = ctypes.c_char_p
+    if lib.hla_s6_version() != ABI_VERSION:
+        raise RuntimeError(f'libhla_s6 ABI {lib.hla_s6_version()} != expected {ABI_VERSION}; rebuild it')
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int32
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str):
+    if rc == OK:
+        return
+    msg = load().hla_s6_last_error().decode(errors='replace')
+    if rc == EINVAL:
+        raise ValueError(f'{what}: {msg}')
+    raise RuntimeError(f'{what}: {msg}')
+
+
+def call(name: str, *args):
+    rc = getattr(load(), name)(*args)
+    check(rc, name)
+
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)

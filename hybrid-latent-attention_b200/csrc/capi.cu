@@ -1,0 +1,226 @@
+// C-ABI surface of libhla_s6: argument validation, error reporting, TMA descriptor cache
+// and the exported history entry points.  Declarations live in include/hla_s6.h.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/hla_s6.h"
+#include "hla_s6_internal.h"
+
+namespace hla {
+
+static thread_local char g_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return kStatusOk;
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return kStatusCuda;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct TmapKey {
+  const void* ptr;
+  int64_t nb, sb, sr;
+  int W, page, dev;
+  bool operator==(const TmapKey& o) const {
+    return ptr == o.ptr && nb == o.nb && sb == o.sb && sr == o.sr && W == o.W && page == o.page && dev == o.dev;
+  }
+};
+
+static std::mutex g_tmap_mu;
+static TmapKey g_tmap_keys[32];
+static CUtensorMap g_tmap_vals[32];
+static int g_tmap_used = 0, g_tmap_next = 0;
+
+int latent_cache_tmap(CUtensorMap* map, const void* cache, int64_t num_blocks, int64_t st_block, int64_t st_row,
+                      int W, int page) {
+  if (reinterpret_cast<uintptr_t>(cache) % 16) {
+    set_error("latent cache base must be 16-byte aligned");
+    return kStatusInvalid;
+  }
+  if ((st_row * 2) % 16 || (st_block * 2) % 16 || st_row < 2 * W || st_block < 1) {
+    set_error("latent cache strides must be multiples of 8 elements (row %lld, block %lld)",
+              static_cast<long long>(st_row), static_cast<long long>(st_block));
+    return kStatusInvalid;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const TmapKey key{cache, num_blocks, st_block, st_row, W, page, dev};
+  {
+    std::lock_guard<std::mutex> lock(g_tmap_mu);
+    for (int i = 0; i < g_tmap_used; ++i)
+      if (g_tmap_keys[i] == key) {
+        *map = g_tmap_vals[i];
+        return kStatusOk;
+      }
+  }
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return kStatusCuda;
+  }
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(page), static_cast<cuuint64_t>(2 * W / 64),
+                        static_cast<cuuint64_t>(num_blocks)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(st_row * 2), 128, static_cast<cuuint64_t>(st_block * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(page), static_cast<cuuint32_t>(2 * W / 64), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(cache), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for the latent cache", static_cast<int>(r));
+    return kStatusCuda;
+  }
+  std::lock_guard<std::mutex> lock(g_tmap_mu);
+  const int slot = g_tmap_used < 32 ? g_tmap_used++ : (g_tmap_next++ % 32);
+  g_tmap_keys[slot] = key;
+  g_tmap_vals[slot] = *map;
+  return kStatusOk;
+}
+
+static int check_history_args(const HistoryArgs& a) {
+  if (a.T < 0 || a.H < 1 || a.H > 16) {
+    set_error("history attention needs 1..16 query heads per KV head (got H=%d, T=%d)", a.H, a.T);
+    return kStatusInvalid;
+  }
+  if ((a.q_st % 2) || (a.q_sh % 2) || (reinterpret_cast<uintptr_t>(a.q) % 4)) {
+    set_error("q_lat needs even token/head strides and a unit last-dim stride");
+    return kStatusInvalid;
+  }
+  if (a.num_kv_splits < 1) {
+    set_error("num_kv_splits must be >= 1");
+    return kStatusInvalid;
+  }
+  if (a.page != 16 && a.page != 32) {
+    set_error("page size %d unsupported (16 or 32)", a.page);
+    return kStatusInvalid;
+  }
+  return kStatusOk;
+}
+
+static HistoryArgs make_history_args(const void* q, int64_t q_st, int64_t q_sh, const void* cache,
+                                     int64_t num_blocks, int64_t st_block, int64_t st_row, const int32_t* bt,
+                                     int64_t bt_st, int32_t max_blocks, const int32_t* ctx, int32_t T, int32_t H, int32_t W,
+                                     int32_t page, float scale, int32_t splits, float* ws, int64_t ws_floats,
+                                     int* err) {
+  HistoryArgs a;
+  a.q = q;
+  a.q_st = q_st;
+  a.q_sh = q_sh;
+  a.cache = cache;
+  a.num_blocks = num_blocks;
+  a.cache_st_block = st_block;
+  a.cache_st_row = st_row;
+  a.block_table = bt;
+  a.bt_st = bt_st;
+  a.max_blocks = max_blocks;
+  a.ctx = ctx;
+  a.T = T;
+  a.H = H;
+  a.W = W;
+  a.page = page;
+  a.scale = scale;
+  a.num_kv_splits = splits;
+  a.ws = ws;
+  a.ws_floats = ws_floats;
+  a.waves = 1;
+  a.err = err;
+  return a;
+}
+
+}  // namespace hla
+
+using namespace hla;
+
+extern "C" {
+
+int hla_s6_version(void) { return HLA_S6_ABI_VERSION; }
+
+const char* hla_s6_last_error(void) { return g_error; }
+
+int hla_s6_history_attention(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                             int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,
+                             const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                             const int32_t* ctx, const uint8_t* empty, int32_t num_tokens, int32_t num_heads, int32_t width,
+                             int32_t page, float scale, int32_t num_kv_splits, float* workspace,
+                             int64_t workspace_floats, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                             float* lse, int* error_flag, void* stream) {
+  HistoryArgs a = make_history_args(q_lat, q_stride_t, q_stride_h, cache, num_blocks, cache_stride_block,
+                                    cache_stride_row, block_table, block_table_stride, max_blocks, ctx, num_tokens, num_heads,
+                                    width, page, scale, num_kv_splits, workspace, workspace_floats, error_flag);
+  int rc = check_history_args(a);
+  if (rc) return rc;
+  HistoryPlan plan;
+  if ((rc = history_plan(a, &plan))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = history_split(a, plan, s))) return rc;
+  return history_reduce(a, plan, empty, out, out_stride_t, out_stride_h, nullptr, lse, s);
+}
+
+int hla_s6_history_partials(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                            int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,
+                            const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                            const int32_t* ctx, int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, float scale,
+                            int32_t num_kv_splits, float* workspace, int64_t workspace_floats, int* error_flag,
+                            void* stream) {
+  HistoryArgs a = make_history_args(q_lat, q_stride_t, q_stride_h, cache, num_blocks, cache_stride_block,
+                                    cache_stride_row, block_table, block_table_stride, max_blocks, ctx, num_tokens, num_heads,
+                                    width, page, scale, num_kv_splits, workspace, workspace_floats, error_flag);
+  int rc = check_history_args(a);
+  if (rc) return rc;
+  HistoryPlan plan;
+  if ((rc = history_plan(a, &plan))) return rc;
+  return history_split(a, plan, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_history_reduce(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,
+                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const uint8_t* empty,
+                          void* out, int64_t out_stride_t, int64_t out_stride_h, float* out_f32, float* lse,
+                          void* stream) {
+  HistoryArgs a = make_history_args(nullptr, 0, 0, nullptr, 0, 0, 0, nullptr, 0, 0, nullptr, num_tokens, num_heads,
+                                    width, page, 1.f, num_kv_splits, workspace, workspace_floats, nullptr);
+  HistoryPlan plan;
+  int rc = history_plan(a, &plan);
+  if (rc) return rc;
+  return history_reduce(a, plan, empty, out, out_stride_t, out_stride_h, out_f32, lse,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_history_plan(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, int32_t num_kv_splits,
+                        int64_t workspace_floats, int32_t* stream_mode, int32_t* grid, int32_t* slots) {
+  HistoryArgs a = make_history_args(nullptr, 0, 0, nullptr, 0, 0, 0, nullptr, 0, 0, nullptr, num_tokens, num_heads,
+                                    width, page, 1.f, num_kv_splits, reinterpret_cast<float*>(0x100),
+                                    workspace_floats, nullptr);
+  HistoryPlan plan;
+  int rc = history_plan(a, &plan);
+  if (rc) return rc;
+  if (stream_mode) *stream_mode = plan.stream_mode;
+  if (grid) *grid = plan.grid;
+  if (slots) *slots = plan.slots_cap;
+  return kStatusOk;
+}
+
+}  // extern "C"

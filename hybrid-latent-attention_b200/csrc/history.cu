@@ -1,0 +1,570 @@
+// Paged latent-history reader of the S6 decode path (SURVEY A1 + A2).
+//
+// Reference behaviour: hla/vllm_latent/s6_ops.py:117-161 (history_attention /
+// history_attention_kv) and its torch oracle s6_ops.py:204-222 (_history_reference):
+// a fully visible softmax of q_lat[T,H,W] over the first ctx[t] rows of an MQA latent cache
+// [num_blocks, 1, page, 2W] (row = K | V), paged through a per-token block table.  Only
+// block-table columns < ceil(ctx[t] / page) are read.  Empty rows give o = 0, lse = -inf.
+//
+// B200 design
+//  * one producer warp streams whole pages with a 4-D TMA tensor map
+//    (64-element inner box, rows, 64-column slabs, blocks) and SWIZZLE_128B into a STAGES-deep
+//    shared-memory ring (mbarrier complete_tx); no multicast - every CTA reads its own pages.
+//  * NC = W/128 consumer warps each own 128 latent columns.  Heads are the M = 16 dimension
+//    of mma.m16n8k16 (the 16 query heads share one KV head), keys are N, columns are K:
+//      S_w  = Q[:, cols_w] . K[keys, cols_w]^T   (partial scores, reduced across warps in smem)
+//      O_w += P . V[keys, cols_w]                (P reused from the score fragments, FA2 style)
+//  * stream-K partition: the grid splits the flattened (row, page) space evenly, so mixed
+//    lengths balance across the 148 SMs; each CTA emits one fp32 partial (o, lse) per row
+//    segment it touched into the caller's workspace.  CTA c writes row t's partial at slot
+//    c + t, and CTA 0 records each row's slot range in `meta`.
+//  * a reduce kernel (the Triton stage-2 equivalent) or the fused decode combine turns the
+//    partials into the op outputs.
+#include "common.cuh"
+#include "hla_s6_internal.h"
+
+namespace hla {
+
+struct HistoryParams {
+  const __nv_bfloat16* q;
+  int64_t q_st, q_sh;          // q strides (elements) for token and head; unit last stride
+  const int32_t* block_table;  // [T, max_blocks] per token
+  int64_t bt_st;
+  int32_t max_blocks;          // columns beyond it load as zeros (never read out of the table)
+  const int32_t* ctx;          // [T] rows of history to read
+  int32_t T, H;
+  float scale_log2;            // softmax scale * log2(e)
+  float* ws_o;                 // [slots][H][W] normalised partial outputs
+  float* ws_lse;               // [slots][H] natural-log partial lse
+  int2* meta;                  // [T] slot range per row (stream mode)
+  int32_t slots_cap;
+  int32_t grid;                // CTAs launched (stream mode)
+  int32_t stream_mode;         // 1: stream-K over pages, 0: one CTA per row
+  int* err;
+};
+
+template <int W, int PG>
+struct HistoryCfg {
+  static constexpr int NC = W / 128;                   // consumer warps
+  static constexpr int NT = PG / 8;                    // n8 key tiles per page
+  static constexpr int SLAB_BYTES = PG * 128;          // one 64-column slab of a page
+  static constexpr int PAGE_BYTES = PG * 2 * W * 2;    // K and V of a page, bf16
+  static constexpr int STAGES = PAGE_BYTES <= 16384 ? 4 : (PAGE_BYTES <= 32768 ? 3 : 2);
+  static constexpr int THREADS = (NC + 1) * 32;
+  static constexpr int XBUF_BYTES = 2 * NC * NT * 32 * 16;
+};
+
+__host__ __device__ inline int64_t stream_start(int64_t c, int64_t P, int64_t G) { return c * P / G; }
+
+// Largest CTA index c with stream_start(c) <= p.
+__host__ __device__ inline int64_t stream_owner(int64_t p, int64_t P, int64_t G) {
+  return ((p + 1) * G - 1) / P;
+}
+
+__device__ __forceinline__ uint32_t mask_pair(uint32_t v, int key_lo, int valid) {
+  if (key_lo >= valid) return 0u;
+  if (key_lo + 1 >= valid) return v & 0xffffu;
+  return v;
+}
+
+template <int W, int PG>
+__global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, 1)
+    history_split_kernel(const __grid_constant__ CUtensorMap tmap, const HistoryParams p) {
+  using C = HistoryCfg<W, PG>;
+  constexpr int NC = C::NC, NT = C::NT, STAGES = C::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  float4* xbuf = reinterpret_cast<float4*>(smem + STAGES * C::PAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::PAGE_BYTES + C::XBUF_BYTES);
+  uint64_t* empty = full + STAGES;
+  int* misc = reinterpret_cast<int*>(empty + STAGES);  // [0]=abort
+  int* pref = misc + 4;                                 // [T+1] page prefix (stream mode)
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.T;
+  int64_t P = 0, G = 1, p0 = 0, p1 = 0;
+  int row0 = 0;
+
+  if (p.stream_mode) {
+    for (int t = tid; t < T; t += blockDim.x) {
+      const int c = max(p.ctx[t], 0);
+      pref[t + 1] = (c + PG - 1) / PG;
+    }
+    if (tid == 0) pref[0] = 0;
+    __syncthreads();
+    if (warp == 0) {
+      int carry = 0;
+      for (int base = 0; base < T; base += 32) {
+        const int idx = base + lane;
+        int v = idx < T ? pref[idx + 1] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += n;
+        }
+        if (idx < T) pref[idx + 1] = v + carry;
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+    }
+    __syncthreads();
+    P = pref[T];
+    G = p.grid < P ? static_cast<int64_t>(p.grid) : P;
+    if (blockIdx.x == 0) {
+      for (int t = tid; t < T; t += blockDim.x) {
+        const int a = pref[t], b = pref[t + 1];
+        int2 m = make_int2(0, 0);
+        if (b > a) {
+          const int lo = static_cast<int>(stream_owner(a, P, G)) + t;
+          const int hi = static_cast<int>(stream_owner(b - 1, P, G)) + t + 1;
+          m = make_int2(lo, hi);
+        }
+        p.meta[t] = m;
+      }
+    }
+    if (static_cast<int64_t>(blockIdx.x) >= G) return;
+    p0 = stream_start(blockIdx.x, P, G);
+    p1 = stream_start(blockIdx.x + 1, P, G);
+    int lo = 0, hi = T;  // largest r with pref[r] <= p0
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pref[mid] <= p0) lo = mid; else hi = mid;
+    }
+    row0 = lo;
+  } else {
+    row0 = blockIdx.x;
+    const int c = max(p.ctx[row0], 0);
+    p0 = 0;
+    p1 = (c + PG - 1) / PG;
+    if (p1 == 0) {  // empty row: its slot says so
+      if (tid < p.H && row0 < p.slots_cap) p.ws_lse[static_cast<int64_t>(row0) * p.H + tid] = -INFINITY;
+      return;
+    }
+  }
+
+  if (tid == 0) {
+    misc[0] = 0;
+    misc[1] = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  __syncthreads();
+
+  // Walk of (row, local page) over the global page range [p0, p1); identical in every role.
+  auto row_pages_base = [&](int r, int& base, int& n) {
+    if (p.stream_mode) {
+      base = pref[r];
+      n = pref[r + 1] - pref[r];
+    } else {
+      base = 0;
+      n = static_cast<int>(p1);
+    }
+  };
+
+  if (warp == NC) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap);
+      int r = row0, base, n;
+      row_pages_base(r, base, n);
+      int it = 0;
+      for (int64_t g = p0; g < p1; ++g, ++it) {
+        while (g >= base + n) {
+          ++r;
+          row_pages_base(r, base, n);
+        }
+        const int lp = static_cast<int>(g - base);
+        const int s = it % STAGES;
+        if (it >= STAGES) {
+          if (!mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) {
+            record_error(p.err, kErrWaitEmpty);
+            atomicExch(&misc[0], 1);
+            break;
+          }
+        }
+        mbar_arrive_expect_tx(&full[s], C::PAGE_BYTES);
+        const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
+        tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g8 = lane >> 2, c4 = lane & 3;
+  const int col0 = warp * 128;  // first latent column owned by this warp
+  uint32_t qa[8][4];
+  float o[16][4];
+  float m_run[2], l_run[2];
+  int buf = 0;
+
+  int r = row0, base, n;
+  row_pages_base(r, base, n);
+  int it = 0;
+  bool seg_open = false;
+  int ctx_r = 0;
+
+  for (int64_t g = p0; g < p1; ++g, ++it) {
+    while (g >= base + n) {
+      ++r;
+      row_pages_base(r, base, n);
+    }
+    const int lp = static_cast<int>(g - base);
+    if (!seg_open) {
+      seg_open = true;
+      ctx_r = max(p.ctx[r], 0);
+      const __nv_bfloat16* qr = p.q + static_cast<int64_t>(r) * p.q_st;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int d = col0 + kk * 16 + 2 * c4;
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(qr + static_cast<int64_t>(g8) * p.q_sh + d);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(qr + static_cast<int64_t>(g8 + 8) * p.q_sh + d);
+        const bool h0 = g8 < p.H, h1 = g8 + 8 < p.H;
+        qa[kk][0] = h0 ? __ldg(q0) : 0u;
+        qa[kk][1] = h1 ? __ldg(q1) : 0u;
+        qa[kk][2] = h0 ? __ldg(q0 + 4) : 0u;
+        qa[kk][3] = h1 ? __ldg(q1 + 4) : 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+      m_run[0] = m_run[1] = -INFINITY;
+      l_run[0] = l_run[1] = 0.f;
+    }
+    const int s = it % STAGES;
+    const bool ok = mbar_wait(&full[s], (it / STAGES) & 1);
+    if (!ok) {
+      record_error(p.err, kErrWaitFull);
+      misc[1] = 1;
+    }
+    const uint32_t sbase = smem_u32(stages + s * C::PAGE_BYTES);
+    const int valid = min(PG, ctx_r - lp * PG);
+
+    // ---- partial scores over this warp's 128 columns
+    float sc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int kp = 0; kp < NT / 2; ++kp) {
+      const int key = kp * 16 + ((lane >> 4) << 3) + (lane & 7);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int slab = (col0 >> 6) + (kk >> 2);
+        const int chunk = ((kk & 3) << 1) + ((lane >> 3) & 1);
+        const uint32_t addr = sbase + slab * C::SLAB_BYTES + key * 128 + ((chunk ^ (key & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma_bf16_16816(sc[2 * kp], qa[kk], b0, b1);
+        mma_bf16_16816(sc[2 * kp + 1], qa[kk], b2, b3);
+      }
+    }
+    if constexpr (NC > 1) {
+      float4* mine = xbuf + (buf * NC + warp) * NT * 32;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mine[j * 32 + lane] = make_float4(sc[j][0], sc[j][1], sc[j][2], sc[j][3]);
+      named_bar_sync(1, NC * 32);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+      for (int w = 0; w < NC; ++w) {
+        const float4* part = xbuf + (buf * NC + w) * NT * 32;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const float4 v = part[j * 32 + lane];
+          sc[j][0] += v.x; sc[j][1] += v.y; sc[j][2] += v.z; sc[j][3] += v.w;
+        }
+      }
+      buf ^= 1;
+      if (misc[1]) break;  // uniform across consumer warps: every setter wrote it before this barrier
+    } else {
+      if (misc[1]) break;
+    }
+
+    // ---- online softmax (log2 domain); keys >= valid are masked
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int k0 = j * 8 + 2 * c4;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool in = (k0 + e) < valid;
+        sc[j][e] = in ? sc[j][e] * p.scale_log2 : -INFINITY;
+        sc[j][2 + e] = in ? sc[j][2 + e] * p.scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, sc[j][e]);
+        mx1 = fmaxf(mx1, sc[j][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+    const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
+    m_run[0] = mn0;
+    m_run[1] = mn1;
+    float rs0 = 0.f, rs1 = 0.f;
+    uint32_t pa[NT / 2][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const float e0 = exp2f(sc[j][0] - mn0), e1 = exp2f(sc[j][1] - mn0);
+      const float e2 = exp2f(sc[j][2] - mn1), e3 = exp2f(sc[j][3] - mn1);
+      rs0 += e0 + e1;
+      rs1 += e2 + e3;
+      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16(e0, e1);
+      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16(e2, e3);
+    }
+    l_run[0] = l_run[0] * al0 + rs0;
+    l_run[1] = l_run[1] * al1 + rs1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= al0; o[j][1] *= al0;
+      o[j][2] *= al1; o[j][3] *= al1;
+    }
+
+    // ---- O += P . V over this warp's columns
+#pragma unroll
+    for (int ks = 0; ks < NT / 2; ++ks) {
+      const int key = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int kb0 = ks * 16 + 2 * c4, kb1 = kb0 + 8;  // keys of (b0|b2) and (b1|b3) pairs
+#pragma unroll
+      for (int jd = 0; jd < 8; ++jd) {
+        const int dcol = col0 + jd * 16;
+        const int slab = (W >> 6) + (dcol >> 6);
+        const int chunk = ((dcol & 63) >> 3) + (lane >> 4);
+        const uint32_t addr = sbase + slab * C::SLAB_BYTES + key * 128 + ((chunk ^ (key & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(addr, b0, b1, b2, b3);
+        if (valid < PG) {
+          b0 = mask_pair(b0, kb0, valid);
+          b1 = mask_pair(b1, kb1, valid);
+          b2 = mask_pair(b2, kb0, valid);
+          b3 = mask_pair(b3, kb1, valid);
+        }
+        mma_bf16_16816(o[2 * jd], pa[ks], b0, b1);
+        mma_bf16_16816(o[2 * jd + 1], pa[ks], b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    // ---- segment end: write the normalised partial and its lse
+    const bool seg_end = (g + 1 == p1) || (lp + 1 == n);
+    if (seg_end) {
+      seg_open = false;
+      float l0 = l_run[0], l1 = l_run[1];
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+      const int slot = p.stream_mode ? static_cast<int>(blockIdx.x) + r : r;
+      if (slot >= p.slots_cap) {
+        record_error(p.err, kErrSlots);
+      } else {
+        const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+        float* base0 = p.ws_o + (static_cast<int64_t>(slot) * p.H + g8) * W;
+        float* base1 = p.ws_o + (static_cast<int64_t>(slot) * p.H + g8 + 8) * W;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int d = col0 + j * 8 + 2 * c4;
+          if (g8 < p.H) *reinterpret_cast<float2*>(base0 + d) = make_float2(o[j][0] * inv0, o[j][1] * inv0);
+          if (g8 + 8 < p.H) *reinterpret_cast<float2*>(base1 + d) = make_float2(o[j][2] * inv1, o[j][3] * inv1);
+        }
+        if (warp == 0 && c4 == 0) {
+          const float ln2 = 0.6931471805599453f;
+          if (g8 < p.H) p.ws_lse[static_cast<int64_t>(slot) * p.H + g8] = (m_run[0] + log2f(l0)) * ln2;
+          if (g8 + 8 < p.H) p.ws_lse[static_cast<int64_t>(slot) * p.H + g8 + 8] = (m_run[1] + log2f(l1)) * ln2;
+        }
+      }
+    }
+  }
+}
+
+// Stage-2 reduce: partials of row t -> o[t, h, :] (bf16 and/or fp32) and lse[h, t].
+template <int W>
+__global__ void __launch_bounds__(W / 4) history_reduce_kernel(const float* __restrict__ ws_o,
+                                                                const float* __restrict__ ws_lse,
+                                                                const int2* __restrict__ meta, int stream_mode,
+                                                                int T, int H, const uint8_t* __restrict__ empty,
+                                                                __nv_bfloat16* __restrict__ out, int64_t o_st,
+                                                                int64_t o_sh, float* __restrict__ out_f32,
+                                                                float* __restrict__ lse_out) {
+  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  int lo, hi;
+  if (stream_mode) {
+    const int2 m = meta[t];
+    lo = m.x;
+    hi = m.y;
+  } else {
+    lo = t;
+    hi = t + 1;
+  }
+  float mx = -INFINITY;
+  for (int s = lo; s < hi; ++s) mx = fmaxf(mx, ws_lse[static_cast<int64_t>(s) * H + h]);
+  const bool is_empty = (empty && empty[t]) || mx == -INFINITY;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
+  if (!is_empty) {
+    for (int s = lo; s < hi; ++s) {
+      const float w = expf(ws_lse[static_cast<int64_t>(s) * H + h] - mx);
+      const float4 v = reinterpret_cast<const float4*>(ws_o + (static_cast<int64_t>(s) * H + h) * W)[tid];
+      wsum += w;
+      acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+    }
+    const float inv = 1.f / wsum;
+    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+  }
+  if (out) {
+    __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + tid * 4;
+    reinterpret_cast<__nv_bfloat162*>(dst)[0] = __floats2bfloat162_rn(acc.x, acc.y);
+    reinterpret_cast<__nv_bfloat162*>(dst)[1] = __floats2bfloat162_rn(acc.z, acc.w);
+  }
+  if (out_f32) reinterpret_cast<float4*>(out_f32 + (static_cast<int64_t>(t) * H + h) * W)[tid] = acc;
+  if (tid == 0 && lse_out) lse_out[static_cast<int64_t>(h) * T + t] = is_empty ? -INFINITY : mx + logf(wsum);
+}
+
+// ------------------------------------------------------------------ host side
+template <int W, int PG>
+size_t history_smem_bytes(int T) {
+  using C = HistoryCfg<W, PG>;
+  return 1024 + static_cast<size_t>(C::STAGES) * C::PAGE_BYTES + C::XBUF_BYTES + 2 * C::STAGES * 8 + 16 +
+         4 * (static_cast<size_t>(T) + 1);
+}
+
+template <int W, int PG>
+static int occupancy_for() {
+  using C = HistoryCfg<W, PG>;
+  static int cached = -1;
+  if (cached < 0) {
+    const size_t smem = history_smem_bytes<W, PG>(kHistoryMaxStreamRows);
+    cudaFuncSetAttribute(history_split_kernel<W, PG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, history_split_kernel<W, PG>, C::THREADS, smem) !=
+            cudaSuccess ||
+        n < 1)
+      n = 1;
+    cached = n;
+  }
+  return cached;
+}
+
+
+template <int W, int PG>
+static int launch_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t stream) {
+  using C = HistoryCfg<W, PG>;
+  CUtensorMap tmap;
+  int rc = latent_cache_tmap(&tmap, a.cache, a.num_blocks, a.cache_st_block, a.cache_st_row, W, PG);
+  if (rc) return rc;
+  HistoryParams p;
+  p.q = static_cast<const __nv_bfloat16*>(a.q);
+  p.q_st = a.q_st;
+  p.q_sh = a.q_sh;
+  p.block_table = a.block_table;
+  p.bt_st = a.bt_st;
+  p.max_blocks = a.max_blocks;
+  p.ctx = a.ctx;
+  p.T = a.T;
+  p.H = a.H;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.ws_o = plan.ws_o;
+  p.ws_lse = plan.ws_lse;
+  p.meta = plan.meta;
+  p.slots_cap = plan.slots_cap;
+  p.grid = plan.grid;
+  p.stream_mode = plan.stream_mode;
+  p.err = a.err;
+  const size_t smem = history_smem_bytes<W, PG>(plan.stream_mode ? a.T : 0);
+  occupancy_for<W, PG>();
+  history_split_kernel<W, PG><<<plan.grid, C::THREADS, smem, stream>>>(tmap, p);
+  return cuda_status(cudaGetLastError(), "history_split_kernel launch");
+}
+
+int history_plan(const HistoryArgs& a, HistoryPlan* plan) {
+  // Workspace accounting mirrors s6_ops.S6Workspace.attn_logits (s6_ops.py:109-114): the op may use
+  // T * splits * H * (W + 1) floats and raises when the buffer is smaller.
+  const int64_t need = static_cast<int64_t>(a.T) * a.num_kv_splits * a.H * (a.W + 1);
+  if (need > a.ws_floats) {
+    set_error("S6 workspace overflow: need %lld floats, have %lld", static_cast<long long>(need),
+              static_cast<long long>(a.ws_floats));
+    return kStatusOverflow;
+  }
+  const int64_t per_slot = static_cast<int64_t>(a.H) * (a.W + 1);
+  const int64_t meta_floats = 2 * static_cast<int64_t>(a.T);
+  int sms = 148, occ = 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  switch (a.W * 100 + a.page) {
+    case 25616: occ = occupancy_for<256, 16>(); break;
+    case 25632: occ = occupancy_for<256, 32>(); break;
+    case 51216: occ = occupancy_for<512, 16>(); break;
+    case 51232: occ = occupancy_for<512, 32>(); break;
+    case 102416: occ = occupancy_for<1024, 16>(); break;
+    default: break;
+  }
+  const int64_t stream_slots = (need - meta_floats) / per_slot;
+  const int64_t g_stream = std::min<int64_t>(static_cast<int64_t>(sms) * occ * a.waves, stream_slots - a.T + 1);
+  if (a.num_kv_splits >= 2 && a.T <= kHistoryMaxStreamRows && g_stream >= 1 && a.T >= 1) {
+    plan->stream_mode = 1;
+    plan->grid = static_cast<int>(g_stream);
+    plan->slots_cap = static_cast<int>(stream_slots);
+  } else {
+    plan->stream_mode = 0;
+    plan->grid = a.T;
+    plan->slots_cap = static_cast<int>(need / per_slot);
+  }
+  plan->ws_o = a.ws;
+  plan->ws_lse = a.ws + static_cast<int64_t>(plan->slots_cap) * a.H * a.W;
+  plan->meta = reinterpret_cast<int2*>(plan->ws_lse + static_cast<int64_t>(plan->slots_cap) * a.H);
+  if (plan->stream_mode && (reinterpret_cast<uintptr_t>(plan->meta) & 7)) {
+    // keep int2 alignment: shift the metadata one float up (still inside `need`)
+    plan->meta = reinterpret_cast<int2*>(plan->ws_lse + static_cast<int64_t>(plan->slots_cap) * a.H + 1);
+    if (static_cast<int64_t>(plan->slots_cap) * per_slot + meta_floats + 1 > need) {
+      plan->slots_cap -= 1;
+      plan->grid = std::min(plan->grid, plan->slots_cap - a.T + 1);
+      plan->ws_lse = a.ws + static_cast<int64_t>(plan->slots_cap) * a.H * a.W;
+      float* m = plan->ws_lse + static_cast<int64_t>(plan->slots_cap) * a.H;
+      if (reinterpret_cast<uintptr_t>(m) & 7) ++m;
+      plan->meta = reinterpret_cast<int2*>(m);
+    }
+  }
+  return kStatusOk;
+}
+
+int history_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t stream) {
+  if (a.T == 0) return kStatusOk;
+  switch (a.W * 100 + a.page) {
+    case 25616: return launch_split<256, 16>(a, plan, stream);
+    case 25632: return launch_split<256, 32>(a, plan, stream);
+    case 51216: return launch_split<512, 16>(a, plan, stream);
+    case 51232: return launch_split<512, 32>(a, plan, stream);
+    case 102416: return launch_split<1024, 16>(a, plan, stream);
+    default:
+      set_error("unsupported latent width %d / page %d (widths 256, 512 with pages 16, 32; width 1024 with page 16)",
+                a.W, a.page);
+      return kStatusInvalid;
+  }
+}
+
+int history_reduce(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out, int64_t o_st,
+                   int64_t o_sh, float* out_f32, float* lse, cudaStream_t stream) {
+  if (a.T == 0) return kStatusOk;
+  dim3 grid(a.T, a.H);
+#define HLA_REDUCE(WW)                                                                                   \
+  history_reduce_kernel<WW><<<grid, WW / 4, 0, stream>>>(plan.ws_o, plan.ws_lse, plan.meta, plan.stream_mode, \
+                                                         a.T, a.H, empty, static_cast<__nv_bfloat16*>(out), o_st, \
+                                                         o_sh, out_f32, lse)
+  switch (a.W) {
+    case 256: HLA_REDUCE(256); break;
+    case 512: HLA_REDUCE(512); break;
+    case 1024: HLA_REDUCE(1024); break;
+    default: set_error("unsupported latent width %d", a.W); return kStatusInvalid;
+  }
+#undef HLA_REDUCE
+  return cuda_status(cudaGetLastError(), "history_reduce_kernel launch");
+}
+
+}  // namespace hla

@@ -1,0 +1,62 @@
+// Internal host-side interfaces shared by the S6 kernel translation units.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace hla {
+
+enum Status : int {
+  kStatusOk = 0,
+  kStatusInvalid = 1,   // bad shape / stride / dtype: ValueError on the Python side
+  kStatusOverflow = 2,  // workspace too small: RuntimeError
+  kStatusCuda = 3,      // CUDA runtime / driver failure: RuntimeError
+};
+
+// Rows above this count use one CTA per row instead of the stream-K page split.
+constexpr int kHistoryMaxStreamRows = 1024;
+
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+
+// 4-D TMA descriptor over a paged latent cache [num_blocks, 1, page, 2W] (unit last stride):
+// dims (64 columns, page rows, 2W/64 slabs, blocks) with SWIZZLE_128B, so a box of
+// (64, page, 2W/64, 1) is one whole page laid out [slab][row][64] in shared memory.
+int latent_cache_tmap(CUtensorMap* map, const void* cache, int64_t num_blocks, int64_t st_block, int64_t st_row,
+                      int W, int page);
+
+struct HistoryArgs {
+  const void* q;            // bf16 [T, H, W], unit last stride
+  int64_t q_st, q_sh;
+  const void* cache;        // bf16 [num_blocks, 1, page, 2W]
+  int64_t num_blocks, cache_st_block, cache_st_row;
+  const int32_t* block_table;
+  int64_t bt_st;
+  int32_t max_blocks;
+  const int32_t* ctx;
+  int32_t T, H, W, page;
+  float scale;
+  int32_t num_kv_splits;
+  float* ws;
+  int64_t ws_floats;
+  int32_t waves;            // CTAs per SM slot multiplier for the stream-K grid (>= 1)
+  int* err;
+};
+
+struct HistoryPlan {
+  int stream_mode;
+  int grid;
+  int slots_cap;
+  float* ws_o;
+  float* ws_lse;
+  int2* meta;
+};
+
+int history_plan(const HistoryArgs& a, HistoryPlan* plan);
+int history_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t stream);
+int history_reduce(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out, int64_t o_st,
+                   int64_t o_sh, float* out_f32, float* lse, cudaStream_t stream);
+
+}  // namespace hla

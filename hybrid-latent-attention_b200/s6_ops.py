@@ -1,0 +1,162 @@
+"""S6 serving ops on B200: the ``hla/vllm_latent/s6_ops.py`` API, backed by libhla_s6 (sm_100a).
+
+Same function names, argument order and meaning, output layouts and error behaviour as the
+reference module, so ``s6_layer.attend`` and the vLLM adapter call them unchanged; the
+backend string of every op is ``'b200'`` (``select_backends()`` returns it).  There is no
+torch or CPU backend here: any other backend string raises ``ValueError`` exactly as an
+unknown backend does in the reference, and a missing ``libhla_s6.so`` raises on first use.
+
+Contracts shared by all ops (reference s6_ops.py:1-10): outputs are normalised attention
+outputs; ``lse`` is a contiguous fp32 ``[H, T]`` natural-log LSE over already-scaled scores;
+empty rows give ``lse = -inf`` and ``o = 0``; no NaN leaves a merge.  No op synchronises with
+the host, loops over requests, or allocates beyond its outputs, so every op can be captured
+in a CUDA graph and replayed with new contents of q, ctx, block tables and caches.
+"""
+from __future__ import annotations
+
+from collections import namedtuple
+
+import torch
+
+from . import _lib
+
+INF = float('inf')
+BACKEND = 'b200'
+Backends = namedtuple('Backends', 'history chunk merge rope')
+B200_BACKENDS = Backends(BACKEND, BACKEND, BACKEND, BACKEND)
+
+
+def _require(backend, kind):
+    if backend != BACKEND:
+        raise ValueError(f'Unknown {kind} backend {backend!r}')
+
+
+def _check_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError('S6 b200 ops take CUDA tensors (no CPU path exists)')
+
+
+# ----------------------------------------------------------------------------- step metadata
+def token_requests(query_start_loc, num_tokens):
+    """Request index per token (long, clamped into range) and ``valid = arange(T) < query_start_loc[-1]``.
+
+    Same contract as reference s6_ops.py:61-68; sync-free.  Padding tokens are ``~valid``.
+    """
+    idx = torch.arange(num_tokens, dtype=query_start_loc.dtype, device=query_start_loc.device)
+    req = torch.searchsorted(query_start_loc[1:], idx, right=True).clamp_(max=query_start_loc.shape[0] - 2)
+    return req.long(), idx < query_start_loc[-1]
+
+
+def history_lengths(seq_lens, query_start_loc):
+    """Per-request history length ``seq_len - query_len``, clamped at 0 (reference s6_ops.py:71-73)."""
+    return (seq_lens - (query_start_loc[1:] - query_start_loc[:-1])).clamp_(min=0)
+
+
+def num_kv_splits(max_seq_len, num_tokens, split_max_tokens, sm_count, head_blocks=1):
+    """Split budget of the paged-history kernel for a step of ``num_tokens`` rows (reference
+    s6_ops.py:76-89, same formula).  On B200 it bounds the partial slots the stream-K history
+    kernel may use (``T * splits`` per call); the kernel balances pages across SMs itself."""
+    if num_tokens > split_max_tokens:
+        return 1
+    ideal = 1 << (max(1, max_seq_len // 512) - 1).bit_length()
+    fill = -(-2 * sm_count // (num_tokens * head_blocks))
+    return max(1, min(max(ideal, fill), 2 * sm_count, -(-max_seq_len // 32)))
+
+
+class S6Workspace:
+    """Persistent fp32 workspace of the history kernel (reference s6_ops.py:92-114).
+
+    Sized for ``rows_x_splits`` (the largest ``num_tokens * num_kv_splits`` a step can request),
+    allocated once on first use and never grown: an oversized request raises.
+    """
+
+    def __init__(self, heads, width_max, rows_x_splits):
+        self.floats = rows_x_splits * heads * (width_max + 1)
+        self.buffer = None
+
+    def ensure(self, device):
+        if self.buffer is None:
+            self.buffer = torch.empty(self.floats, dtype=torch.float32, device=device)
+        return self.buffer
+
+    def attn_logits(self, tokens, heads, splits, width, device=None):
+        need = tokens * heads * splits * (width + 1)
+        buffer = self.ensure(device)
+        if need > buffer.numel():
+            raise RuntimeError(f'S6 workspace overflow: need {need} floats, have {buffer.numel()}')
+        return buffer[:need].view(tokens, heads, splits, width + 1)
+
+
+# ----------------------------------------------------------------------------- A1 history reader
+def _latent_cache_geometry(cache, W):
+    if cache.dim() != 4 or cache.shape[1] != 1 or cache.shape[-1] != 2 * W:
+        raise ValueError(f'latent cache must be [num_blocks, 1, block, {2 * W}], got {tuple(cache.shape)}')
+    if cache.dtype != torch.bfloat16 or cache.stride(-1) != 1:
+        raise ValueError('latent cache must be bf16 with a unit last-dim stride')
+    return cache.shape[0], cache.shape[2], cache.stride(0), cache.stride(2)
+
+
+def history_attention(q_lat, cache, block_table, ctx, scale, num_kv_splits, workspace, k_scale, v_scale, backend,
+                      empty=None):
+    """Fully visible attention of ``q_lat[T,H,W]`` over the first ``ctx[t]`` paged latent rows of an MQA S6 cache.
+
+    ``cache`` is the logical vLLM layout ``[num_blocks, 1, block, 2W]`` (K then V on the last dim);
+    ``block_table[T, max_blocks]`` int32 per token (only columns ``< ceil(ctx[t]/block)`` are read);
+    ``ctx[T]`` int32.  Returns ``(o[T,H,W] bf16, lse[H,T] fp32)``; empty rows give ``o = 0``,
+    ``lse = -inf`` (reference s6_ops.py:117-161).  ``k_scale``/``v_scale`` are accepted for
+    signature compatibility; like the reference adapter, quantized caches are not supported.
+    """
+    _require(backend, 'history')
+    _check_cuda(q_lat, cache, block_table, ctx)
+    if q_lat.dim() != 3 or q_lat.stride(-1) != 1:
+        raise ValueError('q_lat must be [T, H, W] with a unit last-dim stride')
+    if q_lat.dtype != torch.bfloat16:
+        raise ValueError('q_lat must be bf16')
+    T, H, W = q_lat.shape
+    nb, page, sb, sr = _latent_cache_geometry(cache, W)
+    if block_table.dtype != torch.int32 or ctx.dtype != torch.int32:
+        raise ValueError('block_table and ctx must be int32')
+    if block_table.stride(-1) != 1:
+        raise ValueError('block_table needs a unit last-dim stride')
+    o = torch.empty(T, H, W, dtype=q_lat.dtype, device=q_lat.device)
+    lse = torch.empty(H, T, dtype=torch.float32, device=q_lat.device)
+    ws = workspace.attn_logits(T, H, num_kv_splits, W, q_lat.device)
+    buffer = workspace.buffer
+    emp = None
+    if empty is not None:
+        emp = empty.to(torch.uint8) if empty.dtype != torch.bool else empty
+    ctx_c = ctx.contiguous()
+    _lib.call('hla_s6_history_attention', _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), _lib.ptr(cache), nb, sb,
+              sr, _lib.ptr(block_table), block_table.stride(0), block_table.shape[1], _lib.ptr(ctx_c), _lib.ptr(emp), T, H, W, page,
+              float(scale), int(num_kv_splits), _lib.ptr(buffer), ws.numel(), _lib.ptr(o), o.stride(0), o.stride(1),
+              _lib.ptr(lse), None, _lib.stream_of(q_lat))
+    return o, lse
+
+
+def history_attention_kv(q, k, v, block_table, ctx, scale, num_kv_splits, workspace, k_scale, v_scale, backend,
+                         empty=None, mla=False):
+    """Paged attention of ``q[T,H,Lk]`` over ``k[num_blocks,kvH,block,Lk]`` / ``v[...,Lv]`` (reference
+    s6_ops.py:128-161).  The B200 kernel serves the S6 MQA layout: ``kvH == 1`` with ``k`` and
+    ``v`` the two halves of one ``[num_blocks, 1, block, 2W]`` cache (``Lk == Lv``).  Other
+    layouts (per-head caches, the LLA ``mla`` row) raise ``ValueError``."""
+    _require(backend, 'history')
+    W = q.shape[-1]
+    if mla or k.shape[1] != 1 or v.shape[-1] != W or k.shape[-1] != W:
+        raise ValueError('b200 history kernel supports the MQA S6 cache (kvH = 1, Lk = Lv) only')
+    if k.stride() != v.stride() or v.data_ptr() != k.data_ptr() + W * k.element_size():
+        raise ValueError('b200 history kernel needs k and v to be the K/V halves of one latent cache')
+    cache = torch.as_strided(k, (k.shape[0], 1, k.shape[2], 2 * W), k.stride())
+    return history_attention(q, cache, block_table, ctx, scale, num_kv_splits, workspace, k_scale, v_scale,
+                             backend, empty)
+
+
+def select_backends(head_size=128):
+    """The B200 kernel backends for every op; raises when CUDA or libhla_s6 is unavailable
+    (reference s6_ops.py:364-372)."""
+    if not torch.cuda.is_available():
+        raise RuntimeError('S6 b200 ops require CUDA')
+    _lib.load()
+    if head_size != 128:
+        raise RuntimeError(f'b200 window kernel is built for head size 128, got {head_size}')
+    return B200_BACKENDS

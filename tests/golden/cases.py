@@ -1,0 +1,139 @@
+"""Deterministic inputs of the golden cases (numpy PCG64, fixed seeds).
+
+The fixtures under tests/golden/*.npz hold the reference's OUTPUTS for these inputs plus a
+sha256 of the inputs, so the tests rebuild the inputs here and check the hash before using
+the stored outputs.  Values that feed bf16 kernels are bf16-representable float32.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+INF = float('inf')
+
+
+def _bf16(x):
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return (r & 0xFFFFFFFF).astype(np.uint32).view(np.float32).copy()
+
+
+def digest(arrays: dict) -> str:
+    h = hashlib.sha256()
+    for k in sorted(arrays):
+        a = np.ascontiguousarray(arrays[k])
+        h.update(k.encode())
+        h.update(str(a.dtype).encode())
+        h.update(str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def paged_case(seed, heads, width, page, num_blocks, ctx, max_blocks=None, bf16=True, poison=True):
+    """q [T,H,W], cache [nb,1,page,2W] (block 0 = +inf null block), per-token shuffled block
+    tables whose stale columns point at the null block (the reference fixture of
+    test_s6_ops.py:73-90)."""
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(ctx, dtype=np.int32)
+    T = ctx.shape[0]
+    need = -(-ctx // page)
+    mb = max_blocks or max(int(need.max()), 1) + 2
+    cache = rng.standard_normal((num_blocks, 1, page, 2 * width), dtype=np.float32)
+    q = rng.standard_normal((T, heads, width), dtype=np.float32)
+    if bf16:
+        cache, q = _bf16(cache), _bf16(q)
+    if poison:
+        cache[0] = INF
+    table = np.zeros((T, mb), dtype=np.int32)
+    for t in range(T):
+        ids = rng.permutation(np.arange(1, num_blocks))[:mb].astype(np.int32)
+        table[t] = ids
+        table[t, need[t]:] = 0
+    return dict(q=q, cache=cache, block_table=table, ctx=ctx)
+
+
+def history_cases():
+    return {
+        'hist_h2_w8_p4': (paged_case(11, 2, 8, 4, 64, [0, 1, 17, 40, 5, 0], max_blocks=12, bf16=False), 1 / np.sqrt(8)),
+        'hist_h2_w8_p8': (paged_case(12, 2, 8, 8, 64, [0, 1, 17, 40, 5, 0], max_blocks=12, bf16=False), 1 / np.sqrt(8)),
+        'hist_h16_w512_p16': (paged_case(13, 16, 512, 16, 24, [0, 1, 17, 100, 255, 33, 16, 300]), 1 / np.sqrt(128)),
+        'hist_h16_w256_p16': (paged_case(14, 16, 256, 16, 24, [0, 1, 17, 100, 255, 33, 16, 300]), 1 / np.sqrt(128)),
+        'hist_h16_w512_p32': (paged_case(15, 16, 512, 32, 14, [0, 1, 17, 100, 255, 33, 32, 300]), 1 / np.sqrt(128)),
+    }
+
+
+def window_case(seed=21, heads=16, d=128, page=16, window=32, seq_lens=(1, 2, 33, 34, 70, 5), padding=2):
+    """Decode step over per-request exact caches: logical [nb, H, page, 2d] (physical
+    (nb, page, H, 2d)), per-request block tables, the current token already written."""
+    rng = np.random.default_rng(seed)
+    seq_lens = np.asarray(seq_lens, dtype=np.int32)
+    R = seq_lens.shape[0]
+    T = R + padding
+    qsl = np.concatenate(([0], np.arange(1, R + 1))).astype(np.int32)
+    need = -(-seq_lens // page)
+    mb = int(need.max()) + 1
+    nb = int(need.sum()) + 4
+    phys = _bf16(rng.standard_normal((nb, page, heads, 2 * d), dtype=np.float32))
+    phys[0] = INF
+    free = rng.permutation(np.arange(1, nb)).astype(np.int32)
+    table = np.zeros((R, mb), dtype=np.int32)
+    k = 0
+    for r in range(R):
+        table[r, :need[r]] = free[k:k + need[r]]
+        k += need[r]
+    q = _bf16(rng.standard_normal((T, heads, d), dtype=np.float32))
+    return dict(q=q, cache_phys=phys, block_table=table, query_start_loc=qsl, seq_lens=seq_lens,
+                window=np.int32(window))
+
+
+def merge_case(seed=31, tokens=8, heads=16, dim=128):
+    rng = np.random.default_rng(seed)
+    o_h = _bf16(rng.standard_normal((tokens, heads, dim), dtype=np.float32))
+    o_c = _bf16(rng.standard_normal((tokens, heads, dim), dtype=np.float32))
+    l_h = (rng.standard_normal((heads, tokens)) * 3).astype(np.float32)
+    l_c = (rng.standard_normal((heads, tokens)) * 3).astype(np.float32)
+    l_h[:, 0] = -INF
+    l_c[:, 1] = INF
+    l_h[:, 2] = -INF
+    l_c[:, 2] = -INF
+    l_c[:, 3] = -INF
+    invalid = np.zeros(tokens, dtype=bool)
+    invalid[2] = True
+    invalid[7] = True
+    return dict(o_hist=o_h, lse_hist=l_h, o_chunk=o_c, lse_chunk=l_c, invalid=invalid)
+
+
+def rope_case(seed=41, tokens=9, heads=3, widths=(512, 256), max_pos=4096, head_dim=128, theta=1e6):
+    rng = np.random.default_rng(seed)
+    pos = rng.integers(0, max_pos, tokens).astype(np.int64)
+    out = dict(positions=pos, max_pos=np.int64(max_pos), head_dim=np.int64(head_dim), theta=np.float64(theta))
+    for w in widths:
+        out[f'x{w}'] = _bf16(rng.standard_normal((heads, tokens, w), dtype=np.float32)).transpose(1, 0, 2).copy()
+        out[f'row{w}'] = _bf16(rng.standard_normal((tokens, 2 * w), dtype=np.float32))
+    return out
+
+
+def writer_case(seed=51, tokens=7, hidden=256, rank=512, rank1=256, loops=4, max_pos=4096, theta=1e6):
+    """Writer inputs: per-loop attention inputs h, bf16 writer weights (LatentLayer.cand_s /
+    cand1 shapes), positions, and a paged cache placement (page 16, shuffled blocks)."""
+    rng = np.random.default_rng(seed)
+    h = _bf16(rng.standard_normal((loops, tokens, hidden), dtype=np.float32))
+    E = _bf16(rng.standard_normal((loops - 1, 2 * rank, hidden), dtype=np.float32) / np.sqrt(hidden))
+    E1 = _bf16(rng.standard_normal((2 * rank1, hidden), dtype=np.float32) / np.sqrt(hidden))
+    pos = rng.integers(0, max_pos, tokens).astype(np.int64)
+    return dict(h=h, E=E, E1=E1, positions=pos, max_pos=np.int64(max_pos), theta=np.float64(theta),
+                head_dim=np.int64(128), rank=np.int64(rank), rank1=np.int64(rank1))
+
+
+def meta_cases():
+    """Integer metadata cases (test_s6_ops.py:16-27, 51-70)."""
+    return dict(
+        token_requests=[((0, 1, 2, 3), 3), ((0, 5), 5), ((0, 3, 4, 6), 6), ((0, 2, 3, 3, 3), 3),
+                        ((0, 2, 3, 3, 3), 5), ((0, 2, 3), 5)],
+        history_lengths=[((4, 7, 0, 0), (0, 2, 3, 3, 3)), ((1, 1), (0, 2, 4))],
+        num_kv_splits=[(8448, 1, 512, 108), (8448, 32, 512, 108), (8448, 512, 512, 108), (384, 1, 512, 108),
+                       (100, 8, 512, 108), (8448, 513, 512, 108), (1 << 20, 1, 512, 4), (8192, 64, 512, 148),
+                       (8192, 1, 512, 148), (32768, 256, 512, 148), (131072, 4, 512, 148)],
+    )

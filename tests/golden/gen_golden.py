@@ -1,0 +1,147 @@
+"""Generate the golden fixtures by running the REFERENCE's own torch code on the inputs of cases.py.
+
+Usage (needs the reference checkout, read-only):
+    python tests/golden/gen_golden.py --reference /path/to/hybrid-latent-attention
+
+Writes tests/golden/<name>.npz with the reference outputs and a sha256 of the inputs.
+The reference functions called (file:line in the reference project):
+  hla/vllm_latent/s6_ops.py:117 history_attention (torch backend -> _history_reference :204)
+  hla/vllm_latent/s6_ops.py:290 window_attention, :234 chunk_attention('torch'), :353 merge_lse
+  hla/vllm_latent/s6_ops.py:262 merge_states('torch'), :23 latent_rope('torch'), :61 token_requests,
+  :71 history_lengths, :76 num_kv_splits
+  hla/vllm_latent/s6_layer.py:16 latent_inv_freq, :21 latent_rope_table, :32 latent_query,
+  :124 write_rows, :135 committed_row
+  hla/latent/register.py:28 LatentLayer (write_step / write1 / pack / fields)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import cases  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--reference', default='/root/reference')
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    import torch
+    from hla.latent.register import LatentLayer
+    from hla.vllm_latent import s6_layer, s6_ops
+    torch.set_num_threads(4)
+    T_ = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+
+    def save(name, inputs, **outputs):
+        np.savez_compressed(HERE / f'{name}.npz', input_sha256=np.array(cases.digest(inputs)), **outputs)
+        print('wrote', name, {k: getattr(v, 'shape', v) for k, v in outputs.items()})
+
+    # ---- A1 history reader
+    for name, (inp, scale) in cases.history_cases().items():
+        o, lse = s6_ops.history_attention(T_(inp['q']), T_(inp['cache']), T_(inp['block_table']), T_(inp['ctx']),
+                                          float(scale), 1, None, None, None, 'torch')
+        save(name, inp, o=o.numpy(), lse=lse.numpy(), scale=np.float64(scale))
+
+    # ---- A5 decode window (the reference's own non-fused composition of the same keys as
+    #      window_attention_fa: chunk over the current token + window history + merge_lse)
+    w = cases.window_case()
+    q, phys, table = T_(w['q']), T_(w['cache_phys']), T_(w['block_table'])
+    qsl, seq_lens, window = T_(w['query_start_loc']), T_(w['seq_lens']), int(w['window'])
+    Tn, H, d = q.shape
+    page = phys.shape[1]
+    logical = phys.transpose(1, 2)                       # [nb, H, page, 2d]
+    req, valid = s6_ops.token_requests(qsl, Tn)
+    invalid = ~valid
+    last = (seq_lens[req] - 1).clamp(min=0)
+    blk = table[req, last // page].long()
+    cur = phys[blk, last % page]                          # [T, H, 2d] current token rows
+    k_cur, v_cur = cur[..., :d].contiguous(), cur[..., d:].contiguous()
+    scale = 1 / math.sqrt(d)
+    o_c, lse_c = s6_ops.chunk_attention(q, k_cur, v_cur, torch.arange(Tn + 1, dtype=torch.int32).clamp(max=int(qsl[-1])),
+                                        1, invalid, scale, 'torch')
+    ctx = torch.where(valid, last, 0).int()
+    o_w, lse_w = s6_ops.window_attention(q, logical, table[req], ctx, window, scale)
+    o, lse = s6_ops.merge_lse(o_w, lse_w, o_c, lse_c)
+    o = o.masked_fill(invalid[:, None, None], 0)
+    lse = lse.masked_fill(invalid[None, :], -float('inf'))
+    save('window_decode', w, o=o.numpy(), lse=lse.numpy(), scale=np.float64(scale))
+
+    # ---- A7 merges
+    m = cases.merge_case()
+    out = s6_ops.merge_states(T_(m['o_hist']), T_(m['lse_hist']), T_(m['o_chunk']), T_(m['lse_chunk']),
+                              T_(m['invalid']), 'torch')
+    l_c_noinf = np.where(m['lse_chunk'] == np.inf, -np.inf, m['lse_chunk']).astype(np.float32)
+    o2, l2 = s6_ops.merge_lse(T_(m['o_hist']), T_(m['lse_hist']), T_(m['o_chunk']), T_(l_c_noinf))
+    save('merge', m, merge_states=out.numpy(), merge_lse_o=o2.numpy(), merge_lse_lse=l2.numpy())
+
+    # ---- A4 latent RoPE / tables / query
+    r = cases.rope_case()
+    inv = s6_layer.latent_inv_freq(int(r['head_dim']), float(r['theta']))
+    outs = dict(inv_freq=inv.numpy())
+    pos = T_(r['positions'])
+    for wd in (512, 256):
+        table32 = s6_layer.latent_rope_table(int(r['max_pos']), inv, wd, torch.float32)
+        table16 = s6_layer.latent_rope_table(int(r['max_pos']), inv, wd, torch.bfloat16)
+        outs[f'table{wd}_rows'] = table32[pos].numpy()
+        outs[f'table{wd}_bf16_rows'] = table16[pos].float().numpy()
+        x = T_(r[f'x{wd}']).bfloat16()
+        outs[f'rope{wd}_bf16'] = s6_ops.latent_rope(x, pos, table16, 'torch').float().numpy()
+        outs[f'rope{wd}_f32'] = s6_ops.latent_rope(x.float(), pos, table32, 'torch').numpy()
+        row = T_(r[f'row{wd}']).bfloat16()
+        outs[f'rowrope{wd}_bf16'] = s6_ops.latent_rope(row[:, :wd], pos, table16, 'torch').float().numpy()
+    save('rope', r, **outs)
+
+    # ---- A9 writer: write_rows / committed_row in bf16 against LatentLayer.pack
+    wc = cases.writer_case()
+    hidden, rank, rank1 = wc['h'].shape[-1], int(wc['rank']), int(wc['rank1'])
+    sl = LatentLayer(hidden, 16, 128, 4, rank, rank, rank1).to(torch.bfloat16)
+    with torch.no_grad():
+        for i in range(3):
+            sl.cand_s[i].weight.copy_(T_(wc['E'][i]).bfloat16())
+        sl.cand1.weight.copy_(T_(wc['E1']).bfloat16())
+    pos = T_(wc['positions'])
+    inv = s6_layer.latent_inv_freq(128, float(wc['theta']))
+    tables = {wd: s6_layer.latent_rope_table(int(wc['max_pos']), inv, wd, torch.bfloat16) for wd in (rank, rank1)}
+
+    class Ctx:
+        positions = pos
+        backends = s6_ops.TORCH_BACKENDS
+    Ctx.tables = tables
+    state, rows, regs = None, {}, []
+    with torch.no_grad():
+        hs = [T_(wc['h'][i]).bfloat16() for i in range(4)]
+        for loop in range(4):
+            state = s6_layer.write_rows(sl, loop, hs[loop], state)
+            regs.append((state.reg if loop else state.first).float().numpy())
+            row = s6_layer.committed_row(sl, loop, state, Ctx)
+            if row is not None:
+                rows[loop] = torch.cat(row, -1).float().numpy()
+        emb = (pos[:, None].float() * inv[None]).repeat(1, 2)
+        cos, sin = emb.cos().bfloat16(), emb.sin().bfloat16()
+        packed = sl.pack(sl.write(hs)[-1], sl.write1(hs[0]), cos, sin).float().numpy()
+    save('writer', wc, first=regs[0], reg1=regs[1], reg2=regs[2], reg3=regs[3], row_l1=rows[0], row_main=rows[3],
+         packed=packed)
+
+    # ---- integer metadata
+    mc = cases.meta_cases()
+    meta = dict(
+        token_requests=[[x.tolist() for x in s6_ops.token_requests(torch.tensor(qsl_, dtype=torch.int32), n)]
+                        for qsl_, n in mc['token_requests']],
+        history_lengths=[s6_ops.history_lengths(torch.tensor(a, dtype=torch.int32), torch.tensor(b, dtype=torch.int32)).tolist()
+                         for a, b in mc['history_lengths']],
+        num_kv_splits=[s6_ops.num_kv_splits(*c) for c in mc['num_kv_splits']],
+    )
+    (HERE / 'meta.json').write_text(json.dumps({'cases': {k: [list(map(lambda v: list(v) if isinstance(v, tuple) else v, c)) for c in mc[k]] for k in mc},
+                                                'reference': meta}, indent=1))
+    print('wrote meta.json')
+
+
+if __name__ == '__main__':
+    main()
