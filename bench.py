@@ -1,0 +1,394 @@
+"""Benchmark of the B200 S6 hybrid decode path (BASELINE config 2 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|4]
+
+One step = one decode step of an Ouro-1.4B-shaped S6 model's attention path: 24 layers x 4 loops
+of (writer projection, latent query, exact RoPE + window append, paged latent-history read,
+fused window/B/merge combine, row commits), B = 64 sequences at context 8192 per GPU, paged
+caches with a shuffled page table, random-init bf16 weights and synthetic activations.  The
+dense Ouro body (QKV/O/MLP GEMMs) is not part of the step.
+
+value: decode tokens/s over all ranks, device-timed (CUDA events around K graph replays,
+barrier + synchronize on both sides, max over ranks); inputs resident in HBM and larger than
+L2 (the latent caches are ~40 GB per GPU).  e2e: the same step with its per-step activations
+copied host->device from pinned memory and its outputs read back, inside the timed region.
+roofline: the dominant kernel (history split) timed alone in a graph of its 96 launches.
+cpu_baseline / --impl reference: the CPU oracle (numpy fp32 restatement of the reference's
+torch path) on a bounded sample of the same workload, extrapolated to a step.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PKG = 'hybrid-latent-attention_b200'
+FALLBACK_HBM_GBS = 6650.0
+METRIC = 'S6 decode tokens/s and latent-history HBM GB/s (% roofline), B=64 ctx 8K, 1/2/4/8 GPU'
+
+
+def dist_env():
+    return int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1)), int(os.environ.get('LOCAL_RANK', 0))
+
+
+def config_batch(config, rank, world, seed):
+    """Per-rank request contexts.  Config 2: 64 sequences at 8192 per GPU (weak scaling).  Config 4:
+    256 log-uniform contexts in [64, 32768] split across ranks by greedy sum-of-context balance."""
+    import numpy as np
+    if config == 2:
+        return [8192] * 64, 'weak'
+    rng = np.random.default_rng(seed)
+    ctx = np.exp(rng.uniform(math.log(64), math.log(32768), 256)).astype(np.int64)
+    ctx[:8] = rng.integers(1, 32, 8)           # some sequences shorter than the window
+    loads = [0] * world
+    mine = [[] for _ in range(world)]
+    for c in sorted(ctx.tolist(), reverse=True):
+        r = loads.index(min(loads))
+        loads[r] += c
+        mine[r].append(c)
+    return mine[rank], 'strong'
+
+
+def peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d['hbm_gbs']), 'measured'
+    return FALLBACK_HBM_GBS, 'fallback'
+
+
+def ncu_traffic():
+    p = ROOT / 'profiles' / 'ncu_traffic.json'
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text())
+    except json.JSONDecodeError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.gpu, self.proc, self.file = str(gpu_index), None, None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200'], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(',')]
+            if len(parts) >= 9 and parts[0] == self.gpu:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == 'active'})
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': float(rows[0][2]),
+                'samples': len(rows), 'reasons': reasons,
+                'power_w_max': max(float(r[3]) for r in rows if r[3].replace('.', '').isdigit())}
+
+
+# ----------------------------------------------------------------------------- CPU oracle baseline
+class CpuSample:
+    """The oracle's per-(layer, loop) decode composition (writer GEMM, latent query, exact window, paged
+    history, B, merge) at widths 512 and 256 on ``rows_sample`` sequences of the workload (the longest:
+    an upper bound on the work per row).  Inputs are built and the path run once untimed (BLAS thread
+    start, page faults) in the constructor; ``run()`` times one pass and extrapolates it to a full step:
+    24 x (3 t_512 + t_256) x (B / rows_sample) seconds."""
+
+    def __init__(self, ctx_list, shape, rows_sample, seed=0):
+        import numpy as np
+        from oracle import s6_oracle as orc
+        self.orc, self.np, self.shape = orc, np, shape
+        rng = np.random.default_rng(seed)
+        self.B = len(ctx_list)
+        sample = sorted(ctx_list, reverse=True)[:rows_sample]
+        H, d, page, W_ = shape.heads, shape.head_dim, shape.page, shape.window
+        self.scale = 1 / math.sqrt(d)
+        self.data = {}
+        n = len(sample)
+        for width in (shape.rank, shape.rank1):
+            pages = [-(-(c + 1) // page) for c in sample]
+            lat = rng.standard_normal((sum(pages) + 1, 1, page, 2 * width), dtype=np.float32)
+            ltab = np.zeros((n, max(pages)), dtype=np.int32)
+            k = 1
+            for r, p in enumerate(pages):
+                ltab[r, :p] = np.arange(k, k + p)
+                k += p
+            etab = np.zeros_like(ltab)           # exact cache: only each row's window pages exist
+            k = 1
+            for r, c in enumerate(sample):
+                for col in range(max(0, c - W_) // page, c // page + 1):
+                    etab[r, col] = k
+                    k += 1
+            self.data[width] = dict(
+                lat=lat, ltab=ltab, etab=etab, ex=rng.standard_normal((k, H, page, 2 * d), dtype=np.float32),
+                q_pre=rng.standard_normal((n, H, d), dtype=np.float32),
+                h=rng.standard_normal((n, shape.hidden), dtype=np.float32),
+                E=rng.standard_normal((2 * width, shape.hidden), dtype=np.float32),
+                A=rng.standard_normal((H, d, width), dtype=np.float32),
+                Bm=rng.standard_normal((H, width, d), dtype=np.float32),
+                tab=np.zeros((max(sample) + 1, width), dtype=np.float32), pos=np.asarray(sample),
+                qsl=np.arange(n + 1, dtype=np.int32), seq=np.asarray(sample, dtype=np.int32) + 1,
+                ctx_lat=np.maximum(np.asarray(sample) - W_, 0), invalid=np.zeros(n, dtype=bool))
+        self.n, self.ctx_max = n, max(sample)
+        self.run()
+
+    def _one(self, width):
+        D, orc, np = self.data[width], self.orc, self.np
+        _ = D['h'] @ D['E'].T                                                     # writer projection
+        q_lat = orc.latent_query(D['q_pre'], D['A'], D['pos'], D['tab'], dt=np.float32)  # absorb + RoPE
+        orc.attend_decode(q_lat, D['q_pre'], D['lat'], D['ltab'], D['ctx_lat'], D['ex'], D['etab'], D['qsl'],
+                          D['seq'], self.shape.window, D['Bm'], self.scale, D['invalid'], dt=np.float32)
+
+    def run(self):
+        s = self.shape
+        t = {}
+        for width in (s.rank, s.rank1):
+            t0 = time.perf_counter()
+            self._one(width)
+            t[width] = time.perf_counter() - t0
+        return s.layers * ((s.loops - 1) * t[s.rank] + t[s.rank1]) * (self.B / self.n)
+
+    def describe(self):
+        s = self.shape
+        return (f'oracle numpy fp32 per-(layer, loop) decode op (writer GEMM, latent query, window, paged history, '
+                f'B, merge) at widths {s.rank}/{s.rank1} on {self.n} of {self.B} sequences (ctx {self.ctx_max}), '
+                f'extrapolated x{s.layers} layers x (3+1) loops x {self.B}/{self.n}')
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        return max(i['num_threads'] for i in threadpoolctl.threadpool_info()) or os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def run_reference(args):
+    """--impl reference: the CPU oracle port of the reference path on this host, rank 0 only."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    dec = importlib.import_module(f'{PKG}.decode')
+    shape = dec.OuroShape()
+    ctx, scaling = config_batch(args.config, 0, 1 if args.config == 2 else world, args.seed)
+    cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        sec = cs.run()
+        if i >= args.warmup:
+            samples.append(sec)
+    desc = cs.describe()
+    sec = statistics.mean(samples)
+    tok = len(ctx) / sec
+    line = {'metric': METRIC, 'value': tok, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': sec * 1e3, 'higher_is_better': True, 'scaling': scaling,
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded)', 'impl': 'reference',
+            'config': {'workload': f'BASELINE config {args.config}: S6 decode step attention path',
+                       'global_batch': len(ctx), 'ctx': max(ctx), 'parallelism': 'host cores'},
+            'cpu_baseline': {'value': tok, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
+                             'sample': desc},
+            'e2e': {'value': tok, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def time_graph(torch, graph, steps, dist, flush=None):
+    """Device time of ``steps`` replays (ms, max over ranks), barrier + synchronize on both sides."""
+    stream = torch.cuda.current_stream()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device='cuda')
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    importlib.import_module(f'{PKG}._lib').load()
+    dec = importlib.import_module(f'{PKG}.decode')
+    shape = dec.OuroShape()
+    ctx, scaling = config_batch(args.config, rank, world, args.seed)
+    model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=args.seed + rank)
+    torch.cuda.synchronize()
+    model.step()                       # eager warm-up: descriptor caches, occupancy
+    graph = model.capture()
+    hist_graph = model.capture_history()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ---- value: device-timed graph replays, clocks sampled meanwhile
+    with ClockSampler(local) as clk:
+        ms_total = time_graph(torch, graph, args.steps, dist)
+    clocks = clk.summary()
+    ms_step = ms_total / args.steps
+    tokens_all = len(ctx) * (world if scaling == 'weak' else 1)
+    if scaling == 'strong':
+        tokens_all = 256
+    value = tokens_all / (ms_step / 1e3)
+
+    # ---- roofline of the dominant kernel: the 96 history launches of a step, alone
+    for _ in range(3):
+        hist_graph.replay()
+    ms_hist = time_graph(torch, hist_graph, args.steps, dist) / args.steps
+    hist_launches = shape.layers * shape.loops
+    bytes_hist = model.latent_bytes_per_step()
+    achieved = bytes_hist / (ms_hist / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    tr = ncu_traffic()
+    if tr and args.config == 2:
+        traffic = tr.get('history_split_w512_bytes_per_launch_config2')
+
+    # ---- e2e: pinned host activations in, outputs out, every step
+    host_in = torch.empty(model.acts.shape, dtype=model.acts.dtype, pin_memory=True)
+    host_in.copy_(model.acts)
+    host_out = torch.empty(model.out.shape, dtype=model.out.dtype, pin_memory=True)
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        model.acts.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(model.out, non_blocking=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        model.acts.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(model.out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([ms_e2e], device='cuda')
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = {'value': tokens_all / (ms_e2e / 1e3), 'unit': 'tokens/s',
+           'h2d_bytes_per_step': host_in.numel() * host_in.element_size(),
+           'd2h_bytes_per_step': host_out.numel() * host_out.element_size(),
+           'path': 'S6DecodeModel CUDA-graph step (public API) with pinned host activations in and outputs out'}
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
+            secs = [cs.run() for _ in range(args.cpu_reps)]
+            sec, desc = statistics.median(secs), cs.describe() + f'; median of {args.cpu_reps} timed passes'
+            cpu = {'value': len(ctx) / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
+                   'sample': desc}
+        attn_bytes = model.latent_bytes_per_step() + model.window_bytes_per_step()
+        line = {
+            'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': scaling,
+            'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded), random-init weights',
+            'config': {'workload': f'BASELINE config {args.config}: Ouro-1.4B-shaped S6 decode step, attention path '
+                                   f'(24 layers x 4 loops), dense body excluded',
+                       'global_batch': tokens_all, 'batch_per_gpu': len(ctx), 'ctx': max(ctx),
+                       'seq_len': max(ctx) + 1, 'page': shape.page, 'window': shape.window,
+                       'parallelism': f'request-partitioned x{world} (no collectives)',
+                       'l2': 'inputs larger than L2 (latent caches ~40 GB per GPU), no flush'},
+            'latent_history': {'bytes_per_step': bytes_hist, 'GBps_in_step': bytes_hist / (ms_step / 1e3) / 1e9,
+                               'attention_bytes_per_step': attn_bytes,
+                               'attention_GBps': attn_bytes / (ms_step / 1e3) / 1e9,
+                               'frac_of_peak_in_step': attn_bytes / (ms_step / 1e3) / 1e9 / peak},
+            'roofline': {'bound': 'hbm', 'kernel': 'history_split_kernel (96 launches per step)',
+                         'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
+                         'peak_source': f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured'
+                         else 'fallback 6.65 TB/s', 'ms_per_launch': ms_hist / hist_launches,
+                         'bytes_per_launch': bytes_hist / hist_launches, 'traffic': traffic},
+            'cpu_baseline': cpu,
+            'e2e': e2e,
+            'gpu_launches': model.launches_per_step() * args.steps,
+            'clocks': clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph, hist_graph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=100)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--config', type=int, default=2, choices=[2, 4])
+    ap.add_argument('--seed', type=int, default=0)
+    ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
+    ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')
+    ap.add_argument('--no-cpu', action='store_true', help='skip the CPU baseline leg')
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit('--warmup must be >= 3')
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -28,6 +28,19 @@ SIGNATURES = {
                                 _i32, P, _i64, P, P],
     'hla_s6_history_reduce': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i64, _i64, P, P, P],
     'hla_s6_history_plan': [_i32, _i32, _i32, _i32, _i32, _i64, P, P, P],
+    'hla_s6_window_attention': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32,
+                                _i32, _i32, _i32, P, _i64, _i64, P, P],
+    'hla_s6_merge_states': [P, _i64, _i64, P, P, _i64, _i64, P, P, P, _i64, _i64, _i32, _i32, _i32, P],
+    'hla_s6_merge_lse': [P, _i64, _i64, P, P, _i64, _i64, P, P, _i64, _i64, P, _i32, _i32, _i32, P],
+    'hla_s6_latent_rope': [P, _i64, _i64, _i32, _i32, _i32, P, P, _i64, _i64, P],
+    'hla_s6_latent_query': [P, _i64, _i64, P, _i64, _i64, P, P, _i64, _i64, P, _i64, _i64, _i32, _i32, _i32, _i32, P],
+    'hla_s6_exact_append': [P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, P, _i64, _i64, P, _i64,
+                            _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _i32, _i32, _i32, P, P],
+    'hla_s6_writer_project': [P, _i64, P, _i64, P, _i64, P, _i64, _i32, _i32, _i32, P],
+    'hla_s6_commit_rows': [P, _i64, _i32, P, P, _i64, _i64, P, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _i32,
+                           P, P],
+    'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, P, _i64, _i64, P, _i64, _i64, P, _i64,
+                              _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, P],
 }
 
 _lib = None

@@ -1,0 +1,275 @@
+// Exported C entry points of the decode ops around the history reader (include/hla_s6.h).
+#include "../../include/hla_s6.h"
+#include "combine.cuh"
+#include "decode_ops.cuh"
+#include "hla_s6_internal.h"
+
+namespace hla {
+
+static bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+static int check_window(const WindowArgs& w, int head_dim) {
+  if (head_dim != 128) {
+    set_error("exact window kernel is built for head_dim 128 (got %d)", head_dim);
+    return kStatusInvalid;
+  }
+  if (w.window < 0 || w.window > 127) {
+    set_error("window %d unsupported (0..127)", w.window);
+    return kStatusInvalid;
+  }
+  if (w.page < 1 || !aligned(w.cache, 16) || (w.c_sb % 8) || (w.c_sh % 8) || (w.c_sr % 8)) {
+    set_error("exact cache needs a 16-byte aligned base and strides that are multiples of 8 elements");
+    return kStatusInvalid;
+  }
+  if (!aligned(w.q, 4) || (w.q_st % 2) || (w.q_sh % 2)) {
+    set_error("q needs even strides and a unit last-dim stride");
+    return kStatusInvalid;
+  }
+  return kStatusOk;
+}
+
+static WindowArgs make_window(const void* q, int64_t q_st, int64_t q_sh, const void* cache, int64_t num_blocks,
+                              int64_t c_sb, int64_t c_sh, int64_t c_sr, int32_t page, const int32_t* bt,
+                              int64_t bt_st, int32_t max_blocks, const int32_t* qsl, int32_t R,
+                              const int32_t* seq_lens, int32_t window, float scale) {
+  WindowArgs w;
+  w.q = static_cast<const __nv_bfloat16*>(q);
+  w.q_st = q_st;
+  w.q_sh = q_sh;
+  w.cache = static_cast<const __nv_bfloat16*>(cache);
+  w.c_sb = c_sb;
+  w.c_sh = c_sh;
+  w.c_sr = c_sr;
+  w.num_blocks = num_blocks;
+  w.page = page;
+  w.bt = bt;
+  w.bt_st = bt_st;
+  w.max_blocks = max_blocks;
+  w.qsl = qsl;
+  w.R = R;
+  w.seq_lens = seq_lens;
+  w.window = window;
+  w.scale = scale;
+  return w;
+}
+
+}  // namespace hla
+
+using namespace hla;
+
+extern "C" {
+
+int hla_s6_window_attention(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                            int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                            int64_t cache_stride_row, int32_t page, const int32_t* block_table,
+                            int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
+                            int32_t num_reqs, const int32_t* seq_lens, int32_t window, float scale,
+                            int32_t num_tokens, int32_t num_heads, int32_t head_dim, void* out, int64_t out_stride_t,
+                            int64_t out_stride_h, float* lse, void* stream) {
+  WindowArgs w = make_window(q, q_stride_t, q_stride_h, cache, num_blocks, cache_stride_block, cache_stride_head,
+                             cache_stride_row, page, block_table, block_table_stride, max_blocks, query_start_loc,
+                             num_reqs, seq_lens, window, scale);
+  int rc = check_window(w, head_dim);
+  if (rc) return rc;
+  if (num_reqs < 1) {
+    set_error("window attention needs at least one request");
+    return kStatusInvalid;
+  }
+  return window_attention(w, num_tokens, num_heads, out, out_stride_t, out_stride_h, lse,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_merge_states(const void* o_hist, int64_t hist_stride_t, int64_t hist_stride_h, const float* lse_hist,
+                        const void* o_chunk, int64_t chunk_stride_t, int64_t chunk_stride_h, const float* lse_chunk,
+                        const uint8_t* invalid, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                        int32_t num_tokens, int32_t num_heads, int32_t dim, void* stream) {
+  return merge(o_hist, hist_stride_t, hist_stride_h, lse_hist, o_chunk, chunk_stride_t, chunk_stride_h, lse_chunk,
+               invalid, out, out_stride_t, out_stride_h, nullptr, num_tokens, num_heads, dim, 0,
+               static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_merge_lse(const void* o1, int64_t o1_stride_t, int64_t o1_stride_h, const float* lse1, const void* o2,
+                     int64_t o2_stride_t, int64_t o2_stride_h, const float* lse2, void* out, int64_t out_stride_t,
+                     int64_t out_stride_h, float* lse_out, int32_t num_tokens, int32_t num_heads, int32_t dim,
+                     void* stream) {
+  return merge(o1, o1_stride_t, o1_stride_h, lse1, o2, o2_stride_t, o2_stride_h, lse2, nullptr, out, out_stride_t,
+               out_stride_h, lse_out, num_tokens, num_heads, dim, 1, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_latent_rope(void* x, int64_t x_stride_t, int64_t x_stride_h, int32_t num_tokens, int32_t num_heads,
+                       int32_t width, const int64_t* positions, const void* table, int64_t table_stride,
+                       int64_t max_position, void* stream) {
+  if (width < 2 || (width % 2) || max_position < 1 || table_stride < width) {
+    set_error("latent rope needs an even width and a [max_position, width] table");
+    return kStatusInvalid;
+  }
+  return latent_rope(x, x_stride_t, x_stride_h, num_tokens, num_heads, width, positions, table, table_stride,
+                     max_position, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_latent_query(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A, int64_t a_stride_h,
+                        int64_t a_stride_k, const int64_t* positions, const void* table, int64_t table_stride,
+                        int64_t max_position, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                        int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t width, void* stream) {
+  if (head_dim != 128) {
+    set_error("latent query is built for head_dim 128 (got %d)", head_dim);
+    return kStatusInvalid;
+  }
+  if (max_position < 1 || table_stride < width) {
+    set_error("latent query needs a [max_position, width] RoPE table");
+    return kStatusInvalid;
+  }
+  return latent_query(q_pre, q_stride_t, q_stride_h, A, a_stride_h, a_stride_k, positions, table, table_stride,
+                      max_position, out, out_stride_t, out_stride_h, num_tokens, num_heads, width,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                        int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, void* k_out,
+                        int64_t k_out_stride_t, int64_t k_out_stride_h, const int64_t* positions,
+                        const float* cos_sin, int64_t cos_sin_stride, int64_t max_position, void* cache,
+                        int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                        int64_t cache_stride_row, int32_t page, const int32_t* block_table, int64_t block_table_stride,
+                        int32_t max_blocks, const int32_t* query_start_loc, int32_t num_reqs, int32_t num_tokens,
+                        int32_t num_heads, int32_t head_dim, int64_t* slot_out, void* stream) {
+  if (head_dim != 128 || page < 1 || num_reqs < 1 || max_position < 1 || cos_sin_stride < 128) {
+    set_error("exact append needs head_dim 128, page >= 1, >= 1 request and a [max_position, 128] cos|sin table");
+    return kStatusInvalid;
+  }
+  ExactArgs a;
+  a.q = static_cast<__nv_bfloat16*>(q);
+  a.q_st = q_stride_t;
+  a.q_sh = q_stride_h;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.k_st = k_stride_t;
+  a.k_sh = k_stride_h;
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.v_st = v_stride_t;
+  a.v_sh = v_stride_h;
+  a.k_out = static_cast<__nv_bfloat16*>(k_out);
+  a.ko_st = k_out_stride_t;
+  a.ko_sh = k_out_stride_h;
+  a.positions = positions;
+  a.cos_sin = cos_sin;
+  a.cs_st = cos_sin_stride;
+  a.max_pos = max_position;
+  a.cache = static_cast<__nv_bfloat16*>(cache);
+  a.c_sb = cache_stride_block;
+  a.c_sh = cache_stride_head;
+  a.c_sr = cache_stride_row;
+  a.num_blocks = num_blocks;
+  a.page = page;
+  a.bt = block_table;
+  a.bt_st = block_table_stride;
+  a.max_blocks = max_blocks;
+  a.qsl = query_start_loc;
+  a.R = num_reqs;
+  a.H = num_heads;
+  a.slot_out = slot_out;
+  return exact_append(a, num_tokens, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_writer_project(const void* h, int64_t h_stride_t, const void* weight, int64_t weight_stride_n,
+                          const void* reg_in, int64_t reg_in_stride_t, void* reg_out, int64_t reg_out_stride_t,
+                          int32_t num_tokens, int32_t out_features, int32_t in_features, void* stream) {
+  if (in_features % 16 || out_features % 2 || (h_stride_t % 2) || (weight_stride_n % 2) || !aligned(h, 4) ||
+      !aligned(weight, 4) || (reg_in && ((reg_in_stride_t % 2) || !aligned(reg_in, 4))) || (reg_out_stride_t % 2) ||
+      !aligned(reg_out, 4)) {
+    set_error("writer projection needs in_features % 16 == 0, even out_features and even row strides");
+    return kStatusInvalid;
+  }
+  return writer_project(h, h_stride_t, weight, weight_stride_n, reg_in, reg_in_stride_t, reg_out, reg_out_stride_t,
+                        num_tokens, out_features, in_features, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, const int64_t* positions,
+                       const void* table, int64_t table_stride, int64_t max_position, void* cache, int64_t num_blocks,
+                       int64_t cache_stride_block, int64_t cache_stride_row, int32_t page, const int32_t* block_table,
+                       int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
+                       int32_t num_reqs, int32_t num_tokens, int64_t* slot_out, void* stream) {
+  if (width < 2 || (width % 2) || page < 1 || num_reqs < 1 || max_position < 1 || table_stride < width) {
+    set_error("commit rows needs an even width, page >= 1, >= 1 request and a [max_position, width] table");
+    return kStatusInvalid;
+  }
+  CommitArgs a;
+  a.row = static_cast<const __nv_bfloat16*>(row);
+  a.row_st = row_stride_t;
+  a.w = width;
+  a.positions = positions;
+  a.table = static_cast<const __nv_bfloat16*>(table);
+  a.tab_st = table_stride;
+  a.max_pos = max_position;
+  a.cache = static_cast<__nv_bfloat16*>(cache);
+  a.c_sb = cache_stride_block;
+  a.c_sr = cache_stride_row;
+  a.num_blocks = num_blocks;
+  a.page = page;
+  a.bt = block_table;
+  a.bt_st = block_table_stride;
+  a.max_blocks = max_blocks;
+  a.qsl = query_start_loc;
+  a.R = num_reqs;
+  a.slot_out = slot_out;
+  return commit_rows(a, num_tokens, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
+                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
+                          const float* lse_in, const uint8_t* empty, const void* B, int64_t b_stride_h,
+                          int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
+                          const void* exact_cache, int64_t exact_num_blocks, int64_t exact_stride_block,
+                          int64_t exact_stride_head, int64_t exact_stride_row, int32_t exact_page,
+                          const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                          const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
+                          float scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse_out,
+                          void* stream) {
+  CombineParams p;
+  p.win = make_window(q_rope, q_stride_t, q_stride_h, exact_cache, exact_num_blocks, exact_stride_block,
+                      exact_stride_head, exact_stride_row, exact_page, block_table, block_table_stride, max_blocks,
+                      query_start_loc, num_reqs, seq_lens, window, scale);
+  int rc = check_window(p.win, 128);
+  if (rc) return rc;
+  if (num_heads < 1 || num_heads > 16 || num_reqs < 1) {
+    set_error("decode combine needs 1..16 heads and >= 1 request");
+    return kStatusInvalid;
+  }
+  if ((out_stride_t % 2) || (out_stride_h % 2)) {
+    set_error("decode combine output needs even strides");
+    return kStatusInvalid;
+  }
+  HistoryPlan plan{};
+  if (!z_in) {
+    HistoryArgs a{};
+    a.T = num_tokens;
+    a.H = num_heads;
+    a.W = width;
+    a.page = latent_page;
+    a.num_kv_splits = num_kv_splits;
+    a.ws = workspace;
+    a.ws_floats = workspace_floats;
+    a.waves = 1;
+    if ((rc = history_plan(a, &plan))) return rc;
+  } else if (!lse_in || !aligned(z_in, 16)) {
+    set_error("a reduced history input needs a 16-byte aligned z [T, H, W] and its lse [H, T]");
+    return kStatusInvalid;
+  }
+  p.ws_o = plan.ws_o;
+  p.ws_lse = plan.ws_lse;
+  p.meta = plan.meta;
+  p.stream_mode = plan.stream_mode;
+  p.z_in = z_in;
+  p.lse_in = lse_in;
+  p.empty = empty;
+  p.T = num_tokens;
+  p.H = num_heads;
+  p.B = static_cast<const __nv_bfloat16*>(B);
+  p.b_sh = b_stride_h;
+  p.b_sk = b_stride_k;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_st = out_stride_t;
+  p.o_sh = out_stride_h;
+  p.lse_out = lse_out;
+  return decode_combine(p, width, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

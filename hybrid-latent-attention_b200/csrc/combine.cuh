@@ -1,0 +1,28 @@
+// Argument block of the fused decode combine (combine.cu).
+#pragma once
+#include "decode_ops.cuh"
+
+namespace hla {
+
+struct CombineParams {
+  // history input: split partials of the history kernel (ws_o / ws_lse / meta as planned for the
+  // same call) or, when z_in is set, a reduced fp32 z [T, H, W] with lse_in [H, T]
+  const float* ws_o;
+  const float* ws_lse;
+  const int2* meta;
+  int stream_mode;
+  const float* z_in;
+  const float* lse_in;
+  const uint8_t* empty;  // optional [T]: rows whose latent history is empty
+  int T, H;
+  const __nv_bfloat16* B;  // [H, W, 128] up-projection
+  int64_t b_sh, b_sk;
+  WindowArgs win;
+  __nv_bfloat16* out;  // [T, H, 128]
+  int64_t o_st, o_sh;
+  float* lse_out;  // optional [H, T] merged lse
+};
+
+int decode_combine(const CombineParams& p, int W, cudaStream_t s);
+
+}  // namespace hla

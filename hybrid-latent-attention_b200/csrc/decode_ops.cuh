@@ -1,0 +1,229 @@
+// Device helpers and argument blocks shared by decode_ops.cu and combine.cu.
+#pragma once
+#include "common.cuh"
+
+namespace hla {
+
+__device__ __forceinline__ int64_t clamp_pos(int64_t p, int64_t max_pos) {
+  return p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);
+}
+
+// Token -> request of a varlen batch (s6_ops.py:61-68): r = #{i in 1..R : qsl[i] <= t},
+// clamped to R - 1; valid = t < qsl[R].
+__device__ __forceinline__ bool token_request(const int32_t* __restrict__ qsl, int R, int t, int& r) {
+  int lo = 1, hi = R + 1;  // first i in [1, R] with qsl[i] > t
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (qsl[mid] <= t) lo = mid + 1; else hi = mid;
+  }
+  r = min(lo - 1, R - 1);
+  return t < qsl[R];
+}
+
+// Neox rotate-half pair (x1 at i, x2 at i + w/2) in the torch bf16 operation order:
+// y1 = bf16(bf16(x1*c) + bf16(-x2*s)), y2 = bf16(bf16(x2*c) + bf16(x1*s)).
+__device__ __forceinline__ void rope_pair_torch(float x1, float x2, float c, float s, float& y1, float& y2) {
+  const float a1 = bf16_round(x1 * c), b1 = bf16_round(-x2 * s);
+  const float a2 = bf16_round(x2 * c), b2 = bf16_round(x1 * s);
+  y1 = bf16_round(a1 + b1);
+  y2 = bf16_round(a2 + b2);
+}
+
+// merge_states weights (s6_ops.py:275-284): +inf lse is empty, both empty -> 0.
+__device__ __forceinline__ void merge_weights_states(float l1, float l2, float& w1, float& w2) {
+  if (l1 == INFINITY) l1 = -INFINITY;
+  if (l2 == INFINITY) l2 = -INFINITY;
+  float peak = fmaxf(l1, l2);
+  if (isinf(peak)) peak = 0.f;
+  const float e1 = expf(l1 - peak), e2 = expf(l2 - peak), tot = e1 + e2;
+  w1 = tot > 0.f ? e1 / tot : 0.f;
+  w2 = tot > 0.f ? e2 / tot : 0.f;
+}
+
+// merge_lse weights (s6_ops.py:353-361).
+__device__ __forceinline__ void merge_weights_lse(float l1, float l2, float& w1, float& w2) {
+  float peak = fmaxf(l1, l2);
+  if (isinf(peak)) peak = 0.f;
+  const float e1 = expf(l1 - peak), e2 = expf(l2 - peak), tot = e1 + e2;
+  w1 = tot > 0.f ? e1 / tot : 0.f;
+  w2 = tot > 0.f ? e2 / tot : 0.f;
+}
+
+__device__ __forceinline__ float merged_lse(float l1, float l2) {
+  float peak = fmaxf(l1, l2);
+  if (isinf(peak)) peak = 0.f;
+  return peak + logf(expf(l1 - peak) + expf(l2 - peak));
+}
+
+// ------------------------------------------------------------------ exact window (A5)
+struct WindowArgs {
+  const __nv_bfloat16* q;  // roped q [T, H, 128]
+  int64_t q_st, q_sh;
+  const __nv_bfloat16* cache;  // logical [nb, H, page, 256] (K | V); strides per block, head, row
+  int64_t c_sb, c_sh, c_sr;
+  int64_t num_blocks;
+  int page;
+  const int32_t* bt;  // per-request block table [R, max_blocks]
+  int64_t bt_st;
+  int max_blocks;
+  const int32_t* qsl;  // query_start_loc [R + 1]
+  int R;
+  const int32_t* seq_lens;  // [R]
+  int window;
+  float scale;
+};
+
+// One warp computes the exact window attention of token t, head h over keys
+// [pos - window, pos] (pos = seq_len - query_len + index in chunk; for decode seq_len - 1),
+// the current token included.  Lane l owns dims 4l..4l+3 of the output.  Invalid tokens or
+// an empty key range give o = 0, lse = -inf.  q_s: 128 floats of this warp's shared memory.
+__device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, float* q_s, float (&o)[4],
+                                            float& lse) {
+  const int lane = threadIdx.x & 31;
+  o[0] = o[1] = o[2] = o[3] = 0.f;
+  lse = -INFINITY;
+  int r;
+  if (!token_request(a.qsl, a.R, t, r)) return;
+  const int qlen = a.qsl[r + 1] - a.qsl[r];
+  const int64_t pos = static_cast<int64_t>(a.seq_lens[r]) - qlen + (t - a.qsl[r]);
+  if (pos < 0) return;
+  const int64_t first = pos - a.window > 0 ? pos - a.window : 0;
+  const int n = static_cast<int>(pos - first + 1);
+  {
+    const __nv_bfloat16* qp = a.q + static_cast<int64_t>(t) * a.q_st + static_cast<int64_t>(h) * a.q_sh + lane * 4;
+    const __nv_bfloat162 p0 = reinterpret_cast<const __nv_bfloat162*>(qp)[0];
+    const __nv_bfloat162 p1 = reinterpret_cast<const __nv_bfloat162*>(qp)[1];
+    q_s[lane * 4 + 0] = __bfloat162float(p0.x);
+    q_s[lane * 4 + 1] = __bfloat162float(p0.y);
+    q_s[lane * 4 + 2] = __bfloat162float(p1.x);
+    q_s[lane * 4 + 3] = __bfloat162float(p1.y);
+  }
+  __syncwarp();
+  constexpr int MAXC = 4;  // up to 128 keys (window <= 127)
+  float sc[MAXC];
+  int64_t off[MAXC];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int ch = 0; ch < MAXC; ++ch) {
+    sc[ch] = -INFINITY;
+    off[ch] = -1;
+    const int kb = ch * 32 + lane;
+    if (ch * 32 >= n) continue;
+    if (kb < n) {
+      const int64_t j = first + kb;
+      const int64_t col = j / a.page;
+      if (col < a.max_blocks) {
+        const int blk = a.bt[static_cast<int64_t>(r) * a.bt_st + col];
+        if (blk >= 0 && blk < a.num_blocks) {
+          off[ch] = static_cast<int64_t>(blk) * a.c_sb + static_cast<int64_t>(h) * a.c_sh + (j % a.page) * a.c_sr;
+          const uint4* kp = reinterpret_cast<const uint4*>(a.cache + off[ch]);
+          float dot = 0.f;
+#pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            const uint4 u = __ldg(kp + v);
+            const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              dot = fmaf(q_s[v * 8 + 2 * e], __bfloat162float(b[e].x), dot);
+              dot = fmaf(q_s[v * 8 + 2 * e + 1], __bfloat162float(b[e].y), dot);
+            }
+          }
+          sc[ch] = dot * a.scale;
+        }
+      }
+    }
+    mx = fmaxf(mx, sc[ch]);
+  }
+  mx = warp_max(mx);
+  if (mx == -INFINITY) return;
+  float l = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < MAXC; ++ch) {
+    sc[ch] = sc[ch] == -INFINITY ? 0.f : expf(sc[ch] - mx);
+    l += sc[ch];
+  }
+  l = warp_sum(l);
+#pragma unroll
+  for (int ch = 0; ch < MAXC; ++ch) {
+    if (ch * 32 >= n) break;
+    const int cnt = min(32, n - ch * 32);
+    for (int src = 0; src < cnt; ++src) {
+      const float p = __shfl_sync(0xffffffffu, sc[ch], src);
+      const int64_t ro = __shfl_sync(0xffffffffu, off[ch], src);
+      if (ro < 0) continue;
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.cache + ro + 128 + lane * 4));
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+      o[0] = fmaf(p, __bfloat162float(b[0].x), o[0]);
+      o[1] = fmaf(p, __bfloat162float(b[0].y), o[1]);
+      o[2] = fmaf(p, __bfloat162float(b[1].x), o[2]);
+      o[3] = fmaf(p, __bfloat162float(b[1].y), o[3]);
+    }
+  }
+  const float inv = 1.f / l;
+  o[0] *= inv;
+  o[1] *= inv;
+  o[2] *= inv;
+  o[3] *= inv;
+  lse = mx + logf(l);
+}
+
+// ------------------------------------------------------------------ exact append (A10)
+struct ExactArgs {
+  __nv_bfloat16* q;  // [T, H, 128] roped in place (may be NULL)
+  int64_t q_st, q_sh;
+  const __nv_bfloat16* k;
+  int64_t k_st, k_sh;
+  const __nv_bfloat16* v;
+  int64_t v_st, v_sh;
+  __nv_bfloat16* k_out;  // optional roped k copy [T, H, 128]
+  int64_t ko_st, ko_sh;
+  const int64_t* positions;
+  const float* cos_sin;  // [max_pos, 128] = [cos 64 | sin 64] fp32
+  int64_t cs_st, max_pos;
+  __nv_bfloat16* cache;  // logical [nb, H, page, 256]
+  int64_t c_sb, c_sh, c_sr, num_blocks;
+  int page;
+  const int32_t* bt;
+  int64_t bt_st;
+  int max_blocks;
+  const int32_t* qsl;
+  int R, H;
+  int64_t* slot_out;  // optional [T]
+};
+
+// ------------------------------------------------------------------ committed rows (A9 + A10)
+struct CommitArgs {
+  const __nv_bfloat16* row;  // [T, 2w] (K | V)
+  int64_t row_st;
+  int w;
+  const int64_t* positions;
+  const __nv_bfloat16* table;  // [max_pos, w] = [cos | sin]
+  int64_t tab_st, max_pos;
+  __nv_bfloat16* cache;  // [nb, 1, page, 2w]
+  int64_t c_sb, c_sr, num_blocks;
+  int page;
+  const int32_t* bt;  // per-request block table
+  int64_t bt_st;
+  int max_blocks;
+  const int32_t* qsl;
+  int R;
+  int64_t* slot_out;
+};
+
+// host launchers (decode_ops.cu)
+int window_attention(const WindowArgs& a, int T, int H, void* out, int64_t o_st, int64_t o_sh, float* lse,
+                     cudaStream_t s);
+int merge(const void* o1, int64_t s1t, int64_t s1h, const float* lse1, const void* o2, int64_t s2t, int64_t s2h,
+          const float* lse2, const uint8_t* invalid, void* out, int64_t sot, int64_t soh, float* lse_out, int T, int H,
+          int D, int mode, cudaStream_t s);
+int latent_rope(void* x, int64_t st, int64_t sh, int T, int H, int w, const int64_t* positions, const void* table,
+                int64_t tab_st, int64_t max_pos, cudaStream_t s);
+int latent_query(const void* q, int64_t q_st, int64_t q_sh, const void* A, int64_t a_sh, int64_t a_sk,
+                 const int64_t* positions, const void* table, int64_t tab_st, int64_t max_pos, void* out,
+                 int64_t o_st, int64_t o_sh, int T, int H, int W, cudaStream_t s);
+int exact_append(const ExactArgs& a, int T, cudaStream_t s);
+int writer_project(const void* h, int64_t h_st, const void* E, int64_t e_st, const void* reg_in, int64_t ri_st,
+                   void* reg_out, int64_t ro_st, int T, int N, int K, cudaStream_t s);
+int commit_rows(const CommitArgs& a, int T, cudaStream_t s);
+
+}  // namespace hla

@@ -1,0 +1,252 @@
+"""A whole S6 decode step of an Ouro-1.4B-shaped model through the B200 kernels.
+
+Per step: for loop in 0..3, for layer in 0..23 (the hot loop of hla/vllm_latent/ouro_latent.py:270-274),
+one (layer, loop) of OuroLatentAttention.forward (ouro_latent.py:106-131) without the dense projections:
+
+  1. writer projection       s6_layer.write_rows       (register.py:45-61)
+  2. latent query            ctx.latent_query          (s6_layer.py:32-40, 82-84)
+  3. exact RoPE + append     rotary_emb + unified_kv_cache_update (ouro_latent.py:113-123)
+  4. history split           s6_ops.history_attention stage 1 (s6_ops.py:117-161)
+  5. fused combine           window_attention_fa + stage 2 + einsum B + merge_states (s6_layer.py:97-115)
+  6. committed row           s6_layer.committed_row + unified_kv_cache_update (ouro_latent.py:127-129)
+
+The inputs of a (layer, loop) - pre-RoPE q, k, v and the attention input h - come from a resident
+activation buffer (synthetic, seeded); its output goes to an output buffer.  Caches are paged with
+a shuffled page table (block 0 is the null block); the exact window cache keeps only the pages a
+W-row sliding window touches, as vLLM's sliding-window KV manager does for the reference.
+
+``step()`` issues the launches eagerly; ``capture()`` records one step as a CUDA graph (what the
+reference's FULL_DECODE_ONLY serving replays) and ``replay()`` runs it.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib, s6_layer, s6_ops
+from .latent import LatentLayer
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class OuroShape:
+    """Ouro-1.4B geometry (hla/vendor/config.json) and the S6 student widths (register.py:98-100)."""
+    layers: int = 24
+    hidden: int = 2048
+    heads: int = 16
+    head_dim: int = 128
+    loops: int = 4
+    rank: int = 512
+    rank1: int = 256
+    page: int = 16
+    window: int = 32
+    theta: float = 1e6
+    max_position: int = 65536
+
+
+@dataclass
+class DecodeBatch:
+    """Per-request history lengths (tokens before the current one)."""
+    ctx: list = field(default_factory=lambda: [8192] * 64)
+
+
+class S6DecodeModel:
+    def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512):
+        self.s, self.device = shape, torch.device(device)
+        s = shape
+        B = len(batch.ctx)
+        self.B = B
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        gen = lambda *shape_, std=1.0, dtype=BF16: (torch.randn(*shape_, generator=g, device=self.device) * std).to(dtype)
+        ctx = torch.tensor(batch.ctx, dtype=torch.int64)
+        self.ctx_host = ctx
+        if int(ctx.max()) + 1 > s.max_position:
+            raise ValueError(f'context {int(ctx.max())} exceeds max_position {s.max_position}')
+        # ---- weights: one latent student per layer (random init, bf16)
+        self.layers = []
+        for _ in range(s.layers):
+            lat = LatentLayer(s.hidden, s.heads, s.head_dim, s.loops, s.rank, s.rank, s.rank1)
+            with torch.no_grad():
+                lat = lat.to(self.device, BF16)
+                for p in (lat.q_absorb, lat.q_absorb1):
+                    p.copy_(gen(*p.shape, std=1 / math.sqrt(s.head_dim)))
+                lat.out_absorb.copy_(gen(*lat.out_absorb.shape, std=1 / math.sqrt(s.rank)))
+                lat.out_absorb1.copy_(gen(*lat.out_absorb1.shape, std=1 / math.sqrt(s.rank1)))
+                for lin in (*lat.cand_s, lat.cand1):
+                    lin.weight.copy_(gen(*lin.weight.shape, std=1 / math.sqrt(s.hidden)))
+            self.layers.append(lat.requires_grad_(False))
+        # ---- step metadata (decode: one token per request)
+        self.positions = ctx.to(self.device)
+        self.qsl = torch.arange(B + 1, dtype=torch.int32, device=self.device)
+        self.seq_lens = (ctx + 1).to(torch.int32).to(self.device)
+        self.ctx_latent = (ctx - s.window).clamp(min=0).to(torch.int32).to(self.device)
+        self.latent_rows = int((ctx - s.window).clamp(min=0).sum())
+        # ---- latent caches: pages for rows [0, ctx] of every request, shuffled
+        lpages = [-(-(c + 1) // s.page) for c in batch.ctx]
+        self.lmax = max(lpages)
+        lnb = sum(lpages) + 1
+        perm = torch.randperm(lnb - 1, generator=torch.Generator().manual_seed(seed + 1)).to(torch.int32) + 1
+        ltab = torch.zeros(B, self.lmax, dtype=torch.int32)
+        k = 0
+        for r, n in enumerate(lpages):
+            ltab[r, :n] = perm[k:k + n]
+            k += n
+        self.latent_table = ltab.to(self.device)
+        self.main = [gen(lnb, 1, s.page, 2 * s.rank) for _ in range(s.layers)]
+        self.l1 = [gen(lnb, 1, s.page, 2 * s.rank1) for _ in range(s.layers)]
+        for c in (*self.main, *self.l1):
+            c[0].fill_(float('inf'))   # null block: any read of it would be loud
+        # ---- exact caches: only the pages of [ctx - W, ctx] exist per request
+        etab = torch.zeros(B, self.lmax, dtype=torch.int32)
+        k = 1
+        for r, c in enumerate(batch.ctx):
+            for col in range(max(0, c - s.window) // s.page, c // s.page + 1):
+                etab[r, col] = k
+                k += 1
+        self.exact_table = etab.to(self.device)
+        self.exact = [[gen(k, s.page, s.heads, 2 * s.head_dim) for _ in range(s.loops)] for _ in range(s.layers)]
+        self.exact_logical = [[e.transpose(1, 2) for e in row] for row in self.exact]
+        # ---- RoPE tables
+        inv = s6_layer.latent_inv_freq(s.head_dim, s.theta)
+        self.tables = {w: s6_layer.latent_rope_table(s.max_position, inv, w, BF16).to(self.device)
+                       for w in (s.rank, s.rank1)}
+        ang = torch.arange(s.max_position).float()[:, None] * inv[None]
+        self.cos_sin = torch.cat((ang.cos(), ang.sin()), -1).to(self.device)
+        # ---- workspace and activations
+        props = torch.cuda.get_device_properties(self.device)
+        self.splits = s6_ops.num_kv_splits(s.max_position, B, split_max_tokens, props.multi_processor_count)
+        self.workspace = s6_ops.S6Workspace(s.heads, s.rank, B * self.splits)
+        self.ws = self.workspace.ensure(self.device)
+        self.ws_floats = B * self.splits * s.heads * (s.rank + 1)
+        D = s.heads * s.head_dim
+        self.acts = gen(s.layers, s.loops, B, 3 * D + s.hidden)          # q | k | v | h per (layer, loop)
+        self.out = torch.zeros(s.layers, s.loops, B, s.heads, s.head_dim, dtype=BF16, device=self.device)
+        self.q_lat = torch.empty(B, s.heads, s.rank, dtype=BF16, device=self.device)
+        self.reg = [torch.empty(B, 2 * s.rank, dtype=BF16, device=self.device) for _ in range(s.layers)]
+        self.first = torch.empty(B, 2 * s.rank1, dtype=BF16, device=self.device)
+        self.scale = s.head_dim ** -0.5
+        self.graph = None
+        self.history_graph = None
+
+    # ------------------------------------------------------------------ bytes
+    def latent_bytes_per_step(self):
+        """Algorithmic latent-history bytes of one step: every layer reads ctx_latent rows of the
+        loop-1 latent (2 * rank1 bf16) at loop 0 and of the main latent (2 * rank bf16) at loops 1-3."""
+        s = self.s
+        return s.layers * self.latent_rows * 2 * (2 * s.rank1 + (s.loops - 1) * 2 * s.rank)
+
+    def window_bytes_per_step(self):
+        """Exact window bytes: W rows + the current row, K|V of every head, every loop and layer."""
+        s = self.s
+        rows = int(sum(min(c, s.window) + 1 for c in self.ctx_host.tolist()))
+        return s.layers * s.loops * rows * s.heads * 2 * s.head_dim * 2
+
+    # ------------------------------------------------------------------ launches
+    def _views(self, layer, loop):
+        s, B = self.s, self.B
+        D = s.heads * s.head_dim
+        a = self.acts[layer, loop]
+        q = a[:, :D].view(B, s.heads, s.head_dim)
+        k = a[:, D:2 * D].view(B, s.heads, s.head_dim)
+        v = a[:, 2 * D:3 * D].view(B, s.heads, s.head_dim)
+        h = a[:, 3 * D:]
+        return q, k, v, h
+
+    def _history(self, layer, loop, stream):
+        s, B = self.s, self.B
+        A, _, width = self.layers[layer].readers(loop)
+        cache = self.l1[layer] if loop == 0 else self.main[layer]
+        q_lat = self.q_lat[..., :width] if width != s.rank else self.q_lat
+        _lib.call('hla_s6_history_partials', _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), _lib.ptr(cache),
+                  cache.shape[0], cache.stride(0), cache.stride(2), _lib.ptr(self.latent_table),
+                  self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.ctx_latent), B, s.heads,
+                  width, s.page, float(self.scale), self.splits, _lib.ptr(self.ws), self.ws_floats, None, stream)
+
+    def layer_loop(self, layer, loop, stream):
+        s, B = self.s, self.B
+        lat = self.layers[layer]
+        q, k, v, h = self._views(layer, loop)
+        A, Bm, width = lat.readers(loop)
+        # 1. writer
+        E = lat.writer(loop)
+        dst = self.first if loop == 0 else self.reg[layer]
+        reg_in = None if loop <= 1 else self.reg[layer]
+        _lib.call('hla_s6_writer_project', _lib.ptr(h), h.stride(0), _lib.ptr(E), E.stride(0), _lib.ptr(reg_in),
+                  0 if reg_in is None else reg_in.stride(0), _lib.ptr(dst), dst.stride(0), B, E.shape[0], E.shape[1],
+                  stream)
+        # 2. latent query (pre-RoPE q)
+        q_lat = self.q_lat[..., :width] if width != s.rank else self.q_lat
+        table = self.tables[width]
+        _lib.call('hla_s6_latent_query', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(A), A.stride(0), A.stride(1),
+                  _lib.ptr(self.positions), _lib.ptr(table), table.stride(0), table.shape[0], _lib.ptr(q_lat),
+                  q_lat.stride(0), q_lat.stride(1), B, s.heads, s.head_dim, width, stream)
+        # 3. exact RoPE of q (in place) and k, append k | v to this loop's exact cache
+        ex = self.exact_logical[layer][loop]
+        _lib.call('hla_s6_exact_append', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(k), k.stride(0), k.stride(1),
+                  _lib.ptr(v), v.stride(0), v.stride(1), None, 0, 0, _lib.ptr(self.positions),
+                  _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(ex), ex.shape[0],
+                  ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
+                  self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, B, s.heads,
+                  s.head_dim, None, stream)
+        # 4. history split
+        self._history(layer, loop, stream)
+        # 5. fused combine -> out
+        out = self.out[layer, loop]
+        _lib.call('hla_s6_decode_combine', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws), self.ws_floats,
+                  None, None, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(q), q.stride(0), q.stride(1),
+                  _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
+                  _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
+                  _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), _lib.ptr(out),
+                  out.stride(0), out.stride(1), None, stream)
+        # 6. committed rows: loop-1 latent after loop 0, main latent after the last loop
+        if loop == 0 or loop == s.loops - 1:
+            row = self.first if loop == 0 else self.reg[layer]
+            cache = self.l1[layer] if loop == 0 else self.main[layer]
+            _lib.call('hla_s6_commit_rows', _lib.ptr(row), row.stride(0), width, _lib.ptr(self.positions),
+                      _lib.ptr(table), table.stride(0), table.shape[0], _lib.ptr(cache), cache.shape[0],
+                      cache.stride(0), cache.stride(2), s.page, _lib.ptr(self.latent_table),
+                      self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.qsl), B, B, None, stream)
+
+    def launches_per_step(self):
+        s = self.s
+        return s.layers * (s.loops * 5 + 2)
+
+    def step(self):
+        stream = _lib.stream_of(self.out)
+        for loop in range(self.s.loops):
+            for layer in range(self.s.layers):
+                self.layer_loop(layer, loop, stream)
+
+    def history_only(self):
+        """The 96 history-split launches of a step alone (roofline timing of the dominant kernel)."""
+        stream = _lib.stream_of(self.out)
+        for loop in range(self.s.loops):
+            for layer in range(self.s.layers):
+                self._history(layer, loop, stream)
+
+    # ------------------------------------------------------------------ graphs
+    def _capture(self, fn):
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            fn()                       # warm-up outside capture (descriptor caches, occupancy queries)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        return graph
+
+    def capture(self):
+        self.graph = self._capture(self.step)
+        return self.graph
+
+    def capture_history(self):
+        self.history_graph = self._capture(self.history_only)
+        return self.history_graph
+
+    def replay(self):
+        self.graph.replay()

@@ -151,6 +151,102 @@ def history_attention_kv(q, k, v, block_table, ctx, scale, num_kv_splits, worksp
                              backend, empty)
 
 
+def _bool_ptr(mask):
+    if mask is None:
+        return None
+    return mask if mask.dtype in (torch.bool, torch.uint8) else mask.to(torch.uint8)
+
+
+# ----------------------------------------------------------------------------- A5 exact window
+def _exact_cache_geometry(cache):
+    """Logical TRITON_ATTN view [num_blocks, H, block, 2d] -> (nb, H, block, 2d, strides)."""
+    if cache.dim() != 4 or cache.dtype != torch.bfloat16 or cache.stride(-1) != 1:
+        raise ValueError('exact cache must be a bf16 [num_blocks, H, block, 2*head_dim] view with unit last stride')
+    return cache.shape, cache.stride()
+
+
+def window_attention_fa(q, cache, block_table, query_start_loc, seq_lens, window, scale, max_seqlen_k, invalid):
+    """Decode-only exact window over keys ``[seq_len - 1 - window, seq_len - 1]`` (the window history
+    plus the current token, already written) of the exact cache ``[nb, H, block, 2d]``.
+
+    Per-request ``block_table`` / ``seq_lens``; every request has query length 1.  Returns
+    ``(o[T,H,d] bf16, lse[H,T] fp32)``; ``invalid`` rows get ``o = 0``, ``lse = -inf``
+    (reference s6_ops.py:317-331; ``max_seqlen_k`` is accepted for signature compatibility).
+    """
+    _check_cuda(q, cache, block_table, query_start_loc, seq_lens)
+    T, H, d = q.shape
+    (nb, Hc, block, two_d), (sb, sh, sr, _) = _exact_cache_geometry(cache)
+    if Hc != H or two_d != 2 * d or q.stride(-1) != 1 or q.dtype != torch.bfloat16:
+        raise ValueError('window attention: q [T,H,d] bf16 must match the exact cache [nb, H, block, 2d]')
+    o = torch.empty(T, H, d, dtype=q.dtype, device=q.device)
+    lse = torch.empty(H, T, dtype=torch.float32, device=q.device)
+    _lib.call('hla_s6_window_attention', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(cache), nb, sb, sh, sr,
+              block, _lib.ptr(block_table), block_table.stride(0), block_table.shape[1],
+              _lib.ptr(query_start_loc), query_start_loc.shape[0] - 1, _lib.ptr(seq_lens), int(window), float(scale),
+              T, H, d, _lib.ptr(o), o.stride(0), o.stride(1), _lib.ptr(lse), _lib.stream_of(q))
+    return o, lse
+
+
+# ----------------------------------------------------------------------------- A7 merges
+def merge_states(o_hist, lse_hist, o_chunk, lse_chunk, invalid, backend):
+    """LSE merge of two partial softmaxes; ``[T,H,D]`` outputs, ``[H,T]`` fp32 lse; ``invalid`` rows are
+    zeroed; ``+inf`` lse counts as empty; both empty give 0 (reference s6_ops.py:262-284)."""
+    _require(backend, 'merge')
+    _check_cuda(o_hist, o_chunk, lse_hist, lse_chunk)
+    T, H, D = o_chunk.shape
+    for x in (o_hist, o_chunk):
+        if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+            raise ValueError('merge_states takes bf16 outputs with a unit last-dim stride')
+    out = torch.empty(T, H, D, dtype=o_chunk.dtype, device=o_chunk.device)
+    lh, lc = lse_hist.contiguous(), lse_chunk.contiguous()
+    inv = _bool_ptr(invalid)   # held in a local: the buffer must outlive the launch's argument list
+    _lib.call('hla_s6_merge_states', _lib.ptr(o_hist), o_hist.stride(0), o_hist.stride(1), _lib.ptr(lh),
+              _lib.ptr(o_chunk), o_chunk.stride(0), o_chunk.stride(1), _lib.ptr(lc), _lib.ptr(inv),
+              _lib.ptr(out), out.stride(0), out.stride(1), T, H, D, _lib.stream_of(o_chunk))
+    return out
+
+
+def merge_lse(o1, lse1, o2, lse2):
+    """LSE merge that also returns the merged lse (``[T,H,d]`` outputs, ``[H,T]`` lse); both empty give
+    ``0, -inf``; NaN in either output (FA scratch rows) is ignored (reference s6_ops.py:353-361)."""
+    _check_cuda(o1, o2, lse1, lse2)
+    T, H, D = o1.shape
+    out = torch.empty(T, H, D, dtype=o1.dtype, device=o1.device)
+    lse = torch.empty(H, T, dtype=torch.float32, device=o1.device)
+    l1, l2 = lse1.contiguous(), lse2.contiguous()
+    _lib.call('hla_s6_merge_lse', _lib.ptr(o1), o1.stride(0), o1.stride(1), _lib.ptr(l1), _lib.ptr(o2), o2.stride(0),
+              o2.stride(1), _lib.ptr(l2), _lib.ptr(out), out.stride(0), out.stride(1), _lib.ptr(lse), T, H, D,
+              _lib.stream_of(o1))
+    return out, lse
+
+
+# ----------------------------------------------------------------------------- A4 latent RoPE
+def latent_rope(x, positions, table, backend):
+    """Neox RoPE of ``x`` by ``table[positions]`` IN PLACE; ``table[max_position, w]`` holds ``[cos | sin]``.
+
+    ``x`` is ``[T, w]``, ``[T, H, w]`` (any head stride, unit last stride) or ``[T, H*w]``;
+    ``positions`` int64 ``[T]``.  Per element the torch bf16 order of ``LatentLayer.pack``
+    (register.py:73-79): bit-identical to the reference's training formula.  Returns ``x``
+    (reference s6_ops.py:23-41, vLLM backend semantics: in place).
+    """
+    _require(backend, 'rope')
+    _check_cuda(x, positions, table)
+    w = table.shape[1]
+    if x.dtype != torch.bfloat16 or table.dtype != torch.bfloat16 or x.stride(-1) != 1:
+        raise ValueError('latent_rope takes bf16 x (unit last stride) and a bf16 table')
+    T = x.shape[0]
+    if x.dim() == 3:
+        H, st, sh = x.shape[1], x.stride(0), x.stride(1)
+    elif x.shape[-1] == w:
+        H, st, sh = 1, x.stride(0), w
+    else:
+        H, st, sh = x.shape[-1] // w, x.stride(0), w
+    pos = positions if positions.dtype == torch.int64 else positions.long()
+    _lib.call('hla_s6_latent_rope', _lib.ptr(x), st, sh, T, H, w, _lib.ptr(pos), _lib.ptr(table), table.stride(0),
+              table.shape[0], _lib.stream_of(x))
+    return x
+
+
 def select_backends(head_size=128):
     """The B200 kernel backends for every op; raises when CUDA or libhla_s6 is unavailable
     (reference s6_ops.py:364-372)."""

@@ -78,6 +78,98 @@ int hla_s6_history_reduce(int32_t num_tokens, int32_t num_heads, int32_t width, 
 int hla_s6_history_plan(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, int32_t num_kv_splits,
                         int64_t workspace_floats, int32_t* stream_mode, int32_t* grid, int32_t* slots);
 
+/* Exact window attention of the roped q over keys [pos - window, pos] of a paged exact cache
+ * (the current token already written; pos = seq_len - query_len + index, i.e. seq_len - 1 in
+ * decode).  cache is the logical [num_blocks, H, page, 2 * head_dim] (K | V) view with strides
+ * per block / head / row; block_table is per request; head_dim must be 128, window <= 127.
+ * Invalid (padding) tokens give o = 0, lse = -inf.
+ * Replaces hla/vllm_latent/s6_ops.py:317 window_attention_fa (FA2 varlen, window_size=[W, 0]). */
+int hla_s6_window_attention(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                            int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                            int64_t cache_stride_row, int32_t page, const int32_t* block_table,
+                            int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
+                            int32_t num_reqs, const int32_t* seq_lens, int32_t window, float scale,
+                            int32_t num_tokens, int32_t num_heads, int32_t head_dim, void* out, int64_t out_stride_t,
+                            int64_t out_stride_h, float* lse, void* stream);
+
+/* LSE merge of two partial softmaxes: +inf lse counts as empty, both empty -> 0, invalid rows
+ * zeroed.  Replaces s6_ops.py:262 merge_states (vLLM merge_attn_states; oracle :275-284). */
+int hla_s6_merge_states(const void* o_hist, int64_t hist_stride_t, int64_t hist_stride_h, const float* lse_hist,
+                        const void* o_chunk, int64_t chunk_stride_t, int64_t chunk_stride_h, const float* lse_chunk,
+                        const uint8_t* invalid, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                        int32_t num_tokens, int32_t num_heads, int32_t dim, void* stream);
+
+/* LSE merge that also returns the merged lse; NaN/inf outputs of either side are sanitised.
+ * Replaces s6_ops.py:353 merge_lse. */
+int hla_s6_merge_lse(const void* o1, int64_t o1_stride_t, int64_t o1_stride_h, const float* lse1, const void* o2,
+                     int64_t o2_stride_t, int64_t o2_stride_h, const float* lse2, void* out, int64_t out_stride_t,
+                     int64_t out_stride_h, float* lse_out, int32_t num_tokens, int32_t num_heads, int32_t dim,
+                     void* stream);
+
+/* In-place neox latent RoPE of x [T, H, width] (any token/head stride) by table[positions]
+ * ([max_position, width] = [cos | sin] bf16), in the torch bf16 operation order of
+ * register.py:73-79.  Replaces s6_ops.py:23 latent_rope (vLLM rotary_embedding backend). */
+int hla_s6_latent_rope(void* x, int64_t x_stride_t, int64_t x_stride_h, int32_t num_tokens, int32_t num_heads,
+                       int32_t width, const int64_t* positions, const void* table, int64_t table_stride,
+                       int64_t max_position, void* stream);
+
+/* Latent query: out[t, h, :] = latent_rope(bf16(q_pre[t, h, :] . A[h])) with A [H, 128, width]
+ * (strides a_stride_h, a_stride_k, unit last).  Replaces s6_layer.py:32 latent_query (einsum +
+ * s6_ops.latent_rope). */
+int hla_s6_latent_query(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A, int64_t a_stride_h,
+                        int64_t a_stride_k, const int64_t* positions, const void* table, int64_t table_stride,
+                        int64_t max_position, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                        int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t width, void* stream);
+
+/* Exact-cache append of the current tokens: exact neox RoPE of q (in place, may be NULL) and k
+ * (fp32 math, [max_position, 128] = [cos 64 | sin 64] fp32 table), then k_rope | v written at
+ * slot = block_table[req, pos / page] * page + pos % page; padding tokens are skipped (slot -1).
+ * slot_out (optional int64 [T]) receives the slots.  Replaces the model rotary_emb +
+ * unified_kv_cache_update at hla/vllm_latent/ouro_latent.py:113-123. */
+int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                        int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, void* k_out,
+                        int64_t k_out_stride_t, int64_t k_out_stride_h, const int64_t* positions,
+                        const float* cos_sin, int64_t cos_sin_stride, int64_t max_position, void* cache,
+                        int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                        int64_t cache_stride_row, int32_t page, const int32_t* block_table, int64_t block_table_stride,
+                        int32_t max_blocks, const int32_t* query_start_loc, int32_t num_reqs, int32_t num_tokens,
+                        int32_t num_heads, int32_t head_dim, int64_t* slot_out, void* stream);
+
+/* Writer projection: reg_out = bf16(reg_in + bf16(h . weight^T)) (reg_in may be NULL), weight
+ * [out_features, in_features] as nn.Linear.  Replaces register.py:45-61 write_step / write1
+ * (cand_s[t-1](h) + previous, cand1(h)) called from s6_layer.py:124 write_rows. */
+int hla_s6_writer_project(const void* h, int64_t h_stride_t, const void* weight, int64_t weight_stride_n,
+                          const void* reg_in, int64_t reg_in_stride_t, void* reg_out, int64_t reg_out_stride_t,
+                          int32_t num_tokens, int32_t out_features, int32_t in_features, void* stream);
+
+/* Committed row: row [T, 2 * width] (K | V) -> latent cache [num_blocks, 1, page, 2 * width]
+ * at slot = block_table[req, pos / page] * page + pos % page with the K half latent-RoPE'd
+ * (torch bf16 order) and the V half copied; padding tokens skipped.  Replaces
+ * s6_layer.py:135 committed_row + unified_kv_cache_update at ouro_latent.py:127-129. */
+int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, const int64_t* positions,
+                       const void* table, int64_t table_stride, int64_t max_position, void* cache, int64_t num_blocks,
+                       int64_t cache_stride_block, int64_t cache_stride_row, int32_t page, const int32_t* block_table,
+                       int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
+                       int32_t num_reqs, int32_t num_tokens, int64_t* slot_out, void* stream);
+
+/* Fused decode tail of one (layer, loop): reduce the history partials left by
+ * hla_s6_history_partials (same T, H, width, page, splits, workspace) - or take a reduced
+ * z_in fp32 [T, H, width] with lse_in [H, T] instead - round to bf16, up-project by
+ * B [H, width, 128], run the exact window (as hla_s6_window_attention) and LSE-merge the two
+ * (merge_states semantics; invalid tokens zeroed).  out bf16 [T, H, 128]; lse_out (optional
+ * [H, T]) receives the merged lse.  Replaces s6_layer.py:97-115 (window_attention_fa +
+ * history stage 2 + einsum B + merge_states). */
+int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
+                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
+                          const float* lse_in, const uint8_t* empty, const void* B, int64_t b_stride_h,
+                          int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
+                          const void* exact_cache, int64_t exact_num_blocks, int64_t exact_stride_block,
+                          int64_t exact_stride_head, int64_t exact_stride_row, int32_t exact_page,
+                          const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                          const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
+                          float scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse_out,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif
