@@ -5,7 +5,7 @@ is missing or was built for another ABI version, importing the ops raises.
 """
 from __future__ import annotations
 
-import ctypes
+import ctypes  # noqa: F401  (re-exported for callers that build stream handles)
 import os
 from pathlib import Path
 
@@ -16,6 +16,7 @@ LIB_PATH = Path(os.environ.get('HLA_S6_LIB', _PKG / 'libhla_s6.so'))
 ABI_VERSION = 1
 
 OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
+COMBINE_AFTER_PARTIALS = 1   # hla_s6_decode_combine flag (include/hla_s6.h)
 
 _c_void_p, _i32, _i64, _f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 P = _c_void_p
@@ -37,10 +38,16 @@ SIGNATURES = {
     'hla_s6_exact_append': [P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, P, _i64, _i64, P, _i64,
                             _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _i32, _i32, _i32, P, P],
     'hla_s6_writer_project': [P, _i64, P, _i64, P, _i64, P, _i64, _i32, _i32, _i32, P],
+    'hla_s6_writer_commit': [P, _i64, P, _i64, P, _i64, P, _i64, _i32, _i32, _i32, P, P, _i64, _i64, P, _i64, _i64,
+                             _i64, _i32, P, _i64, _i32, P, _i32, P],
+    'hla_s6_decode_prepare': [P, _i64, _i64, P, _i64, _i64, P, P, _i64, _i64, P, _i64, _i64, _i32, _i32, _i32, _i32,
+                              P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, _i64, _i64,
+                              _i32, P, _i64, _i32, P, _i32, P, P],
     'hla_s6_commit_rows': [P, _i64, _i32, P, P, _i64, _i64, P, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _i32,
                            P, P],
     'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, P, _i64, _i64, P, _i64, _i64, P, _i64,
-                              _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, P],
+                              _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, _i32,
+                              P],
 }
 
 _lib = None

@@ -2,6 +2,7 @@
 #include "../../include/hla_s6.h"
 #include "combine.cuh"
 #include "decode_ops.cuh"
+#include "gemm_ops.cuh"
 #include "hla_s6_internal.h"
 
 namespace hla {
@@ -21,8 +22,8 @@ static int check_window(const WindowArgs& w, int head_dim) {
     set_error("exact cache needs a 16-byte aligned base and strides that are multiples of 8 elements");
     return kStatusInvalid;
   }
-  if (!aligned(w.q, 4) || (w.q_st % 2) || (w.q_sh % 2)) {
-    set_error("q needs even strides and a unit last-dim stride");
+  if (!aligned(w.q, 8) || (w.q_st % 4) || (w.q_sh % 4)) {
+    set_error("q needs 8-byte aligned rows (strides multiples of 4) and a unit last-dim stride");
     return kStatusInvalid;
   }
   return kStatusOk;
@@ -111,17 +112,82 @@ int hla_s6_latent_query(const void* q_pre, int64_t q_stride_t, int64_t q_stride_
                         int64_t a_stride_k, const int64_t* positions, const void* table, int64_t table_stride,
                         int64_t max_position, void* out, int64_t out_stride_t, int64_t out_stride_h,
                         int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t width, void* stream) {
-  if (head_dim != 128) {
-    set_error("latent query is built for head_dim 128 (got %d)", head_dim);
+  return hla_s6_decode_prepare(q_pre, q_stride_t, q_stride_h, A, a_stride_h, a_stride_k, positions, table,
+                               table_stride, max_position, out, out_stride_t, out_stride_h, num_tokens, num_heads,
+                               head_dim, width, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0,
+                               0, 0, 0, 0, nullptr, 0, 0, nullptr, 0, nullptr, stream);
+}
+
+int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A,
+                          int64_t a_stride_h, int64_t a_stride_k, const int64_t* positions, const void* table,
+                          int64_t table_stride, int64_t max_position, void* q_lat, int64_t q_lat_stride_t,
+                          int64_t q_lat_stride_h, int32_t num_tokens, int32_t num_heads, int32_t head_dim,
+                          int32_t width, void* q_rope, int64_t q_rope_stride_t, int64_t q_rope_stride_h,
+                          const void* k, int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
+                          int64_t v_stride_h, const float* cos_sin, int64_t cos_sin_stride, int64_t cos_sin_rows,
+                          void* cache, int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                          int64_t cache_stride_row, int32_t page, const int32_t* block_table,
+                          int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
+                          int32_t num_reqs, int64_t* slot_out, void* stream) {
+  if (head_dim != 128 || (width != 256 && width != 512 && width != 1024)) {
+    set_error("latent query needs head_dim 128 and width 256, 512 or 1024 (got %d, %d)", head_dim, width);
     return kStatusInvalid;
   }
-  if (max_position < 1 || table_stride < width) {
-    set_error("latent query needs a [max_position, width] RoPE table");
+  if (max_position < 1 || table_stride < width || !aligned(q_pre, 16) || (q_stride_t % 8) || (q_stride_h % 8) ||
+      !aligned(A, 16) || (a_stride_h % 8) || (a_stride_k % 8)) {
+    set_error("latent query needs a [max_position, width] table and 16-byte aligned q rows / A rows");
     return kStatusInvalid;
   }
-  return latent_query(q_pre, q_stride_t, q_stride_h, A, a_stride_h, a_stride_k, positions, table, table_stride,
-                      max_position, out, out_stride_t, out_stride_h, num_tokens, num_heads, width,
-                      static_cast<cudaStream_t>(stream));
+  if (k && (page < 1 || num_reqs < 1 || cos_sin_rows < 1 || cos_sin_stride < 128 || (cos_sin_stride % 4) || !q_rope ||
+            !aligned(cos_sin, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(q_rope, 16) || !aligned(cache, 16) ||
+            (k_stride_t % 8) || (k_stride_h % 8) || (v_stride_t % 8) || (v_stride_h % 8) || (q_rope_stride_t % 8) ||
+            (q_rope_stride_h % 8) || (cache_stride_block % 8) || (cache_stride_head % 8) || (cache_stride_row % 8))) {
+    set_error("exact part needs page >= 1, >= 1 request, a 16-byte aligned [max_position, 128] cos|sin table, a q_rope "
+              "buffer and 16-byte aligned rows of k, v, q_rope and the exact cache");
+    return kStatusInvalid;
+  }
+  PrepareParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q_pre);
+  p.q_st = q_stride_t;
+  p.q_sh = q_stride_h;
+  p.A = static_cast<const __nv_bfloat16*>(A);
+  p.a_sh = a_stride_h;
+  p.a_sk = a_stride_k;
+  p.positions = positions;
+  p.table = static_cast<const __nv_bfloat16*>(table);
+  p.tab_st = table_stride;
+  p.max_pos = max_position;
+  p.q_lat = static_cast<__nv_bfloat16*>(q_lat);
+  p.ql_st = q_lat_stride_t;
+  p.ql_sh = q_lat_stride_h;
+  p.T = num_tokens;
+  p.H = num_heads;
+  p.W = width;
+  p.q_rope = static_cast<__nv_bfloat16*>(q_rope);
+  p.qr_st = q_rope_stride_t;
+  p.qr_sh = q_rope_stride_h;
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.k_st = k_stride_t;
+  p.k_sh = k_stride_h;
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.v_st = v_stride_t;
+  p.v_sh = v_stride_h;
+  p.cos_sin = cos_sin;
+  p.cs_st = cos_sin_stride;
+  p.cs_max = cos_sin_rows;
+  p.cache = static_cast<__nv_bfloat16*>(cache);
+  p.c_sb = cache_stride_block;
+  p.c_sh = cache_stride_head;
+  p.c_sr = cache_stride_row;
+  p.num_blocks = num_blocks;
+  p.page = page;
+  p.bt = block_table;
+  p.bt_st = block_table_stride;
+  p.max_blocks = max_blocks;
+  p.qsl = query_start_loc;
+  p.R = num_reqs;
+  p.slot_out = slot_out;
+  return prepare(p, static_cast<cudaStream_t>(stream));
 }
 
 int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
@@ -169,17 +235,86 @@ int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const v
   return exact_append(a, num_tokens, static_cast<cudaStream_t>(stream));
 }
 
+static int writer_checks(const void* h, int64_t h_st, const void* E, int64_t e_st, const void* reg_in,
+                         int64_t ri_st, const void* reg_out, int64_t ro_st, int32_t N, int32_t K) {
+  if (K % 128 || N % 16 || !aligned(h, 16) || (h_st % 8) || !aligned(E, 16) || (e_st % 8) ||
+      (reg_in && ((ri_st % 2) || !aligned(reg_in, 4))) || (reg_out && ((ro_st % 2) || !aligned(reg_out, 4)))) {
+    set_error("writer needs in_features % 128 == 0, out_features % 16 == 0, 16-byte aligned h / weight rows "
+              "and even register strides");
+    return kStatusInvalid;
+  }
+  return kStatusOk;
+}
+
 int hla_s6_writer_project(const void* h, int64_t h_stride_t, const void* weight, int64_t weight_stride_n,
                           const void* reg_in, int64_t reg_in_stride_t, void* reg_out, int64_t reg_out_stride_t,
                           int32_t num_tokens, int32_t out_features, int32_t in_features, void* stream) {
-  if (in_features % 16 || out_features % 2 || (h_stride_t % 2) || (weight_stride_n % 2) || !aligned(h, 4) ||
-      !aligned(weight, 4) || (reg_in && ((reg_in_stride_t % 2) || !aligned(reg_in, 4))) || (reg_out_stride_t % 2) ||
-      !aligned(reg_out, 4)) {
-    set_error("writer projection needs in_features % 16 == 0, even out_features and even row strides");
+  int rc = writer_checks(h, h_stride_t, weight, weight_stride_n, reg_in, reg_in_stride_t, reg_out,
+                         reg_out_stride_t, out_features, in_features);
+  if (rc) return rc;
+  if (!reg_out) {
+    set_error("writer projection needs an output register");
     return kStatusInvalid;
   }
-  return writer_project(h, h_stride_t, weight, weight_stride_n, reg_in, reg_in_stride_t, reg_out, reg_out_stride_t,
-                        num_tokens, out_features, in_features, static_cast<cudaStream_t>(stream));
+  WriterParams p{};
+  p.h = static_cast<const __nv_bfloat16*>(h);
+  p.h_st = h_stride_t;
+  p.E = static_cast<const __nv_bfloat16*>(weight);
+  p.e_st = weight_stride_n;
+  p.reg_in = static_cast<const __nv_bfloat16*>(reg_in);
+  p.ri_st = reg_in_stride_t;
+  p.reg_out = static_cast<__nv_bfloat16*>(reg_out);
+  p.ro_st = reg_out_stride_t;
+  p.T = num_tokens;
+  p.N = out_features;
+  p.K = in_features;
+  return writer(p, static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_writer_commit(const void* h, int64_t h_stride_t, const void* weight, int64_t weight_stride_n,
+                         const void* reg_in, int64_t reg_in_stride_t, void* reg_out, int64_t reg_out_stride_t,
+                         int32_t num_tokens, int32_t out_features, int32_t in_features, const int64_t* positions,
+                         const void* table, int64_t table_stride, int64_t max_position, void* cache,
+                         int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row, int32_t page,
+                         const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                         const int32_t* query_start_loc, int32_t num_reqs, void* stream) {
+  int rc = writer_checks(h, h_stride_t, weight, weight_stride_n, reg_in, reg_in_stride_t, reg_out,
+                         reg_out_stride_t, out_features, in_features);
+  if (rc) return rc;
+  const int w = out_features / 2;
+  if (w % 16 || page < 1 || num_reqs < 1 || max_position < 1 || table_stride < w) {
+    set_error("writer commit needs width % 16 == 0, page >= 1, >= 1 request and a [max_position, width] table");
+    return kStatusInvalid;
+  }
+  WriterParams p{};
+  p.h = static_cast<const __nv_bfloat16*>(h);
+  p.h_st = h_stride_t;
+  p.E = static_cast<const __nv_bfloat16*>(weight);
+  p.e_st = weight_stride_n;
+  p.reg_in = static_cast<const __nv_bfloat16*>(reg_in);
+  p.ri_st = reg_in_stride_t;
+  p.reg_out = static_cast<__nv_bfloat16*>(reg_out);
+  p.ro_st = reg_out_stride_t;
+  p.T = num_tokens;
+  p.N = out_features;
+  p.K = in_features;
+  p.commit = 1;
+  p.w = w;
+  p.positions = positions;
+  p.table = static_cast<const __nv_bfloat16*>(table);
+  p.tab_st = table_stride;
+  p.max_pos = max_position;
+  p.cache = static_cast<__nv_bfloat16*>(cache);
+  p.c_sb = cache_stride_block;
+  p.c_sr = cache_stride_row;
+  p.num_blocks = num_blocks;
+  p.page = page;
+  p.bt = block_table;
+  p.bt_st = block_table_stride;
+  p.max_blocks = max_blocks;
+  p.qsl = query_start_loc;
+  p.R = num_reqs;
+  return writer(p, static_cast<cudaStream_t>(stream));
 }
 
 int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, const int64_t* positions,
@@ -222,7 +357,7 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
                           const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
                           float scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse_out,
-                          void* stream) {
+                          int32_t flags, void* stream) {
   CombineParams p;
   p.win = make_window(q_rope, q_stride_t, q_stride_h, exact_cache, exact_num_blocks, exact_stride_block,
                       exact_stride_head, exact_stride_row, exact_page, block_table, block_table_stride, max_blocks,
@@ -269,7 +404,8 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
   p.o_st = out_stride_t;
   p.o_sh = out_stride_h;
   p.lse_out = lse_out;
-  return decode_combine(p, width, static_cast<cudaStream_t>(stream));
+  const bool pdl = (flags & HLA_S6_COMBINE_AFTER_PARTIALS) && !z_in;
+  return decode_combine(p, width, pdl, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

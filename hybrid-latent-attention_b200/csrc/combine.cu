@@ -1,14 +1,15 @@
 // Fused decode combine for one (layer, loop) of the S6 decode step: the tail of
 // s6_layer.attend's decode branch (s6_layer.py:97-115) in one launch:
-//   1. reduce the history kernel's split partials -> z[t, h, :] (bf16 values, as the
+//   1. reduce the history kernel's split partials -> z[t, h, :] (rounded to bf16, as the
 //      reference's history output o_hist is bf16) and lse_hist      (vLLM stage 2, s6_ops.py:158)
 //   2. exact window over keys [pos - W, pos] of this loop's exact cache  (window_attention_fa, :317)
-//   3. up-projection o_hist = z . B[h]  (bf16 result)                     (einsum, s6_layer.py:114)
+//   3. up-projection o_hist = z . B[h] (bf16 result)                      (einsum, s6_layer.py:114)
 //   4. LSE merge, invalid (padding) tokens zeroed                        (merge_states, s6_ops.py:262)
-// CTA = (4 tokens, 1 head), 4 warps: warp w owns token t0 + w in steps 1-2; thread d owns output
-// column d in steps 3-4.  Instead of split partials the kernel can take an already reduced
-// (z fp32 [T,H,W], lse [H,T]) pair, which is how a sequence-split history arrives after its
-// cross-GPU exchange.
+// CTA = (8 tokens, head h), 8 warps, one token per warp.  All of B[h] ([W, 128] bf16) is put in
+// flight with cp.async before steps 1-2, so its latency hides behind them; step 3 is mma.m16n8k16 with the 8
+// tokens as M (rows 8-15 zero; z from shared memory, B via ldmatrix.trans).  Instead of split partials the kernel
+// can take an already reduced (z fp32 [T,H,W], lse [H,T]) pair - how a sequence-split history
+// arrives after its cross-GPU exchange.
 #include "combine.cuh"
 #include "common.cuh"
 #include "decode_ops.cuh"
@@ -16,24 +17,65 @@
 
 namespace hla {
 
-template <int W>
-__global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams p) {
-  constexpr int TT = 4, D = 128;
-  __shared__ float z_s[TT][W];
-  __shared__ float q_s[TT][D];
-  __shared__ float ow_s[TT][D];
-  __shared__ float lh_s[TT], lw_s[TT];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * TT, h = blockIdx.y, T = p.T, H = p.H;
+constexpr int kCTok = 8;       // tokens per CTA (one per warp; the mma M of 16 is zero-padded)
+constexpr int kCKC = 64;       // k rows of B per chunk
+constexpr int kCChunkBytes = kCKC * 128 * 2;   // 16 KB
 
-  // ---- 1. history: reduce partials (or take the pre-reduced pair)
+template <int W>
+struct CombineSmem {
+  static constexpr int Z_BYTES = 16 * W * 2;
+  static constexpr int B_OFF = 0;                                // all of B[h]: W/64 chunks
+  static constexpr int Z_OFF = (W / kCKC) * kCChunkBytes;
+  static constexpr int OW_OFF = Z_OFF + Z_BYTES;                 // float [16][128] window outputs
+  static constexpr int Q_OFF = OW_OFF + kCTok * 128 * 4;          // float [8 warps][128]
+  static constexpr int L_OFF = Q_OFF + 8 * 128 * 4;               // float lse_h[16], lse_w[16]
+  static constexpr int QSL_OFF = L_OFF + 2 * kCTok * 4;         // int32 query_start_loc copy
+  static constexpr int BYTES = QSL_OFF + kQslCap * 4;
+};
+
+template <int W>
+__global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams p) {
+  using S = CombineSmem<W>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* ow_s = reinterpret_cast<float*>(smem + S::OW_OFF);
+  float* q_s = reinterpret_cast<float*>(smem + S::Q_OFF);
+  float* lh_s = reinterpret_cast<float*>(smem + S::L_OFF);
+  float* lw_s = lh_s + kCTok;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x, t0 = blockIdx.y * kCTok, T = p.T, H = p.H;
+  constexpr int NK = W / kCKC;
+
+  // ---- all of B[h] in flight now; it lands while steps 1-2 run
+  const __nv_bfloat16* Bh = p.B + static_cast<int64_t>(h) * p.b_sh;
+  for (int kc = 0; kc < NK; ++kc) {
+    uint8_t* dst = smem + S::B_OFF + kc * kCChunkBytes;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {  // 64 rows x 16 chunks = 1024 chunks
+      const int idx = tid + it * 256, row = idx >> 4, ch = idx & 15;
+      cp_async16(dst + swz(row, ch, 256), Bh + static_cast<int64_t>(kc * kCKC + row) * p.b_sk + ch * 8);
+    }
+  }
+  cp_async_commit();
+  WindowArgs win = p.win;
+  win.qsl = stage_qsl(p.win.qsl, p.win.R, reinterpret_cast<int32_t*>(smem + S::QSL_OFF));
+
+  // ---- 1 + 2: warp w owns token t0 + w: exact window first (its inputs precede the history
+  //      kernel), then - after the history grid has completed - the history reduce
   {
-    const int t = t0 + warp;
-    float lse_h = -INFINITY;
+    const int tt = warp, t = t0 + tt;
+    float o[4], lse_w;
+    if (t < T) {
+      window_warp(win, t, h, q_s + warp * 128, o, lse_w);
+    } else {
+      o[0] = o[1] = o[2] = o[3] = 0.f;
+      lse_w = -INFINITY;
+    }
+    griddep_wait();
     constexpr int NV = W / 128;  // float4 per lane
     float4 acc[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lse_h = -INFINITY;
     if (t < T && !(p.empty && p.empty[t])) {
       if (p.z_in) {
         lse_h = p.lse_in[static_cast<int64_t>(h) * T + t];
@@ -49,18 +91,30 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams
           lo = m.x;
           hi = m.y;
         }
+        // up to 4 partial slots per pass, all loads of a pass issued together
         float mx = -INFINITY;
         for (int s = lo; s < hi; ++s) mx = fmaxf(mx, p.ws_lse[static_cast<int64_t>(s) * H + h]);
         if (mx != -INFINITY) {
           float wsum = 0.f;
-          for (int s = lo; s < hi; ++s) {
-            const float wgt = expf(p.ws_lse[static_cast<int64_t>(s) * H + h] - mx);
-            wsum += wgt;
-            const float4* src = reinterpret_cast<const float4*>(p.ws_o + (static_cast<int64_t>(s) * H + h) * W);
+          for (int s0 = lo; s0 < hi; s0 += 4) {
+            float wgt[4];
+            float4 v[4][NV];
 #pragma unroll
-            for (int i = 0; i < NV; ++i) {
-              const float4 v = src[i * 32 + lane];
-              acc[i].x += wgt * v.x; acc[i].y += wgt * v.y; acc[i].z += wgt * v.z; acc[i].w += wgt * v.w;
+            for (int u = 0; u < 4; ++u) {
+              const int s = s0 + u;
+              wgt[u] = s < hi ? expf(p.ws_lse[static_cast<int64_t>(s) * H + h] - mx) : 0.f;
+              const float4* src = reinterpret_cast<const float4*>(p.ws_o + (static_cast<int64_t>(s < hi ? s : lo) * H + h) * W);
+#pragma unroll
+              for (int i = 0; i < NV; ++i) v[u][i] = s < hi ? src[i * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              wsum += wgt[u];
+#pragma unroll
+              for (int i = 0; i < NV; ++i) {
+                acc[i].x += wgt[u] * v[u][i].x; acc[i].y += wgt[u] * v[u][i].y;
+                acc[i].z += wgt[u] * v[u][i].z; acc[i].w += wgt[u] * v[u][i].w;
+              }
             }
           }
           const float inv = 1.f / wsum;
@@ -77,66 +131,89 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const CombineParams
       for (int i = 0; i < NV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
+    for (int i = 0; i < NV; ++i) {  // z row tt: dims 4(32i + lane) .. +3 as bf16 into the swizzled tile
       const int d = (i * 32 + lane) * 4;
-      z_s[warp][d + 0] = bf16_round(acc[i].x);
-      z_s[warp][d + 1] = bf16_round(acc[i].y);
-      z_s[warp][d + 2] = bf16_round(acc[i].z);
-      z_s[warp][d + 3] = bf16_round(acc[i].w);
-    }
-    if (lane == 0) lh_s[warp] = lse_h;
-
-    // ---- 2. exact window of this token (o rounded to bf16 as the FA output is)
-    float o[4], lse_w;
-    if (t < T) {
-      window_warp(p.win, t, h, q_s[warp], o, lse_w);
-    } else {
-      o[0] = o[1] = o[2] = o[3] = 0.f;
-      lse_w = -INFINITY;
+      uint2 pk;
+      pk.x = pack_bf16(acc[i].x, acc[i].y);
+      pk.y = pack_bf16(acc[i].z, acc[i].w);
+      *reinterpret_cast<uint2*>(smem + S::Z_OFF + swz(tt, d >> 3, W * 2) + (d & 7) * 2) = pk;
+      *reinterpret_cast<uint2*>(smem + S::Z_OFF + swz(tt + 8, d >> 3, W * 2) + (d & 7) * 2) = make_uint2(0u, 0u);
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ow_s[warp][lane * 4 + e] = bf16_round(o[e]);
-    if (lane == 0) lw_s[warp] = lse_w;
+    for (int e = 0; e < 4; ++e) ow_s[tt * 128 + lane * 4 + e] = bf16_round(o[e]);
+    if (lane == 0) {
+      lh_s[tt] = lse_h;
+      lw_s[tt] = lse_w;
+    }
   }
+
+  // ---- 3: o_hist[16 x 128] = z[16 x W] . B[h][W x 128]; warp w owns columns 16w .. 16w+15
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const uint32_t zb = smem_u32(smem + S::Z_OFF);
+  cp_async_wait<0>();
   __syncthreads();
-
-  // ---- 3. up-projection: thread d, four tokens
-  const int d = threadIdx.x;
-  float acc[TT] = {0.f, 0.f, 0.f, 0.f};
-  const __nv_bfloat16* Bh = p.B + static_cast<int64_t>(h) * p.b_sh + d;
-#pragma unroll 8
-  for (int k = 0; k < W; ++k) {
-    const float b = __bfloat162float(Bh[static_cast<int64_t>(k) * p.b_sk]);
+  for (int kc = 0; kc < NK; ++kc) {
+    const uint32_t bb = smem_u32(smem + S::B_OFF + kc * kCChunkBytes);
 #pragma unroll
-    for (int tt = 0; tt < TT; ++tt) acc[tt] = fmaf(z_s[tt][k], b, acc[tt]);
+    for (int ks = 0; ks < kCKC / 16; ++ks) {
+      uint32_t a[4], b0, b1, b2, b3;
+      const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4(zb + swz(arow, (kc * kCKC + ks * 16) / 8 + (lane >> 4), W * 2), a[0], a[1], a[2], a[3]);
+      const int krow = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4_t(bb + swz(krow, 2 * warp + (lane >> 4), 256), b0, b1, b2, b3);
+      mma_bf16_16816(acc[0], a, b0, b1);
+      mma_bf16_16816(acc[1], a, b2, b3);
+    }
   }
 
-  // ---- 4. merge
-#pragma unroll
-  for (int tt = 0; tt < TT; ++tt) {
-    const int t = t0 + tt;
-    if (t >= T) break;
-    const bool invalid = t >= p.win.qsl[p.win.R];
+  // ---- 4: merge (row g of the mma tile = token t0 + g; columns 16w + 8nt + 2c, +1)
+  const int g = lane >> 2, c = lane & 3;
+  {
+    const int half = 0;
+    const int tt = g, t = t0 + tt;
+    if (t >= T) return;
+    const bool invalid = t >= win.qsl[win.R];
     float w1, w2;
     merge_weights_states(lh_s[tt], lw_s[tt], w1, w2);
-    const float r = invalid ? 0.f : bf16_round(acc[tt]) * w1 + ow_s[tt][d] * w2;
-    p.out[static_cast<int64_t>(t) * p.o_st + static_cast<int64_t>(h) * p.o_sh + d] = __float2bfloat16_rn(r);
-    if (d == 0 && p.lse_out) {
-      float l1 = lh_s[tt], l2 = lw_s[tt];
-      p.lse_out[static_cast<int64_t>(h) * T + t] = invalid ? -INFINITY : merged_lse(l1, l2);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int col = 16 * warp + 8 * nt + 2 * c;
+      float r0 = bf16_round(acc[nt][2 * half]) * w1 + ow_s[tt * 128 + col] * w2;
+      float r1 = bf16_round(acc[nt][2 * half + 1]) * w1 + ow_s[tt * 128 + col + 1] * w2;
+      if (invalid) r0 = r1 = 0.f;
+      *reinterpret_cast<__nv_bfloat162*>(p.out + static_cast<int64_t>(t) * p.o_st + static_cast<int64_t>(h) * p.o_sh +
+                                         col) = __floats2bfloat162_rn(r0, r1);
     }
+    if (warp == 0 && c == 0 && p.lse_out)
+      p.lse_out[static_cast<int64_t>(h) * T + t] = invalid ? -INFINITY : merged_lse(lh_s[tt], lw_s[tt]);
   }
 }
 
-int decode_combine(const CombineParams& p, int W, cudaStream_t s) {
+template <int W>
+static int launch_combine(const CombineParams& p, bool pdl, cudaStream_t s) {
+  static unsigned attr_mask = 0;
+  const int smem = CombineSmem<W>::BYTES;
+  ensure_smem_limit(decode_combine_kernel<W>, smem, attr_mask);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.H, (p.T + kCTok - 1) / kCTok);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_combine_kernel<W>, p), "decode_combine_kernel launch");
+}
+
+int decode_combine(const CombineParams& p, int W, bool pdl, cudaStream_t s) {
   if (p.T == 0) return kStatusOk;
-  dim3 grid((p.T + 3) / 4, p.H);
   switch (W) {
-    case 256: decode_combine_kernel<256><<<grid, 128, 0, s>>>(p); break;
-    case 512: decode_combine_kernel<512><<<grid, 128, 0, s>>>(p); break;
+    case 256: return launch_combine<256>(p, pdl, s);
+    case 512: return launch_combine<512>(p, pdl, s);
     default: set_error("decode combine width %d unsupported (256 or 512)", W); return kStatusInvalid;
   }
-  return cuda_status(cudaGetLastError(), "decode_combine_kernel launch");
 }
 
 }  // namespace hla

@@ -23,6 +23,8 @@ struct CombineParams {
   float* lse_out;  // optional [H, T] merged lse
 };
 
-int decode_combine(const CombineParams& p, int W, cudaStream_t s);
+// pdl: launch as a programmatic dependent of the immediately preceding launch on `s`, which must
+// be the history split kernel that produced the partials (the window part then overlaps its tail).
+int decode_combine(const CombineParams& p, int W, bool pdl, cudaStream_t s);
 
 }  // namespace hla

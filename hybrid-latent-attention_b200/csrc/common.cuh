@@ -99,6 +99,35 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// ---------------------------------------------------------------- cp.async (16-byte, L2-cached)
+// src_bytes < 16 zero-fills the rest of the 16-byte destination (0 = pure zero fill, no read).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes = 16) {
+  asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a shared tile whose rows are `row_bytes`
+// long (a multiple of 128): chunks are XOR-swizzled by row % 8 so that ldmatrix over 8 rows of
+// the same logical chunk touches 8 distinct bank groups.
+__device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
+  return static_cast<uint32_t>(row * row_bytes + ((chunk ^ (row & 7)) << 4));
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// wait: block until the preceding grid (launched before this one with programmatic stream
+// serialization) has completed and its memory is visible; a no-op for ordinary launches.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// launch_dependents: this CTA no longer holds back the launch of the dependent grid.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- named barriers
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -1,10 +1,10 @@
 // The per-(layer, loop) S6 decode ops around the history reader:
 //   A5  exact window (window_attention_fa)          s6_ops.py:317-331
 //   A7  LSE merges (merge_states / merge_lse)       s6_ops.py:262-284, 353-361
-//   A4  latent RoPE, latent query absorb            s6_ops.py:23-41, s6_layer.py:32-40
+//   A4  latent RoPE (in place)                      s6_ops.py:23-41
 //   A10 exact-cache append with exact RoPE          ouro_latent.py:113-123
-//   A9  writer projection (+ bf16 register add)     register.py:45-61, s6_layer.py:124-132
 //   A9+A10 committed row: latent RoPE + paged scatter  s6_layer.py:135-147, ouro_latent.py:127-129
+// (the writer projection and the latent query GEMMs live in gemm_ops.cu)
 //
 // Latent RoPE everywhere follows the torch bf16 operation order of LatentLayer.pack
 // (register.py:73-79): bf16(x*c), bf16(rotate_half(x)*s), bf16(sum), so committed cache rows
@@ -20,11 +20,14 @@ __global__ void __launch_bounds__(128) window_kernel(const WindowArgs a, __nv_bf
                                                      int64_t o_st, int64_t o_sh, float* __restrict__ lse_out, int T,
                                                      int H) {
   __shared__ float q_s[4][128];
+  __shared__ int32_t qsl_s[kQslCap];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x, h = blockIdx.y * 4 + warp;
+  WindowArgs w = a;
+  w.qsl = stage_qsl(a.qsl, a.R, qsl_s);
   if (h >= H) return;
   float o[4], lse;
-  window_warp(a, t, h, q_s[warp], o, lse);
+  window_warp(w, t, h, q_s[warp], o, lse);
   __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + lane * 4;
   reinterpret_cast<__nv_bfloat162*>(dst)[0] = __floats2bfloat162_rn(o[0], o[1]);
   reinterpret_cast<__nv_bfloat162*>(dst)[1] = __floats2bfloat162_rn(o[2], o[3]);
@@ -105,72 +108,6 @@ int latent_rope(void* x, int64_t st, int64_t sh, int T, int H, int w, const int6
   return cuda_status(cudaGetLastError(), "latent_rope_kernel launch");
 }
 
-// -------------------------------------------------------------------- A4 latent query
-// q_lat[t, h, :] = RoPE_lat(bf16(q_pre[t, h, :] . A[h])).  CTA = (8 tokens, head h); thread j owns
-// latent columns j and j + W/2 (one neox RoPE pair).
-template <int W>
-__global__ void __launch_bounds__(W / 2) latent_query_kernel(const __nv_bfloat16* __restrict__ q, int64_t q_st,
-                                                              int64_t q_sh, const __nv_bfloat16* __restrict__ A,
-                                                              int64_t a_sh, int64_t a_sk,
-                                                              const int64_t* __restrict__ positions,
-                                                              const __nv_bfloat16* __restrict__ table, int64_t tab_st,
-                                                              int64_t max_pos, __nv_bfloat16* __restrict__ out,
-                                                              int64_t o_st, int64_t o_sh, int T) {
-  constexpr int TT = 8, D = 128, HALF = W / 2;
-  __shared__ float q_s[TT][D];
-  const int t0 = blockIdx.x * TT, h = blockIdx.y, j = threadIdx.x;
-  for (int idx = j; idx < TT * D; idx += blockDim.x) {
-    const int tt = idx / D, k = idx - tt * D;
-    q_s[tt][k] = (t0 + tt < T) ? __bfloat162float(q[static_cast<int64_t>(t0 + tt) * q_st + static_cast<int64_t>(h) * q_sh + k]) : 0.f;
-  }
-  __syncthreads();
-  float acc0[TT], acc1[TT];
-#pragma unroll
-  for (int tt = 0; tt < TT; ++tt) acc0[tt] = acc1[tt] = 0.f;
-  const __nv_bfloat16* Ah = A + static_cast<int64_t>(h) * a_sh;
-#pragma unroll 4
-  for (int k = 0; k < D; ++k) {
-    const float a0 = __bfloat162float(Ah[static_cast<int64_t>(k) * a_sk + j]);
-    const float a1 = __bfloat162float(Ah[static_cast<int64_t>(k) * a_sk + j + HALF]);
-#pragma unroll
-    for (int tt = 0; tt < TT; ++tt) {
-      acc0[tt] = fmaf(q_s[tt][k], a0, acc0[tt]);
-      acc1[tt] = fmaf(q_s[tt][k], a1, acc1[tt]);
-    }
-  }
-#pragma unroll
-  for (int tt = 0; tt < TT; ++tt) {
-    const int t = t0 + tt;
-    if (t >= T) break;
-    const int64_t pos = clamp_pos(positions[t], max_pos);
-    const __nv_bfloat16* row = table + pos * tab_st;
-    float a, b;
-    rope_pair_torch(bf16_round(acc0[tt]), bf16_round(acc1[tt]), __bfloat162float(row[j]),
-                    __bfloat162float(row[HALF + j]), a, b);
-    __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh;
-    dst[j] = __float2bfloat16_rn(a);
-    dst[j + HALF] = __float2bfloat16_rn(b);
-  }
-}
-
-int latent_query(const void* q, int64_t q_st, int64_t q_sh, const void* A, int64_t a_sh, int64_t a_sk,
-                 const int64_t* positions, const void* table, int64_t tab_st, int64_t max_pos, void* out,
-                 int64_t o_st, int64_t o_sh, int T, int H, int W, cudaStream_t s) {
-  if (T == 0) return kStatusOk;
-  dim3 grid((T + 7) / 8, H);
-  auto qq = static_cast<const __nv_bfloat16*>(q);
-  auto aa = static_cast<const __nv_bfloat16*>(A);
-  auto tb = static_cast<const __nv_bfloat16*>(table);
-  auto oo = static_cast<__nv_bfloat16*>(out);
-  switch (W) {
-    case 256: latent_query_kernel<256><<<grid, 128, 0, s>>>(qq, q_st, q_sh, aa, a_sh, a_sk, positions, tb, tab_st, max_pos, oo, o_st, o_sh, T); break;
-    case 512: latent_query_kernel<512><<<grid, 256, 0, s>>>(qq, q_st, q_sh, aa, a_sh, a_sk, positions, tb, tab_st, max_pos, oo, o_st, o_sh, T); break;
-    case 1024: latent_query_kernel<1024><<<grid, 512, 0, s>>>(qq, q_st, q_sh, aa, a_sh, a_sk, positions, tb, tab_st, max_pos, oo, o_st, o_sh, T); break;
-    default: set_error("latent query width %d unsupported (256, 512, 1024)", W); return kStatusInvalid;
-  }
-  return cuda_status(cudaGetLastError(), "latent_query_kernel launch");
-}
-
 // -------------------------------------------------------------------- A10 exact append
 // Exact neox RoPE (fp32 math, one rounding, as vLLM's rotary_embedding) of q (in place) and k,
 // then k_rope | v into the exact cache at slot = block_table[req, pos // page] * page + pos % page.
@@ -224,68 +161,6 @@ int exact_append(const ExactArgs& a, int T, cudaStream_t s) {
   if (T == 0) return kStatusOk;
   exact_append_kernel<<<T, 256, 0, s>>>(a);
   return cuda_status(cudaGetLastError(), "exact_append_kernel launch");
-}
-
-// -------------------------------------------------------------------- A9 writer projection
-// reg_out[t, n] = bf16(reg_in[t, n] + bf16(sum_k h[t, k] E[n, k]))   (reg_in may be NULL)
-// mma.m16n8k16: CTA = 4 warps x 16 tokens, 32 output columns; operands straight from L2.
-__global__ void __launch_bounds__(128) writer_kernel(const __nv_bfloat16* __restrict__ h, int64_t h_st,
-                                                     const __nv_bfloat16* __restrict__ E, int64_t e_st,
-                                                     const __nv_bfloat16* __restrict__ reg_in, int64_t ri_st,
-                                                     __nv_bfloat16* __restrict__ reg_out, int64_t ro_st, int T, int N,
-                                                     int K) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int t0 = blockIdx.y * 64 + warp * 16, n0 = blockIdx.x * 32;
-  if (t0 >= T) return;
-  float acc[4][4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  const bool r0 = t0 + g < T, r1 = t0 + g + 8 < T;
-  const __nv_bfloat16* h0 = h + static_cast<int64_t>(min(t0 + g, T - 1)) * h_st;
-  const __nv_bfloat16* h1 = h + static_cast<int64_t>(min(t0 + g + 8, T - 1)) * h_st;
-#pragma unroll 4
-  for (int k = 0; k < K; k += 16) {
-    uint32_t a[4];
-    a[0] = r0 ? __ldg(reinterpret_cast<const uint32_t*>(h0 + k + 2 * c)) : 0u;
-    a[1] = r1 ? __ldg(reinterpret_cast<const uint32_t*>(h1 + k + 2 * c)) : 0u;
-    a[2] = r0 ? __ldg(reinterpret_cast<const uint32_t*>(h0 + k + 8 + 2 * c)) : 0u;
-    a[3] = r1 ? __ldg(reinterpret_cast<const uint32_t*>(h1 + k + 8 + 2 * c)) : 0u;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + j * 8 + g;
-      const __nv_bfloat16* e = E + static_cast<int64_t>(min(n, N - 1)) * e_st + k + 2 * c;
-      const uint32_t b0 = __ldg(reinterpret_cast<const uint32_t*>(e));
-      const uint32_t b1 = __ldg(reinterpret_cast<const uint32_t*>(e + 8));
-      mma_bf16_16816(acc[j], a, b0, b1);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int n = n0 + j * 8 + 2 * c;
-    if (n >= N) continue;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int t = t0 + g + half * 8;
-      if (t >= T) continue;
-      float u0 = bf16_round(acc[j][2 * half]), u1 = bf16_round(acc[j][2 * half + 1]);
-      if (reg_in) {
-        const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(reg_in + static_cast<int64_t>(t) * ri_st + n);
-        u0 = __bfloat162float(p.x) + u0;
-        u1 = __bfloat162float(p.y) + u1;
-      }
-      *reinterpret_cast<__nv_bfloat162*>(reg_out + static_cast<int64_t>(t) * ro_st + n) = __floats2bfloat162_rn(u0, u1);
-    }
-  }
-}
-
-int writer_project(const void* h, int64_t h_st, const void* E, int64_t e_st, const void* reg_in, int64_t ri_st,
-                   void* reg_out, int64_t ro_st, int T, int N, int K, cudaStream_t s) {
-  if (T == 0) return kStatusOk;
-  dim3 grid((N + 31) / 32, (T + 63) / 64);
-  writer_kernel<<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(h), h_st, static_cast<const __nv_bfloat16*>(E),
-                                     e_st, static_cast<const __nv_bfloat16*>(reg_in), ri_st,
-                                     static_cast<__nv_bfloat16*>(reg_out), ro_st, T, N, K);
-  return cuda_status(cudaGetLastError(), "writer_kernel launch");
 }
 
 // -------------------------------------------------------------------- A9 + A10 committed row

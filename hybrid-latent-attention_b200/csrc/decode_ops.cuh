@@ -20,6 +20,17 @@ __device__ __forceinline__ bool token_request(const int32_t* __restrict__ qsl, i
   return t < qsl[R];
 }
 
+// Copy query_start_loc [R + 1] into shared memory (all threads of the CTA must call this) so the
+// per-token binary searches run on shared memory; falls back to the global array when it does
+// not fit in `cap` entries.
+constexpr int kQslCap = 1024;
+__device__ __forceinline__ const int32_t* stage_qsl(const int32_t* __restrict__ qsl, int R, int32_t* buf) {
+  if (R + 1 > kQslCap) return qsl;
+  for (int i = threadIdx.x; i <= R; i += blockDim.x) buf[i] = qsl[i];
+  __syncthreads();
+  return buf;
+}
+
 // Neox rotate-half pair (x1 at i, x2 at i + w/2) in the torch bf16 operation order:
 // y1 = bf16(bf16(x1*c) + bf16(-x2*s)), y2 = bf16(bf16(x2*c) + bf16(x1*s)).
 __device__ __forceinline__ void rope_pair_torch(float x1, float x2, float c, float s, float& y1, float& y2) {
@@ -75,8 +86,10 @@ struct WindowArgs {
 
 // One warp computes the exact window attention of token t, head h over keys
 // [pos - window, pos] (pos = seq_len - query_len + index in chunk; for decode seq_len - 1),
-// the current token included.  Lane l owns dims 4l..4l+3 of the output.  Invalid tokens or
-// an empty key range give o = 0, lse = -inf.  q_s: 128 floats of this warp's shared memory.
+// the current token included.  Lane l scores keys l, l + 32, ... (its K row is read with 16
+// independent 16-byte loads), then owns output dims 4l..4l+3 and accumulates V in groups of 16
+// keys whose loads are issued together.  Invalid tokens or an empty key range give o = 0,
+// lse = -inf.  q_s: 128 floats of this warp's shared memory.
 __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, float* q_s, float (&o)[4],
                                             float& lse) {
   const int lane = threadIdx.x & 31;
@@ -91,12 +104,13 @@ __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, f
   const int n = static_cast<int>(pos - first + 1);
   {
     const __nv_bfloat16* qp = a.q + static_cast<int64_t>(t) * a.q_st + static_cast<int64_t>(h) * a.q_sh + lane * 4;
-    const __nv_bfloat162 p0 = reinterpret_cast<const __nv_bfloat162*>(qp)[0];
-    const __nv_bfloat162 p1 = reinterpret_cast<const __nv_bfloat162*>(qp)[1];
-    q_s[lane * 4 + 0] = __bfloat162float(p0.x);
-    q_s[lane * 4 + 1] = __bfloat162float(p0.y);
-    q_s[lane * 4 + 2] = __bfloat162float(p1.x);
-    q_s[lane * 4 + 3] = __bfloat162float(p1.y);
+    const uint2 u = *reinterpret_cast<const uint2*>(qp);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+    __syncwarp();
+    q_s[lane * 4 + 0] = __bfloat162float(b[0].x);
+    q_s[lane * 4 + 1] = __bfloat162float(b[0].y);
+    q_s[lane * 4 + 2] = __bfloat162float(b[1].x);
+    q_s[lane * 4 + 3] = __bfloat162float(b[1].y);
   }
   __syncwarp();
   constexpr int MAXC = 4;  // up to 128 keys (window <= 127)
@@ -107,30 +121,33 @@ __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, f
   for (int ch = 0; ch < MAXC; ++ch) {
     sc[ch] = -INFINITY;
     off[ch] = -1;
-    const int kb = ch * 32 + lane;
     if (ch * 32 >= n) continue;
+    const int kb = ch * 32 + lane;
     if (kb < n) {
       const int64_t j = first + kb;
       const int64_t col = j / a.page;
       if (col < a.max_blocks) {
         const int blk = a.bt[static_cast<int64_t>(r) * a.bt_st + col];
-        if (blk >= 0 && blk < a.num_blocks) {
+        if (blk >= 0 && blk < a.num_blocks)
           off[ch] = static_cast<int64_t>(blk) * a.c_sb + static_cast<int64_t>(h) * a.c_sh + (j % a.page) * a.c_sr;
-          const uint4* kp = reinterpret_cast<const uint4*>(a.cache + off[ch]);
-          float dot = 0.f;
+      }
+    }
+    if (off[ch] >= 0) {
+      const uint4* kp = reinterpret_cast<const uint4*>(a.cache + off[ch]);
+      uint4 kr[16];
 #pragma unroll
-          for (int v = 0; v < 16; ++v) {
-            const uint4 u = __ldg(kp + v);
-            const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+      for (int v = 0; v < 16; ++v) kr[v] = __ldg(kp + v);
+      float dot = 0.f;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              dot = fmaf(q_s[v * 8 + 2 * e], __bfloat162float(b[e].x), dot);
-              dot = fmaf(q_s[v * 8 + 2 * e + 1], __bfloat162float(b[e].y), dot);
-            }
-          }
-          sc[ch] = dot * a.scale;
+      for (int v = 0; v < 16; ++v) {
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&kr[v]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          dot = fmaf(q_s[v * 8 + 2 * e], __bfloat162float(b[e].x), dot);
+          dot = fmaf(q_s[v * 8 + 2 * e + 1], __bfloat162float(b[e].y), dot);
         }
       }
+      sc[ch] = dot * a.scale;
     }
     mx = fmaxf(mx, sc[ch]);
   }
@@ -146,17 +163,27 @@ __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, f
 #pragma unroll
   for (int ch = 0; ch < MAXC; ++ch) {
     if (ch * 32 >= n) break;
-    const int cnt = min(32, n - ch * 32);
-    for (int src = 0; src < cnt; ++src) {
-      const float p = __shfl_sync(0xffffffffu, sc[ch], src);
-      const int64_t ro = __shfl_sync(0xffffffffu, off[ch], src);
-      if (ro < 0) continue;
-      const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.cache + ro + 128 + lane * 4));
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
-      o[0] = fmaf(p, __bfloat162float(b[0].x), o[0]);
-      o[1] = fmaf(p, __bfloat162float(b[0].y), o[1]);
-      o[2] = fmaf(p, __bfloat162float(b[1].x), o[2]);
-      o[3] = fmaf(p, __bfloat162float(b[1].y), o[3]);
+#pragma unroll
+    for (int g0 = 0; g0 < 32; g0 += 16) {
+      if (ch * 32 + g0 >= n) break;
+      float pw[16];
+      uint2 vv[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        pw[e] = __shfl_sync(0xffffffffu, sc[ch], g0 + e);
+        const int64_t ro = __shfl_sync(0xffffffffu, off[ch], g0 + e);
+        const bool live = (ch * 32 + g0 + e < n) && ro >= 0;
+        vv[e] = live ? __ldg(reinterpret_cast<const uint2*>(a.cache + ro + 128 + lane * 4)) : make_uint2(0u, 0u);
+        if (!live) pw[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&vv[e]);
+        o[0] = fmaf(pw[e], __bfloat162float(b[0].x), o[0]);
+        o[1] = fmaf(pw[e], __bfloat162float(b[0].y), o[1]);
+        o[2] = fmaf(pw[e], __bfloat162float(b[1].x), o[2]);
+        o[3] = fmaf(pw[e], __bfloat162float(b[1].y), o[3]);
+      }
     }
   }
   const float inv = 1.f / l;
@@ -218,12 +245,7 @@ int merge(const void* o1, int64_t s1t, int64_t s1h, const float* lse1, const voi
           int D, int mode, cudaStream_t s);
 int latent_rope(void* x, int64_t st, int64_t sh, int T, int H, int w, const int64_t* positions, const void* table,
                 int64_t tab_st, int64_t max_pos, cudaStream_t s);
-int latent_query(const void* q, int64_t q_st, int64_t q_sh, const void* A, int64_t a_sh, int64_t a_sk,
-                 const int64_t* positions, const void* table, int64_t tab_st, int64_t max_pos, void* out,
-                 int64_t o_st, int64_t o_sh, int T, int H, int W, cudaStream_t s);
 int exact_append(const ExactArgs& a, int T, cudaStream_t s);
-int writer_project(const void* h, int64_t h_st, const void* E, int64_t e_st, const void* reg_in, int64_t ri_st,
-                   void* reg_out, int64_t ro_st, int T, int N, int K, cudaStream_t s);
 int commit_rows(const CommitArgs& a, int T, cudaStream_t s);
 
 }  // namespace hla

@@ -83,6 +83,9 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T;
+  // A dependent grid (the fused combine) may start on SMs this grid frees; it waits for this
+  // grid's completion before it reads the partials.
+  if (tid == 0) griddep_launch_dependents();
   int64_t P = 0, G = 1, p0 = 0, p1 = 0;
   int row0 = 0;
 
@@ -433,22 +436,26 @@ size_t history_smem_bytes(int T) {
          4 * (static_cast<size_t>(T) + 1);
 }
 
+// CTAs per SM of the split kernel at its largest shared-memory footprint (queried once per device).
 template <int W, int PG>
 static int occupancy_for() {
   using C = HistoryCfg<W, PG>;
-  static int cached = -1;
-  if (cached < 0) {
-    const size_t smem = history_smem_bytes<W, PG>(kHistoryMaxStreamRows);
-    cudaFuncSetAttribute(history_split_kernel<W, PG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
+  static unsigned attr_mask = 0;
+  static int cached[32] = {0};
+  const size_t smem = history_smem_bytes<W, PG>(kHistoryMaxStreamRows);
+  ensure_smem_limit(history_split_kernel<W, PG>, static_cast<int>(smem), attr_mask);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 31;
+  if (cached[dev] < 1) {
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, history_split_kernel<W, PG>, C::THREADS, smem) !=
             cudaSuccess ||
         n < 1)
-      n = 1;
-    cached = n;
+      return 1;  // no device here: do not cache the fallback
+    cached[dev] = n;
   }
-  return cached;
+  return cached[dev];
 }
 
 

@@ -19,6 +19,17 @@ enum Status : int {
 constexpr int kHistoryMaxStreamRows = 1024;
 
 void set_error(const char* fmt, ...);
+
+// Raise `func`'s dynamic shared-memory limit to `bytes`, once per device (bit `dev` of `mask`).
+template <typename F>
+inline void ensure_smem_limit(F func, int bytes, unsigned& mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(mask & (1u << dev))) {
+    cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    mask |= 1u << dev;
+  }
+}
 int cuda_status(cudaError_t e, const char* what);
 
 // 4-D TMA descriptor over a paged latent cache [num_blocks, 1, page, 2W] (unit last stride):

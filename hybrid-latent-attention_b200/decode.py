@@ -3,12 +3,13 @@
 Per step: for loop in 0..3, for layer in 0..23 (the hot loop of hla/vllm_latent/ouro_latent.py:270-274),
 one (layer, loop) of OuroLatentAttention.forward (ouro_latent.py:106-131) without the dense projections:
 
-  1. writer projection       s6_layer.write_rows       (register.py:45-61)
-  2. latent query            ctx.latent_query          (s6_layer.py:32-40, 82-84)
-  3. exact RoPE + append     rotary_emb + unified_kv_cache_update (ouro_latent.py:113-123)
-  4. history split           s6_ops.history_attention stage 1 (s6_ops.py:117-161)
-  5. fused combine           window_attention_fa + stage 2 + einsum B + merge_states (s6_layer.py:97-115)
-  6. committed row           s6_layer.committed_row + unified_kv_cache_update (ouro_latent.py:127-129)
+  1. writer (+ commit)       s6_layer.write_rows (register.py:45-61); at loops 0 and 3 the committed
+                             row (s6_layer.committed_row + unified_kv_cache_update, ouro_latent.py:127-129)
+                             is written by the same kernel's epilogue
+  2. prepare                 ctx.latent_query (s6_layer.py:32-40, 82-84) + rotary_emb and the exact
+                             unified_kv_cache_update (ouro_latent.py:113-123), one launch
+  3. history split           s6_ops.history_attention stage 1 (s6_ops.py:117-161)
+  4. fused combine           window_attention_fa + stage 2 + einsum B + merge_states (s6_layer.py:97-115)
 
 The inputs of a (layer, loop) - pre-RoPE q, k, v and the attention input h - come from a resident
 activation buffer (synthetic, seeded); its output goes to an output buffer.  Caches are paged with
@@ -125,8 +126,8 @@ class S6DecodeModel:
         self.acts = gen(s.layers, s.loops, B, 3 * D + s.hidden)          # q | k | v | h per (layer, loop)
         self.out = torch.zeros(s.layers, s.loops, B, s.heads, s.head_dim, dtype=BF16, device=self.device)
         self.q_lat = torch.empty(B, s.heads, s.rank, dtype=BF16, device=self.device)
+        self.q_rope = torch.empty(B, s.heads, s.head_dim, dtype=BF16, device=self.device)
         self.reg = [torch.empty(B, 2 * s.rank, dtype=BF16, device=self.device) for _ in range(s.layers)]
-        self.first = torch.empty(B, 2 * s.rank1, dtype=BF16, device=self.device)
         self.scale = s.head_dim ** -0.5
         self.graph = None
         self.history_graph = None
@@ -165,60 +166,78 @@ class S6DecodeModel:
                   self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.ctx_latent), B, s.heads,
                   width, s.page, float(self.scale), self.splits, _lib.ptr(self.ws), self.ws_floats, None, stream)
 
-    def layer_loop(self, layer, loop, stream):
+    def layer_loop(self, layer, loop, stream, wstream=None):
+        """The four launches of one (layer, loop); the writer goes to ``wstream`` when given (it reads only
+        ``h`` and feeds only the commit and the next loop's writer, so it overlaps the attention chain)."""
+        wstream = stream if wstream is None else wstream
         s, B = self.s, self.B
         lat = self.layers[layer]
         q, k, v, h = self._views(layer, loop)
         A, Bm, width = lat.readers(loop)
-        # 1. writer
-        E = lat.writer(loop)
-        dst = self.first if loop == 0 else self.reg[layer]
-        reg_in = None if loop <= 1 else self.reg[layer]
-        _lib.call('hla_s6_writer_project', _lib.ptr(h), h.stride(0), _lib.ptr(E), E.stride(0), _lib.ptr(reg_in),
-                  0 if reg_in is None else reg_in.stride(0), _lib.ptr(dst), dst.stride(0), B, E.shape[0], E.shape[1],
-                  stream)
-        # 2. latent query (pre-RoPE q)
-        q_lat = self.q_lat[..., :width] if width != s.rank else self.q_lat
         table = self.tables[width]
-        _lib.call('hla_s6_latent_query', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(A), A.stride(0), A.stride(1),
-                  _lib.ptr(self.positions), _lib.ptr(table), table.stride(0), table.shape[0], _lib.ptr(q_lat),
-                  q_lat.stride(0), q_lat.stride(1), B, s.heads, s.head_dim, width, stream)
-        # 3. exact RoPE of q (in place) and k, append k | v to this loop's exact cache
+        # 1. writer; at loop 0 (loop-1 latent) and the last loop (main latent) the row is committed in
+        #    the epilogue.  The committed row sits at position ctx, which no history read of this step
+        #    touches (they stop at ctx - W), so committing first equals the reference's commit-after-attend.
+        E = lat.writer(loop)
+        if loop == 0 or loop == s.loops - 1:
+            cache = self.l1[layer] if loop == 0 else self.main[layer]
+            reg_in = None if loop == 0 else self.reg[layer]
+            _lib.call('hla_s6_writer_commit', _lib.ptr(h), h.stride(0), _lib.ptr(E), E.stride(0), _lib.ptr(reg_in),
+                      0 if reg_in is None else reg_in.stride(0), None, 0, B, E.shape[0], E.shape[1],
+                      _lib.ptr(self.positions), _lib.ptr(table), table.stride(0), table.shape[0], _lib.ptr(cache),
+                      cache.shape[0], cache.stride(0), cache.stride(2), s.page, _lib.ptr(self.latent_table),
+                      self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.qsl), B, wstream)
+        else:
+            reg = self.reg[layer]
+            reg_in = None if loop == 1 else reg
+            _lib.call('hla_s6_writer_project', _lib.ptr(h), h.stride(0), _lib.ptr(E), E.stride(0), _lib.ptr(reg_in),
+                      0 if reg_in is None else reg_in.stride(0), _lib.ptr(reg), reg.stride(0), B, E.shape[0],
+                      E.shape[1], wstream)
+        # 2. latent query from the pre-RoPE q + exact RoPE (q -> q_rope, k) + exact-cache append
+        q_lat = self.q_lat[..., :width] if width != s.rank else self.q_lat
         ex = self.exact_logical[layer][loop]
-        _lib.call('hla_s6_exact_append', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(k), k.stride(0), k.stride(1),
-                  _lib.ptr(v), v.stride(0), v.stride(1), None, 0, 0, _lib.ptr(self.positions),
-                  _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(ex), ex.shape[0],
-                  ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
-                  self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, B, s.heads,
-                  s.head_dim, None, stream)
-        # 4. history split
+        qr = self.q_rope
+        _lib.call('hla_s6_decode_prepare', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(A), A.stride(0),
+                  A.stride(1), _lib.ptr(self.positions), _lib.ptr(table), table.stride(0), table.shape[0],
+                  _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), B, s.heads, s.head_dim, width, _lib.ptr(qr),
+                  qr.stride(0), qr.stride(1), _lib.ptr(k), k.stride(0), k.stride(1), _lib.ptr(v), v.stride(0),
+                  v.stride(1), _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(ex),
+                  ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
+                  self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, None, stream)
+        # 3. history split
         self._history(layer, loop, stream)
-        # 5. fused combine -> out
+        # 4. fused combine -> out
         out = self.out[layer, loop]
         _lib.call('hla_s6_decode_combine', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws), self.ws_floats,
-                  None, None, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(q), q.stride(0), q.stride(1),
+                  None, None, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
                   _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
                   _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
                   _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), _lib.ptr(out),
-                  out.stride(0), out.stride(1), None, stream)
-        # 6. committed rows: loop-1 latent after loop 0, main latent after the last loop
-        if loop == 0 or loop == s.loops - 1:
-            row = self.first if loop == 0 else self.reg[layer]
-            cache = self.l1[layer] if loop == 0 else self.main[layer]
-            _lib.call('hla_s6_commit_rows', _lib.ptr(row), row.stride(0), width, _lib.ptr(self.positions),
-                      _lib.ptr(table), table.stride(0), table.shape[0], _lib.ptr(cache), cache.shape[0],
-                      cache.stride(0), cache.stride(2), s.page, _lib.ptr(self.latent_table),
-                      self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.qsl), B, B, None, stream)
+                  out.stride(0), out.stride(1), None, _lib.COMBINE_AFTER_PARTIALS, stream)
 
     def launches_per_step(self):
         s = self.s
-        return s.layers * (s.loops * 5 + 2)
+        return s.layers * s.loops * 4
 
-    def step(self):
+    def step(self, overlap_writer=True):
+        """One decode step.  With ``overlap_writer`` the writer launches run on a side stream forked from
+        and joined back into the current stream (a parallel branch when captured in a graph)."""
+        main = torch.cuda.current_stream(self.device)
         stream = _lib.stream_of(self.out)
+        if not overlap_writer:
+            for loop in range(self.s.loops):
+                for layer in range(self.s.layers):
+                    self.layer_loop(layer, loop, stream)
+            return
+        if getattr(self, '_side', None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        side = self._side
+        side.wait_stream(main)
+        wstream = _lib.ctypes.c_void_p(side.cuda_stream)
         for loop in range(self.s.loops):
             for layer in range(self.s.layers):
-                self.layer_loop(layer, loop, stream)
+                self.layer_loop(layer, loop, stream, wstream)
+        main.wait_stream(side)
 
     def history_only(self):
         """The 96 history-split launches of a step alone (roofline timing of the dominant kernel)."""

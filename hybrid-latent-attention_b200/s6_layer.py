@@ -135,7 +135,8 @@ def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_sc
               _lib.ptr(empty), _lib.ptr(B), B.stride(0), B.stride(1), _lib.ptr(q_rope), q_rope.stride(0),
               q_rope.stride(1), _lib.ptr(exact), enb, esb, esh, esr, epage, _lib.ptr(exact_table),
               exact_table.stride(0), exact_table.shape[1], _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(seq_lens),
-              int(ctx.window), float(ctx.scale), _lib.ptr(out), out.stride(0), out.stride(1), None, stream)
+              int(ctx.window), float(ctx.scale), _lib.ptr(out), out.stride(0), out.stride(1), None,
+              _lib.COMBINE_AFTER_PARTIALS if use_history else 0, stream)
     return out
 
 

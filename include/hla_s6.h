@@ -135,12 +135,45 @@ int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const v
                         int32_t max_blocks, const int32_t* query_start_loc, int32_t num_reqs, int32_t num_tokens,
                         int32_t num_heads, int32_t head_dim, int64_t* slot_out, void* stream);
 
+/* Latent query fused with the exact-path preparation of the same (layer, loop), one launch:
+ * q_lat = latent_rope(bf16(q_pre . A[h])) as hla_s6_latent_query, and, when k is not NULL,
+ * q_rope = exact neox RoPE of q_pre (a separate output; q_pre is not modified) plus the
+ * exact-cache append of RoPE(k) | v as hla_s6_exact_append (slot_out optional).
+ * Replaces s6_layer.py:82-84 latent_query + the model rotary_emb + unified_kv_cache_update at
+ * hla/vllm_latent/ouro_latent.py:112-123.  q_pre and A rows must be 16-byte aligned. */
+int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A,
+                          int64_t a_stride_h, int64_t a_stride_k, const int64_t* positions, const void* table,
+                          int64_t table_stride, int64_t max_position, void* q_lat, int64_t q_lat_stride_t,
+                          int64_t q_lat_stride_h, int32_t num_tokens, int32_t num_heads, int32_t head_dim,
+                          int32_t width, void* q_rope, int64_t q_rope_stride_t, int64_t q_rope_stride_h,
+                          const void* k, int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
+                          int64_t v_stride_h, const float* cos_sin, int64_t cos_sin_stride, int64_t cos_sin_rows,
+                          void* cache, int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                          int64_t cache_stride_row, int32_t page, const int32_t* block_table,
+                          int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
+                          int32_t num_reqs, int64_t* slot_out, void* stream);
+
 /* Writer projection: reg_out = bf16(reg_in + bf16(h . weight^T)) (reg_in may be NULL), weight
- * [out_features, in_features] as nn.Linear.  Replaces register.py:45-61 write_step / write1
- * (cand_s[t-1](h) + previous, cand1(h)) called from s6_layer.py:124 write_rows. */
+ * [out_features, in_features] as nn.Linear; in_features % 128 == 0, out_features % 16 == 0.
+ * Replaces register.py:45-61 write_step / write1 (cand_s[t-1](h) + previous, cand1(h)) called
+ * from s6_layer.py:124 write_rows. */
 int hla_s6_writer_project(const void* h, int64_t h_stride_t, const void* weight, int64_t weight_stride_n,
                           const void* reg_in, int64_t reg_in_stride_t, void* reg_out, int64_t reg_out_stride_t,
                           int32_t num_tokens, int32_t out_features, int32_t in_features, void* stream);
+
+/* Writer projection with the row commit fused into its epilogue: the updated register
+ * [T, 2w] (w = out_features / 2) is written to reg_out when that is not NULL, and committed to
+ * the latent cache [num_blocks, 1, page, 2w] as hla_s6_commit_rows does (K half latent-RoPE'd
+ * in the torch bf16 order, V half copied, padding tokens skipped).  Replaces
+ * s6_layer.write_rows + committed_row + unified_kv_cache_update (s6_layer.py:124-147,
+ * ouro_latent.py:127-129) at the commit loops. */
+int hla_s6_writer_commit(const void* h, int64_t h_stride_t, const void* weight, int64_t weight_stride_n,
+                         const void* reg_in, int64_t reg_in_stride_t, void* reg_out, int64_t reg_out_stride_t,
+                         int32_t num_tokens, int32_t out_features, int32_t in_features, const int64_t* positions,
+                         const void* table, int64_t table_stride, int64_t max_position, void* cache,
+                         int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row, int32_t page,
+                         const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                         const int32_t* query_start_loc, int32_t num_reqs, void* stream);
 
 /* Committed row: row [T, 2 * width] (K | V) -> latent cache [num_blocks, 1, page, 2 * width]
  * at slot = block_table[req, pos / page] * page + pos % page with the K half latent-RoPE'd
@@ -158,7 +191,12 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
  * B [H, width, 128], run the exact window (as hla_s6_window_attention) and LSE-merge the two
  * (merge_states semantics; invalid tokens zeroed).  out bf16 [T, H, 128]; lse_out (optional
  * [H, T]) receives the merged lse.  Replaces s6_layer.py:97-115 (window_attention_fa +
- * history stage 2 + einsum B + merge_states). */
+ * history stage 2 + einsum B + merge_states).
+ * flags: HLA_S6_COMBINE_AFTER_PARTIALS declares that the immediately preceding launch on the
+ * stream is the hla_s6_history_partials call that produced the partials; the combine is then
+ * launched as a programmatic dependent of it, and its B prefetch and exact window (whose inputs
+ * must be complete before that history call) overlap the history kernel's tail. */
+#define HLA_S6_COMBINE_AFTER_PARTIALS 1
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
                           int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
                           const float* lse_in, const uint8_t* empty, const void* B, int64_t b_stride_h,
@@ -168,7 +206,7 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
                           const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
                           float scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse_out,
-                          void* stream);
+                          int32_t flags, void* stream);
 
 #ifdef __cplusplus
 }

@@ -256,3 +256,96 @@ def test_committed_row_in_place_matches_reference_fixture():
     k, v = layer().committed_row(SL, 3, st, Ctx)
     np.testing.assert_array_equal(torch.cat((k, v), -1).float().cpu().numpy(), g['row_main'])
     assert layer().committed_row(SL, 1, st, Ctx) is None
+
+
+# ----------------------------------------------------------------------------- fused entry points
+@pytest.mark.parametrize('loop', [0, 3])
+def test_writer_commit_equals_project_then_commit(loop):
+    """The commit fused into the writer epilogue writes exactly the rows that the projection followed
+    by the torch-order RoPE would (bit for bit), at exactly the vLLM slots; nothing else changes."""
+    rng = np.random.default_rng(loop + 7)
+    T, K, page, max_pos = 37, 256, 16, 4096
+    w = 256 if loop == 0 else 512
+    N = 2 * w
+    h = dev(orc.bf16(rng.standard_normal((T, K), dtype=np.float32)), BF16)
+    E = dev(orc.bf16(rng.standard_normal((N, K), dtype=np.float32) / 16), BF16)
+    reg_in = None if loop == 0 else dev(orc.bf16(rng.standard_normal((T, N), dtype=np.float32)), BF16)
+    lib = pkg('_lib')
+    st = lib.stream_of(h)
+    reg = torch.empty(T, N, dtype=BF16, device=CUDA)
+    lib.call('hla_s6_writer_project', lib.ptr(h), h.stride(0), lib.ptr(E), E.stride(0), lib.ptr(reg_in),
+             0 if reg_in is None else reg_in.stride(0), lib.ptr(reg), reg.stride(0), T, N, K, st)
+    R = T - 3                                                   # three padding tokens
+    qsl = torch.tensor(list(range(R + 1)), dtype=I32, device=CUDA)
+    pos = torch.from_numpy(rng.integers(0, 2 * page, T)).to(CUDA)
+    nb = 2 * R + 2
+    bt = (torch.randperm(nb - 1, device=CUDA).to(I32)[:2 * R] + 1).view(R, 2)
+    inv = layer().latent_inv_freq(128, 1e6)
+    table = layer().latent_rope_table(max_pos, inv, w, BF16).to(CUDA)
+    cache = torch.full((nb, 1, page, 2 * w), float('nan'), dtype=BF16, device=CUDA)
+    lib.call('hla_s6_writer_commit', lib.ptr(h), h.stride(0), lib.ptr(E), E.stride(0), lib.ptr(reg_in),
+             0 if reg_in is None else reg_in.stride(0), None, 0, T, N, K, lib.ptr(pos), lib.ptr(table),
+             table.stride(0), table.shape[0], lib.ptr(cache), nb, cache.stride(0), cache.stride(2), page, lib.ptr(bt),
+             bt.stride(0), bt.shape[1], lib.ptr(qsl), R, st)
+    torch.cuda.synchronize()
+    slots = (bt[torch.arange(R, device=CUDA), pos[:R] // page].long() * page + pos[:R] % page)
+    expect = orc.committed_row(reg[:R].float().cpu().numpy(), w, pos[:R].cpu().numpy(), table.float().cpu().numpy())
+    flat = cache.view(-1, 2 * w)
+    np.testing.assert_array_equal(flat[slots].float().cpu().numpy(), expect)
+    mask = torch.ones(flat.shape[0], dtype=torch.bool, device=CUDA)
+    mask[slots] = False
+    assert torch.isnan(flat[mask]).all()
+    # the projection itself against the oracle (bf16 GEMM tolerance)
+    upd = orc.write_update(h.float().cpu().numpy(), E.float().cpu().numpy())
+    ref = upd if reg_in is None else orc.write_step(reg_in.float().cpu().numpy(), upd)
+    np.testing.assert_allclose(reg.float().cpu().numpy(), ref, atol=3e-2, rtol=1e-2)
+
+
+def test_decode_prepare_fuses_latent_query_and_exact_append():
+    rng = np.random.default_rng(17)
+    T, H, d, W, page, max_pos = 21, 16, 128, 512, 16, 4096
+    R = T - 2
+    q = orc.bf16(rng.standard_normal((T, H, d), dtype=np.float32))
+    k = orc.bf16(rng.standard_normal((T, H, d), dtype=np.float32))
+    v = orc.bf16(rng.standard_normal((T, H, d), dtype=np.float32))
+    A = orc.bf16(rng.standard_normal((H, d, W), dtype=np.float32) / math.sqrt(128))
+    pos = rng.integers(0, 3 * page, T).astype(np.int64)
+    nb = 3 * R + 1
+    table_e = (np.arange(1, nb, dtype=np.int32)).reshape(R, 3)
+    inv = layer().latent_inv_freq(d, 1e6)
+    ltab = layer().latent_rope_table(max_pos, inv, W, BF16).to(CUDA)
+    ang = torch.arange(max_pos).float()[:, None] * inv[None]
+    cos_sin = torch.cat((ang.cos(), ang.sin()), -1).to(CUDA)
+    qd, kd, vd, Ad = dev(q, BF16), dev(k, BF16), dev(v, BF16), dev(A, BF16)
+    q_before = qd.clone()
+    posd, btd = dev(pos), dev(table_e)
+    qsl = torch.arange(R + 1, dtype=I32, device=CUDA)
+    q_lat = torch.empty(T, H, W, dtype=BF16, device=CUDA)
+    q_rope = torch.empty(T, H, d, dtype=BF16, device=CUDA)
+    cache = torch.full((nb, page, H, 2 * d), float('nan'), dtype=BF16, device=CUDA)
+    logical = cache.transpose(1, 2)
+    slots = torch.empty(T, dtype=torch.int64, device=CUDA)
+    lib = pkg('_lib')
+    lib.call('hla_s6_decode_prepare', lib.ptr(qd), qd.stride(0), qd.stride(1), lib.ptr(Ad), Ad.stride(0),
+             Ad.stride(1), lib.ptr(posd), lib.ptr(ltab), ltab.stride(0), ltab.shape[0], lib.ptr(q_lat),
+             q_lat.stride(0), q_lat.stride(1), T, H, d, W, lib.ptr(q_rope), q_rope.stride(0), q_rope.stride(1),
+             lib.ptr(kd), kd.stride(0), kd.stride(1), lib.ptr(vd), vd.stride(0), vd.stride(1), lib.ptr(cos_sin),
+             cos_sin.stride(0), cos_sin.shape[0], lib.ptr(logical), nb, logical.stride(0), logical.stride(1),
+             logical.stride(2), page, lib.ptr(btd), btd.stride(0), btd.shape[1], lib.ptr(qsl), R, lib.ptr(slots),
+             lib.stream_of(qd))
+    torch.cuda.synchronize()
+    assert torch.equal(qd, q_before)   # q_pre is read only
+    np.testing.assert_allclose(q_lat.float().cpu().numpy(), orc.latent_query(q, A, pos, ltab.float().cpu().numpy()),
+                               **O_TOL)
+    np.testing.assert_allclose(q_rope.float().cpu().numpy(), orc.neox_rope(q, pos, d, 1e6), **O_TOL)
+    req, valid = orc.token_requests(qsl.cpu().numpy(), T)
+    want = orc.cache_slots(table_e, req, pos, valid, page)
+    assert slots.cpu().numpy().tolist() == want.tolist()
+    flat = cache.float().cpu().numpy().reshape(nb * page, H, 2 * d)
+    k_ref = orc.neox_rope(k, pos, d, 1e6)
+    for t in range(T):
+        if want[t] >= 0:
+            np.testing.assert_allclose(flat[want[t], :, :d], k_ref[t], **O_TOL)
+            np.testing.assert_array_equal(flat[want[t], :, d:], v[t])
+    untouched = np.setdiff1d(np.arange(nb * page), want[want >= 0])
+    assert np.isnan(flat[untouched]).all()
