@@ -55,6 +55,22 @@ int hla_s6_history_attention(const void* q_lat, int64_t q_stride_t, int64_t q_st
                              int64_t workspace_floats, void* out, int64_t out_stride_t, int64_t out_stride_h,
                              float* lse, int* error_flag, void* stream);
 
+/* hla_s6_history_attention for callers that cannot allocate device memory (a foreign-language
+ * binding that is handed only input/output pointers, or a serving process whose GPU memory was
+ * reserved up front): same arguments and results, minus the workspace, which is taken from a
+ * fixed 8 MiB device array inside the library instead.  No counterpart in the reference.
+ * Limit: T * num_kv_splits * H * (W + 1) <= 2 * 1024 * 1024 floats, else HLA_S6_EOVERFLOW.
+ * The first call on each device looks up that array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the array: calls whose
+ * kernels overlap on the GPU race on it.  It allocates nothing. */
+int hla_s6_history_attention_static(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                                    int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,
+                                    const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
+                                    const int32_t* ctx, const uint8_t* empty, int32_t num_tokens, int32_t num_heads,
+                                    int32_t width, int32_t page, float scale, int32_t num_kv_splits, void* out,
+                                    int64_t out_stride_t, int64_t out_stride_h, float* lse, int* error_flag,
+                                    void* stream);
+
 /* Split stage only: leaves fp32 partials (o, lse per row segment) in the workspace for
  * hla_s6_history_reduce or hla_s6_decode_combine with the same (T, H, W, page, splits,
  * workspace).  Replaces the stage-1 half of s6_ops.py:156-159 (vLLM _fwd_grouped_kernel_stage1). */
