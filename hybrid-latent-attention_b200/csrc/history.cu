@@ -52,6 +52,8 @@ struct HistoryCfg {
   static constexpr int STAGES = PAGE_BYTES <= 16384 ? 4 : (PAGE_BYTES <= 32768 ? 3 : 2);
   static constexpr int THREADS = (NC + 1) * 32;
   static constexpr int XBUF_BYTES = 2 * NC * NT * 32 * 16;
+  // two CTAs per SM where the page ring allows it (W <= 512 with 16-row pages)
+  static constexpr int MIN_CTAS = (STAGES * PAGE_BYTES <= 100 * 1024) ? 2 : 1;
 };
 
 __host__ __device__ inline int64_t stream_start(int64_t c, int64_t P, int64_t G) { return c * P / G; }
@@ -68,7 +70,7 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int key_lo, int valid)
 }
 
 template <int W, int PG>
-__global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, 1)
+__global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>::MIN_CTAS)
     history_split_kernel(const __grid_constant__ CUtensorMap tmap, const HistoryParams p) {
   using C = HistoryCfg<W, PG>;
   constexpr int NC = C::NC, NT = C::NT, STAGES = C::STAGES;
