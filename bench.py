@@ -295,7 +295,7 @@ def run_ours(args):
     traffic = None
     tr = ncu_traffic()
     if tr and args.config == 2:
-        traffic = tr.get('history_split_w512_bytes_per_launch_config2')
+        traffic = tr.get('history_split_avg_bytes_per_launch_config2')
 
     # ---- e2e: pinned host activations in, outputs out, every step
     host_in = torch.empty(model.acts.shape, dtype=model.acts.dtype, pin_memory=True)

@@ -52,8 +52,10 @@ struct HistoryCfg {
   static constexpr int STAGES = PAGE_BYTES <= 16384 ? 4 : (PAGE_BYTES <= 32768 ? 3 : 2);
   static constexpr int THREADS = (NC + 1) * 32;
   static constexpr int XBUF_BYTES = 2 * NC * NT * 32 * 16;
-  // two CTAs per SM where the page ring allows it (W <= 512 with 16-row pages)
-  static constexpr int MIN_CTAS = (STAGES * PAGE_BYTES <= 100 * 1024) ? 2 : 1;
+  // Resident CTAs per SM the register budget is sized for: two for 512-wide 16-row pages, and for
+  // 256-wide pages a bound that keeps registers <= 168, so three 3-warp CTAs fit each SM
+  // sub-partition's register file (shared memory also allows three).
+  static constexpr int MIN_CTAS = PAGE_BYTES <= 16384 ? 4 : ((STAGES * PAGE_BYTES <= 100 * 1024) ? 2 : 1);
 };
 
 __host__ __device__ inline int64_t stream_start(int64_t c, int64_t P, int64_t G) { return c * P / G; }

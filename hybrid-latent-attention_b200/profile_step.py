@@ -1,0 +1,36 @@
+"""Run eager S6 decode steps of an Ouro-shaped model - a small, self-contained workload for profilers.
+
+    python hybrid-latent-attention_b200/profile_step.py [--layers 2] [--batch 64] [--ctx 8192] [--steps 2]
+
+Every step issues the four launches per (layer, loop) of ``decode.S6DecodeModel.step`` in order
+(writer, prepare, history split, combine; loop 0 reads the 256-wide latent, loops 1-3 the 512-wide
+one), so ``ncu -k regex:history_split -s 1 -c 2`` selects one launch of each width.  With the
+defaults the device holds about 3 GB.
+"""
+import argparse
+import importlib
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--layers', type=int, default=2)
+    ap.add_argument('--batch', type=int, default=64)
+    ap.add_argument('--ctx', type=int, default=8192)
+    ap.add_argument('--steps', type=int, default=2)
+    args = ap.parse_args()
+    import torch
+    dec = importlib.import_module('hybrid-latent-attention_b200.decode')
+    model = dec.S6DecodeModel(dec.OuroShape(layers=args.layers), dec.DecodeBatch([args.ctx] * args.batch),
+                              device='cuda', seed=0)
+    for _ in range(args.steps):
+        model.step(overlap_writer=False)
+    torch.cuda.synchronize()
+    print(f'ok: {args.steps} steps, {model.launches_per_step()} launches each')
+
+
+if __name__ == '__main__':
+    main()
