@@ -83,14 +83,18 @@ class ClockSampler:
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
 
-    def __init__(self, gpu_index):
-        self.gpu, self.proc, self.file = str(gpu_index), None, None
+    def __init__(self, local_rank):
+        # nvidia-smi numbers GPUs physically; CUDA_VISIBLE_DEVICES (indices or UUIDs) maps this rank's device
+        visible = [v.strip() for v in os.environ.get('CUDA_VISIBLE_DEVICES', '').split(',') if v.strip()]
+        self.gpu = visible[local_rank] if local_rank < len(visible) else str(local_rank)
+        self.proc, self.file = None, None
 
     def __enter__(self):
         try:
             self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
-            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200'], stdout=self.file, stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', self.gpu, f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -110,7 +114,7 @@ class ClockSampler:
         rows = []
         for line in Path(self.file.name).read_text().splitlines():
             parts = [x.strip() for x in line.split(',')]
-            if len(parts) >= 9 and parts[0] == self.gpu:
+            if len(parts) >= 9:
                 rows.append(parts)
         os.unlink(self.file.name)
         if not rows:
@@ -200,6 +204,17 @@ def cpu_threads():
         return os.cpu_count()
 
 
+def use_all_host_threads():
+    """Let the oracle's BLAS use every host thread (torchrun sets OMP_NUM_THREADS=1 for each rank)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else os.cpu_count()
+    try:
+        import threadpoolctl
+        threadpoolctl.threadpool_limits(limits=n)
+    except Exception:
+        pass
+    return n
+
+
 def run_reference(args):
     """--impl reference: the CPU oracle port of the reference path on this host, rank 0 only."""
     rank, world, _ = dist_env()
@@ -207,7 +222,10 @@ def run_reference(args):
         return
     dec = importlib.import_module(f'{PKG}.decode')
     shape = dec.OuroShape()
-    ctx, scaling = config_batch(args.config, 0, 1 if args.config == 2 else world, args.seed)
+    use_all_host_threads()
+    ctx, scaling = config_batch(args.config, 0, 1, args.seed)
+    if scaling == 'weak':
+        ctx = ctx * world          # the whole job's requests; tokens/s of the CPU path does not depend on B
     cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
     samples = []
     for i in range(args.warmup + args.steps):
@@ -332,6 +350,7 @@ def run_ours(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
+            use_all_host_threads()
             cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
             secs = [cs.run() for _ in range(args.cpu_reps)]
             sec, desc = statistics.median(secs), cs.describe() + f'; median of {args.cpu_reps} timed passes'
