@@ -42,11 +42,21 @@ def dist_env():
 
 
 def config_batch(config, rank, world, seed):
-    """Per-rank request contexts.  Config 2: 64 sequences at 8192 per GPU (weak scaling).  Config 4:
-    256 log-uniform contexts in [64, 32768] split across ranks by greedy sum-of-context balance."""
+    """Per-rank workload.  Returns (request contexts, scaling, latent rows held here or None, max_position).
+
+    Config 2: 64 sequences at 8192 per GPU (weak scaling).  Config 4: 256 log-uniform contexts in
+    [64, 32768] (a few shorter than the window) split across ranks by greedy sum-of-context balance.
+    Config 5: 4 sequences at 131072, each one's latent history split by pages across the ranks."""
     import numpy as np
+    dec = importlib.import_module(f'{PKG}.decode')
     if config == 2:
-        return [8192] * 64, 'weak'
+        return [8192] * 64, 'weak', None, 65536
+    if config == 5:
+        ctx = [131072] * 4
+        if world == 1:
+            return ctx, 'strong', None, 131200
+        split = dec.seq_split_rows([c - 32 for c in ctx], 16, rank, world)
+        return ctx, 'strong', [rows for _, rows in split], 131200
     rng = np.random.default_rng(seed)
     ctx = np.exp(rng.uniform(math.log(64), math.log(32768), 256)).astype(np.int64)
     ctx[:8] = rng.integers(1, 32, 8)           # some sequences shorter than the window
@@ -56,7 +66,7 @@ def config_batch(config, rank, world, seed):
         r = loads.index(min(loads))
         loads[r] += c
         mine[r].append(c)
-    return mine[rank], 'strong'
+    return mine[rank], 'strong', None, 65536
 
 
 def peaks():
@@ -223,7 +233,7 @@ def run_reference(args):
     dec = importlib.import_module(f'{PKG}.decode')
     shape = dec.OuroShape()
     use_all_host_threads()
-    ctx, scaling = config_batch(args.config, 0, 1, args.seed)
+    ctx, scaling, _, _ = config_batch(args.config, 0, 1, args.seed)
     if scaling == 'weak':
         ctx = ctx * world          # the whole job's requests; tokens/s of the CPU path does not depend on B
     cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
@@ -282,8 +292,11 @@ def run_ours(args):
     importlib.import_module(f'{PKG}._lib').load()
     dec = importlib.import_module(f'{PKG}.decode')
     shape = dec.OuroShape()
-    ctx, scaling = config_batch(args.config, rank, world, args.seed)
-    model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=args.seed + rank)
+    ctx, scaling, latent_rows, max_pos = config_batch(args.config, rank, world, args.seed)
+    shape = dec.OuroShape(max_position=max_pos)
+    exchange = (rank, world, dist.group.WORLD) if (args.config == 5 and world > 1) else None
+    model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=args.seed + rank,
+                              latent_rows=latent_rows, exchange=exchange)
     torch.cuda.synchronize()
     model.step()                       # eager warm-up: descriptor caches, occupancy
     graph = model.capture()
@@ -297,9 +310,7 @@ def run_ours(args):
         ms_total = time_graph(torch, graph, args.steps, dist)
     clocks = clk.summary()
     ms_step = ms_total / args.steps
-    tokens_all = len(ctx) * (world if scaling == 'weak' else 1)
-    if scaling == 'strong':
-        tokens_all = 256
+    tokens_all = len(ctx) * world if scaling == 'weak' else {4: 256, 5: 4}[args.config]
     value = tokens_all / (ms_step / 1e3)
 
     # ---- roofline of the dominant kernel: the 96 history launches of a step, alone
@@ -362,10 +373,13 @@ def run_ours(args):
             'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': scaling,
             'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded), random-init weights',
             'config': {'workload': f'BASELINE config {args.config}: Ouro-1.4B-shaped S6 decode step, attention path '
-                                   f'(24 layers x 4 loops), dense body excluded',
+                                   f'(24 layers x 4 loops), dense body excluded' +
+                                   (', latent history sequence-split across GPUs, NCCL all-gather of (z, lse) '
+                                    'per (layer, loop)' if exchange is not None else ''),
                        'global_batch': tokens_all, 'batch_per_gpu': len(ctx), 'ctx': max(ctx),
                        'seq_len': max(ctx) + 1, 'page': shape.page, 'window': shape.window,
-                       'parallelism': f'request-partitioned x{world} (no collectives)',
+                       'parallelism': (f'sequence-split x{world} (NCCL all_gather per layer x loop)' if exchange
+                                       is not None else f'request-partitioned x{world} (no collectives)'),
                        'l2': 'inputs larger than L2 (latent caches ~40 GB per GPU), no flush'},
             'latent_history': {'bytes_per_step': bytes_hist, 'GBps_in_step': bytes_hist / (ms_step / 1e3) / 1e9,
                                'attention_bytes_per_step': attn_bytes,
@@ -395,7 +409,7 @@ def main():
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', type=int, default=2, choices=[2, 4])
+    ap.add_argument('--config', type=int, default=2, choices=[2, 4, 5])
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
     ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')

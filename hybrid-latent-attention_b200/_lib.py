@@ -45,7 +45,8 @@ SIGNATURES = {
                               _i32, P, _i64, _i32, P, _i32, P, P],
     'hla_s6_commit_rows': [P, _i64, _i32, P, P, _i64, _i64, P, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _i32,
                            P, P],
-    'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, P, _i64, _i64, P, _i64, _i64, P, _i64,
+    'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i32, _i64, P, P, _i64, _i64, P, _i64,
+                              _i64, P, _i64,
                               _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, _i32,
                               P],
 }

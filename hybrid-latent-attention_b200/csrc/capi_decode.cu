@@ -350,7 +350,8 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
 
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
                           int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
-                          const float* lse_in, const uint8_t* empty, const void* B, int64_t b_stride_h,
+                          const float* lse_in, int32_t num_parts, int64_t part_stride, const uint8_t* empty,
+                          const void* B, int64_t b_stride_h,
                           int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
                           const void* exact_cache, int64_t exact_num_blocks, int64_t exact_stride_block,
                           int64_t exact_stride_head, int64_t exact_stride_row, int32_t exact_page,
@@ -384,8 +385,9 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
     a.ws_floats = workspace_floats;
     a.waves = 1;
     if ((rc = history_plan(a, &plan))) return rc;
-  } else if (!lse_in || !aligned(z_in, 16)) {
-    set_error("a reduced history input needs a 16-byte aligned z [T, H, W] and its lse [H, T]");
+  } else if (!lse_in || !aligned(z_in, 16) || num_parts < 1 || (num_parts > 1 && (part_stride % 4))) {
+    set_error("a reduced history input needs >= 1 part of 16-byte aligned z [T, H, W] with its lse [H, T] "
+              "(part stride a multiple of 4 floats)");
     return kStatusInvalid;
   }
   p.ws_o = plan.ws_o;
@@ -394,6 +396,8 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
   p.stream_mode = plan.stream_mode;
   p.z_in = z_in;
   p.lse_in = lse_in;
+  p.num_parts = z_in ? num_parts : 0;
+  p.part_stride = part_stride;
   p.empty = empty;
   p.T = num_tokens;
   p.H = num_heads;

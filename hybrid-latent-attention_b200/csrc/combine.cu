@@ -8,8 +8,8 @@
 // CTA = (8 tokens, head h), 8 warps, one token per warp.  All of B[h] ([W, 128] bf16) is put in
 // flight with cp.async before steps 1-2, so its latency hides behind them; step 3 is mma.m16n8k16 with the 8
 // tokens as M (rows 8-15 zero; z from shared memory, B via ldmatrix.trans).  Instead of split partials the kernel
-// can take an already reduced (z fp32 [T,H,W], lse [H,T]) pair - how a sequence-split history
-// arrives after its cross-GPU exchange.
+// can take num_parts reduced (z fp32 [T,H,W], lse [H,T]) pairs and LSE-merge them - how a
+// sequence-split history arrives after its cross-GPU exchange.
 #include "combine.cuh"
 #include "common.cuh"
 #include "decode_ops.cuh"
@@ -78,11 +78,31 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
     float lse_h = -INFINITY;
     if (t < T && !(p.empty && p.empty[t])) {
       if (p.z_in) {
-        lse_h = p.lse_in[static_cast<int64_t>(h) * T + t];
-        if (lse_h != -INFINITY) {
-          const float4* src = reinterpret_cast<const float4*>(p.z_in + (static_cast<int64_t>(t) * H + h) * W);
+        // num_parts reduced partials (e.g. one per GPU of a sequence split): LSE-merge them
+        float mx = -INFINITY;
+        for (int q = 0; q < p.num_parts; ++q)
+          mx = fmaxf(mx, p.lse_in[q * p.part_stride + static_cast<int64_t>(h) * T + t]);
+        if (mx != -INFINITY) {
+          float wsum = 0.f;
+          for (int q = 0; q < p.num_parts; ++q) {
+            const float lq = p.lse_in[q * p.part_stride + static_cast<int64_t>(h) * T + t];
+            if (lq == -INFINITY) continue;
+            const float wgt = expf(lq - mx);
+            wsum += wgt;
+            const float4* src =
+                reinterpret_cast<const float4*>(p.z_in + q * p.part_stride + (static_cast<int64_t>(t) * H + h) * W);
 #pragma unroll
-          for (int i = 0; i < NV; ++i) acc[i] = src[i * 32 + lane];
+            for (int i = 0; i < NV; ++i) {
+              const float4 v = src[i * 32 + lane];
+              acc[i].x += wgt * v.x; acc[i].y += wgt * v.y; acc[i].z += wgt * v.z; acc[i].w += wgt * v.w;
+            }
+          }
+          const float inv = 1.f / wsum;
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            acc[i].x *= inv; acc[i].y *= inv; acc[i].z *= inv; acc[i].w *= inv;
+          }
+          lse_h = mx + logf(wsum);
         }
       } else {
         int lo = t, hi = t + 1;

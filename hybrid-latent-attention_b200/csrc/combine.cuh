@@ -6,13 +6,16 @@ namespace hla {
 
 struct CombineParams {
   // history input: split partials of the history kernel (ws_o / ws_lse / meta as planned for the
-  // same call) or, when z_in is set, a reduced fp32 z [T, H, W] with lse_in [H, T]
+  // same call) or, when z_in is set, num_parts reduced partials (fp32 z and its lse) - one per GPU
+  // of a sequence-split history - that are LSE-merged here
   const float* ws_o;
   const float* ws_lse;
   const int2* meta;
   int stream_mode;
-  const float* z_in;
-  const float* lse_in;
+  const float* z_in;    // part q: z [T, H, W] at z_in + q * part_stride
+  const float* lse_in;  // part q: lse [H, T] at lse_in + q * part_stride
+  int num_parts;
+  int64_t part_stride;  // floats between consecutive parts
   const uint8_t* empty;  // optional [T]: rows whose latent history is empty
   int T, H;
   const __nv_bfloat16* B;  // [H, W, 128] up-projection

@@ -48,6 +48,19 @@ class OuroShape:
     max_position: int = 65536
 
 
+def seq_split_rows(latent_rows, page, rank, world):
+    """Sequence split of each request's latent history across ``world`` GPUs by whole pages: rank r holds
+    pages ``[r * P // world, (r + 1) * P // world)`` of a request with P pages.  Returns, per request,
+    ``(first_page, rows)``; the slices of all ranks tile the history exactly."""
+    out = []
+    for n in latent_rows:
+        pages = -(-int(n) // page)
+        p0, p1 = rank * pages // world, (rank + 1) * pages // world
+        rows = max(0, min(int(n), p1 * page) - p0 * page)
+        out.append((p0, rows))
+    return out
+
+
 @dataclass
 class DecodeBatch:
     """Per-request history lengths (tokens before the current one)."""
@@ -55,7 +68,17 @@ class DecodeBatch:
 
 
 class S6DecodeModel:
-    def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512):
+    """Decode-step state and launches.
+
+    ``latent_rows`` (optional, per request) is the number of latent history rows this GPU holds; by
+    default every request's whole latent history ``ctx - W``.  ``exchange = (rank, world, group)``
+    turns on the sequence split: each GPU holds a contiguous slice of every request's latent pages,
+    reduces its slice's partials to fp32 ``(z, lse)``, all-gathers them over NCCL and merges the
+    ``world`` parts in the combine (the window, query and writer work is replicated).
+    """
+
+    def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
+                 latent_rows=None, exchange=None):
         self.s, self.device = shape, torch.device(device)
         s = shape
         B = len(batch.ctx)
@@ -83,11 +106,18 @@ class S6DecodeModel:
         self.positions = ctx.to(self.device)
         self.qsl = torch.arange(B + 1, dtype=torch.int32, device=self.device)
         self.seq_lens = (ctx + 1).to(torch.int32).to(self.device)
-        self.ctx_latent = (ctx - s.window).clamp(min=0).to(torch.int32).to(self.device)
-        self.latent_rows = int((ctx - s.window).clamp(min=0).sum())
-        # ---- latent caches: pages for rows [0, ctx] of every request, shuffled
-        lpages = [-(-(c + 1) // s.page) for c in batch.ctx]
+        rows = (ctx - s.window).clamp(min=0) if latent_rows is None else torch.tensor(latent_rows, dtype=torch.int64)
+        self.ctx_latent = rows.to(torch.int32).to(self.device)
+        self.latent_rows = int(rows.sum())
+        self.exchange = exchange
+        # ---- latent caches: pages for rows [0, ctx] of every request (room for the committed row), shuffled;
+        #      a sequence-split slice holds only its own rows (its commits fall outside the table: skipped)
+        if latent_rows is None:
+            lpages = [-(-(c + 1) // s.page) for c in batch.ctx]
+        else:
+            lpages = [max(1, -(-int(r) // s.page)) for r in latent_rows]
         self.lmax = max(lpages)
+        self.emax = max(-(-(c + 1) // s.page) for c in batch.ctx)
         lnb = sum(lpages) + 1
         perm = torch.randperm(lnb - 1, generator=torch.Generator().manual_seed(seed + 1)).to(torch.int32) + 1
         ltab = torch.zeros(B, self.lmax, dtype=torch.int32)
@@ -101,7 +131,7 @@ class S6DecodeModel:
         for c in (*self.main, *self.l1):
             c[0].fill_(float('inf'))   # null block: any read of it would be loud
         # ---- exact caches: only the pages of [ctx - W, ctx] exist per request
-        etab = torch.zeros(B, self.lmax, dtype=torch.int32)
+        etab = torch.zeros(B, self.emax, dtype=torch.int32)
         k = 1
         for r, c in enumerate(batch.ctx):
             for col in range(max(0, c - s.window) // s.page, c // s.page + 1):
@@ -128,6 +158,11 @@ class S6DecodeModel:
         self.q_lat = torch.empty(B, s.heads, s.rank, dtype=BF16, device=self.device)
         self.q_rope = torch.empty(B, s.heads, s.head_dim, dtype=BF16, device=self.device)
         self.reg = [torch.empty(B, 2 * s.rank, dtype=BF16, device=self.device) for _ in range(s.layers)]
+        if exchange is not None:
+            world = exchange[1]
+            part = B * s.heads * s.rank + s.heads * B          # z [B, H, W] then lse [H, B], W <= rank
+            self.xsend = torch.empty(part, dtype=torch.float32, device=self.device)
+            self.xrecv = torch.empty(world * part, dtype=torch.float32, device=self.device)
         self.scale = s.head_dim ** -0.5
         self.graph = None
         self.history_graph = None
@@ -206,18 +241,32 @@ class S6DecodeModel:
                   self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, None, stream)
         # 3. history split
         self._history(layer, loop, stream)
+        # 3b. sequence split: reduce this GPU's slice to (z, lse) and all-gather the parts
+        z_in = lse_in = None
+        parts, part_stride, flags = 0, 0, _lib.COMBINE_AFTER_PARTIALS
+        if self.exchange is not None:
+            rank, world, group = self.exchange
+            zf = B * s.heads * width
+            part_stride = zf + s.heads * B
+            send = self.xsend[:part_stride]
+            _lib.call('hla_s6_history_reduce', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws),
+                      self.ws_floats, None, None, 0, 0, _lib.ptr(send), _lib.ptr(send[zf:]), stream)
+            recv = self.xrecv[:world * part_stride]
+            torch.distributed.all_gather_into_tensor(recv, send, group=group)
+            z_in, lse_in, parts, flags = recv, recv[zf:], world, 0
         # 4. fused combine -> out
         out = self.out[layer, loop]
         _lib.call('hla_s6_decode_combine', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws), self.ws_floats,
-                  None, None, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
+                  _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
                   _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
                   _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
                   _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), _lib.ptr(out),
-                  out.stride(0), out.stride(1), None, _lib.COMBINE_AFTER_PARTIALS, stream)
+                  out.stride(0), out.stride(1), None, flags, stream)
 
     def launches_per_step(self):
+        """Launches of this library per step (the sequence split adds one reduce per (layer, loop))."""
         s = self.s
-        return s.layers * s.loops * 4
+        return s.layers * s.loops * (5 if self.exchange is not None else 4)
 
     def step(self, overlap_writer=True):
         """One decode step.  With ``overlap_writer`` the writer launches run on a side stream forked from

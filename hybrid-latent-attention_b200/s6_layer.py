@@ -131,7 +131,7 @@ def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_sc
         ninf = torch.full((H, T), float('-inf'), dtype=torch.float32, device=q_rope.device)
         empty = None
     _lib.call('hla_s6_decode_combine', T, H, width, lpage, int(splits), _lib.ptr(ws_ptr), ws_floats,
-              None if use_history else _lib.ptr(zero), None if use_history else _lib.ptr(ninf),
+              None if use_history else _lib.ptr(zero), None if use_history else _lib.ptr(ninf), 1, 0,
               _lib.ptr(empty), _lib.ptr(B), B.stride(0), B.stride(1), _lib.ptr(q_rope), q_rope.stride(0),
               q_rope.stride(1), _lib.ptr(exact), enb, esb, esh, esr, epage, _lib.ptr(exact_table),
               exact_table.stride(0), exact_table.shape[1], _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(seq_lens),

@@ -202,8 +202,10 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
                        int32_t num_reqs, int32_t num_tokens, int64_t* slot_out, void* stream);
 
 /* Fused decode tail of one (layer, loop): reduce the history partials left by
- * hla_s6_history_partials (same T, H, width, page, splits, workspace) - or take a reduced
- * z_in fp32 [T, H, width] with lse_in [H, T] instead - round to bf16, up-project by
+ * hla_s6_history_partials (same T, H, width, page, splits, workspace) - or, when z_in is not
+ * NULL, LSE-merge num_parts reduced partials (one per GPU of a sequence-split history): part q
+ * is z fp32 [T, H, width] at z_in + q * part_stride and its lse [H, T] at lse_in + q * part_stride
+ * (floats; a multiple of 4) - round to bf16, up-project by
  * B [H, width, 128], run the exact window (as hla_s6_window_attention) and LSE-merge the two
  * (merge_states semantics; invalid tokens zeroed).  out bf16 [T, H, 128]; lse_out (optional
  * [H, T]) receives the merged lse.  Replaces s6_layer.py:97-115 (window_attention_fa +
@@ -215,7 +217,8 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
 #define HLA_S6_COMBINE_AFTER_PARTIALS 1
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
                           int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
-                          const float* lse_in, const uint8_t* empty, const void* B, int64_t b_stride_h,
+                          const float* lse_in, int32_t num_parts, int64_t part_stride, const uint8_t* empty,
+                          const void* B, int64_t b_stride_h,
                           int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
                           const void* exact_cache, int64_t exact_num_blocks, int64_t exact_stride_block,
                           int64_t exact_stride_head, int64_t exact_stride_row, int32_t exact_page,
