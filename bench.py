@@ -396,7 +396,12 @@ def run_ours(args):
             'clocks': clocks,
         }
         print(json.dumps(line), flush=True)
+    # CUDA graphs that hold NCCL calls must be released before the process group is destroyed
+    model.graph = model.history_graph = None
     del graph, hist_graph
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
