@@ -47,8 +47,12 @@ SIGNATURES = {
                            P, P],
     'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i32, _i64, P, P, _i64, _i64, P, _i64,
                               _i64, P, _i64,
-                              _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, _i32,
-                              P],
+                              _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, P,
+                              _i64, _i64, P, _i32, P],
+    'hla_s6_window_history': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _f32, _i32,
+                              _i32, _i32, P, _i64, _i64, P, P],
+    'hla_s6_chunk_attention': [P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i32, _i32, _i32, _i32, _f32, P, _i64,
+                               _i64, P, P],
 }
 
 _lib = None

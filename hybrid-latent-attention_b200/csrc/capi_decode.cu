@@ -51,6 +51,7 @@ static WindowArgs make_window(const void* q, int64_t q_st, int64_t q_sh, const v
   w.seq_lens = seq_lens;
   w.window = window;
   w.scale = scale;
+  w.ctx_tok = nullptr;
   return w;
 }
 
@@ -76,6 +77,22 @@ int hla_s6_window_attention(const void* q, int64_t q_stride_t, int64_t q_stride_
     set_error("window attention needs at least one request");
     return kStatusInvalid;
   }
+  return window_attention(w, num_tokens, num_heads, out, out_stride_t, out_stride_h, lse,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_window_history(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                          int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                          int64_t cache_stride_row, int32_t page, const int32_t* token_block_table,
+                          int64_t block_table_stride, int32_t max_blocks, const int32_t* ctx, int32_t window,
+                          float scale, int32_t num_tokens, int32_t num_heads, int32_t head_dim, void* out,
+                          int64_t out_stride_t, int64_t out_stride_h, float* lse, void* stream) {
+  WindowArgs w = make_window(q, q_stride_t, q_stride_h, cache, num_blocks, cache_stride_block, cache_stride_head,
+                             cache_stride_row, page, token_block_table, block_table_stride, max_blocks, nullptr, 0,
+                             nullptr, window, scale);
+  w.ctx_tok = ctx;
+  int rc = check_window(w, head_dim);
+  if (rc) return rc;
   return window_attention(w, num_tokens, num_heads, out, out_stride_t, out_stride_h, lse,
                           static_cast<cudaStream_t>(stream));
 }
@@ -357,14 +374,26 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           int64_t exact_stride_head, int64_t exact_stride_row, int32_t exact_page,
                           const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
                           const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
-                          float scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse_out,
-                          int32_t flags, void* stream) {
+                          float scale, const void* chunk_o, int64_t chunk_stride_t, int64_t chunk_stride_h,
+                          const float* chunk_lse, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                          float* lse_out, int32_t flags, void* stream) {
   CombineParams p;
   p.win = make_window(q_rope, q_stride_t, q_stride_h, exact_cache, exact_num_blocks, exact_stride_block,
                       exact_stride_head, exact_stride_row, exact_page, block_table, block_table_stride, max_blocks,
                       query_start_loc, num_reqs, seq_lens, window, scale);
-  int rc = check_window(p.win, 128);
-  if (rc) return rc;
+  int rc = kStatusOk;
+  if (chunk_o) {
+    if (!chunk_lse || !aligned(chunk_o, 8) || (chunk_stride_t % 4) || (chunk_stride_h % 4)) {
+      set_error("decode combine: an external chunk part needs 8-byte aligned rows and its lse");
+      return kStatusInvalid;
+    }
+  } else if ((rc = check_window(p.win, 128))) {
+    return rc;
+  }
+  p.chunk_o = static_cast<const __nv_bfloat16*>(chunk_o);
+  p.co_st = chunk_stride_t;
+  p.co_sh = chunk_stride_h;
+  p.chunk_lse = chunk_lse;
   if (num_heads < 1 || num_heads > 16 || num_reqs < 1) {
     set_error("decode combine needs 1..16 heads and >= 1 request");
     return kStatusInvalid;

@@ -64,7 +64,16 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
   {
     const int tt = warp, t = t0 + tt;
     float o[4], lse_w;
-    if (t < T) {
+    if (t < T && p.chunk_o) {
+      const __nv_bfloat16* src = p.chunk_o + static_cast<int64_t>(t) * p.co_st + static_cast<int64_t>(h) * p.co_sh;
+      const uint2 u = *reinterpret_cast<const uint2*>(src + lane * 4);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+      o[0] = __bfloat162float(b[0].x);
+      o[1] = __bfloat162float(b[0].y);
+      o[2] = __bfloat162float(b[1].x);
+      o[3] = __bfloat162float(b[1].y);
+      lse_w = p.chunk_lse[static_cast<int64_t>(h) * T + t];
+    } else if (t < T) {
       window_warp(win, t, h, q_s + warp * 128, o, lse_w);
     } else {
       o[0] = o[1] = o[2] = o[3] = 0.f;

@@ -21,6 +21,11 @@ struct CombineParams {
   const __nv_bfloat16* B;  // [H, W, 128] up-projection
   int64_t b_sh, b_sk;
   WindowArgs win;
+  // external exact part (prefill / mixed steps): the chunk attention already merged with the window
+  // history, used in place of the decode window when chunk_o is set
+  const __nv_bfloat16* chunk_o;
+  int64_t co_st, co_sh;
+  const float* chunk_lse;
   __nv_bfloat16* out;  // [T, H, 128]
   int64_t o_st, o_sh;
   float* lse_out;  // optional [H, T] merged lse

@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(128) window_kernel(const WindowArgs a, __nv_bf
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x, h = blockIdx.y * 4 + warp;
   WindowArgs w = a;
-  w.qsl = stage_qsl(a.qsl, a.R, qsl_s);
+  if (!a.ctx_tok) w.qsl = stage_qsl(a.qsl, a.R, qsl_s);
   if (h >= H) return;
   float o[4], lse;
   window_warp(w, t, h, q_s[warp], o, lse);

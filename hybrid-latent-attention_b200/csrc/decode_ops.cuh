@@ -82,6 +82,9 @@ struct WindowArgs {
   const int32_t* seq_lens;  // [R]
   int window;
   float scale;
+  // per-token history mode (window_history_fa): when set, token t reads rows [ctx_tok[t] - window,
+  // ctx_tok[t]) through row t of a per-token block table, without the current token
+  const int32_t* ctx_tok;
 };
 
 // One warp computes the exact window attention of token t, head h over keys
@@ -95,12 +98,20 @@ __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, f
   const int lane = threadIdx.x & 31;
   o[0] = o[1] = o[2] = o[3] = 0.f;
   lse = -INFINITY;
-  int r;
-  if (!token_request(a.qsl, a.R, t, r)) return;
-  const int qlen = a.qsl[r + 1] - a.qsl[r];
-  const int64_t pos = static_cast<int64_t>(a.seq_lens[r]) - qlen + (t - a.qsl[r]);
+  int r, win = a.window;
+  int64_t pos;
+  if (a.ctx_tok) {
+    r = t;
+    pos = static_cast<int64_t>(a.ctx_tok[t]) - 1;
+    win = a.window - 1;
+    if (a.window <= 0) return;
+  } else {
+    if (!token_request(a.qsl, a.R, t, r)) return;
+    const int qlen = a.qsl[r + 1] - a.qsl[r];
+    pos = static_cast<int64_t>(a.seq_lens[r]) - qlen + (t - a.qsl[r]);
+  }
   if (pos < 0) return;
-  const int64_t first = pos - a.window > 0 ? pos - a.window : 0;
+  const int64_t first = pos - win > 0 ? pos - win : 0;
   const int n = static_cast<int>(pos - first + 1);
   {
     const __nv_bfloat16* qp = a.q + static_cast<int64_t>(t) * a.q_st + static_cast<int64_t>(h) * a.q_sh + lane * 4;

@@ -260,7 +260,8 @@ class S6DecodeModel:
                   _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
                   _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
                   _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
-                  _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), _lib.ptr(out),
+                  _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), None, 0, 0, None,
+                  _lib.ptr(out),
                   out.stride(0), out.stride(1), None, flags, stream)
 
     def launches_per_step(self):

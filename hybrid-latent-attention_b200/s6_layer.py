@@ -7,7 +7,7 @@ then per layer and loop ``latent_query`` (before the exact RoPE), ``attend``, ``
 The decode branch of ``attend`` (``max_query_len == 1`` with an exact window) is two launches:
 the stream-K history kernel and the fused combine (split reduce, B up-projection, exact window,
 LSE merge), where the reference issues FA2, the Triton history stages, a cuBLAS einsum and the
-merge kernel.
+merge kernel.  Prefill / mixed steps add the causal chunk attention and the window history.
 """
 from __future__ import annotations
 
@@ -94,28 +94,33 @@ class StepContext:
 
 
 def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_scale, ctx, window=None):
-    """One softmax over the paged latent history and the exact window + current token (reference
-    s6_layer.py:87-115).  ``window = (exact_cache, per-request block table)``; returns ``[T,H,d]`` with
-    ``~valid`` rows zeroed.
+    """One softmax over the paged latent history and the exact part (reference s6_layer.py:87-115).
 
-    Decode steps (the ones CUDA graphs capture) run the fused path: history split kernel + fused combine.
-    Prefill / mixed steps need the causal chunk attention, which this backend does not provide yet:
-    they raise ``NotImplementedError``.
+    ``window = (exact_cache, per-request block table)`` or None; returns ``[T,H,d]`` with ``~valid``
+    rows zeroed.  Decode steps with a window (the ones CUDA graphs capture): the stream-K history split
+    then one fused combine (split reduce, B up-projection, window over the exact cache incl. the
+    current token, merge).  Other steps: causal chunk attention, merged with the window history when
+    there is a window, then history split + combine taking that exact part.
     """
-    fused = window is not None and ctx.md_present and ctx.max_query_len == 1
-    if not fused:
-        raise NotImplementedError('b200 backend: prefill / mixed S6 steps (causal chunk attention) are not built yet')
     s6_ops._require(ctx.backends.history, 'history')
-    exact, exact_table = window
     T, H, d = q_rope.shape
+    stream = _lib.stream_of(q_rope)
+    qsl, seq_lens = ctx.query_start_loc, ctx.seq_lens
+    fused = window is not None and ctx.md_present and ctx.max_query_len == 1
+    chunk_o = chunk_lse = None
+    if not fused:
+        chunk_o, chunk_lse = s6_ops.chunk_attention(q_rope, k_rope, v, qsl, ctx.max_query_len, ctx.invalid, ctx.scale,
+                                                    ctx.backends.chunk)
+        if cache is None or not ctx.md_present or not ctx.history_needed:
+            return chunk_o.masked_fill_(ctx.invalid[:, None, None], 0)
+        if window is not None:
+            o_win, lse_win = s6_ops.window_history_fa(q_rope, window[0], ctx.block_table(window[1]), ctx.ctx,
+                                                      ctx.window, ctx.scale, ctx.max_seqlen_k, ctx.empty)
+            chunk_o, chunk_lse = s6_ops.merge_lse(chunk_o, chunk_lse, o_win, lse_win)
     A, B, width = sl.readers(loop)
     out = torch.empty(T, H, d, dtype=q_rope.dtype, device=q_rope.device)
-    (enb, _, epage, _), (esb, esh, esr, _) = s6_ops._exact_cache_geometry(exact)
-    qsl, seq_lens = ctx.query_start_loc, ctx.seq_lens
-    stream = _lib.stream_of(q_rope)
     use_history = cache is not None and ctx.md_present and ctx.history_needed
-    ws_ptr, ws_floats, splits = None, 0, ctx.num_kv_splits
-    lpage = 16
+    ws_ptr, ws_floats, splits, lpage = None, 0, ctx.num_kv_splits, 16
     if use_history:
         nb, lpage, sb, sr = s6_ops._latent_cache_geometry(cache, width)
         ws = ctx.workspace.attn_logits(T, H, splits, width, q_lat.device)
@@ -124,19 +129,27 @@ def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_sc
         _lib.call('hla_s6_history_partials', _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), _lib.ptr(cache), nb,
                   sb, sr, _lib.ptr(bt), bt.stride(0), bt.shape[1], _lib.ptr(ctx.ctx_latent), T, H, width, lpage,
                   float(ctx.scale), int(splits), _lib.ptr(ws_ptr), ws_floats, None, stream)
+        z_in = lse_in = None
         empty = ctx.empty_latent
     else:
-        # no history: a reduced (z = 0, lse = -inf) input stands in for the partials
-        zero = torch.zeros(T, H, width, dtype=torch.float32, device=q_rope.device)
-        ninf = torch.full((H, T), float('-inf'), dtype=torch.float32, device=q_rope.device)
+        # no history: one reduced part with lse = -inf stands in for the partials
+        z_in = torch.zeros(T, H, width, dtype=torch.float32, device=q_rope.device)
+        lse_in = torch.full((H, T), float('-inf'), dtype=torch.float32, device=q_rope.device)
         empty = None
-    _lib.call('hla_s6_decode_combine', T, H, width, lpage, int(splits), _lib.ptr(ws_ptr), ws_floats,
-              None if use_history else _lib.ptr(zero), None if use_history else _lib.ptr(ninf), 1, 0,
-              _lib.ptr(empty), _lib.ptr(B), B.stride(0), B.stride(1), _lib.ptr(q_rope), q_rope.stride(0),
-              q_rope.stride(1), _lib.ptr(exact), enb, esb, esh, esr, epage, _lib.ptr(exact_table),
-              exact_table.stride(0), exact_table.shape[1], _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(seq_lens),
-              int(ctx.window), float(ctx.scale), _lib.ptr(out), out.stride(0), out.stride(1), None,
-              _lib.COMBINE_AFTER_PARTIALS if use_history else 0, stream)
+    if fused:
+        exact, exact_table = window
+        (enb, _, epage, _), (esb, esh, esr, _) = s6_ops._exact_cache_geometry(exact)
+        win_args = (_lib.ptr(q_rope), q_rope.stride(0), q_rope.stride(1), _lib.ptr(exact), enb, esb, esh, esr, epage,
+                    _lib.ptr(exact_table), exact_table.stride(0), exact_table.shape[1])
+        chunk_args = (None, 0, 0, None)
+    else:
+        win_args = (None, 0, 0, None, 0, 0, 0, 0, 1, None, 0, 0)
+        chunk_args = (_lib.ptr(chunk_o), chunk_o.stride(0), chunk_o.stride(1), _lib.ptr(chunk_lse))
+    flags = _lib.COMBINE_AFTER_PARTIALS if (use_history and fused) else 0
+    _lib.call('hla_s6_decode_combine', T, H, width, lpage, int(splits), _lib.ptr(ws_ptr), ws_floats, _lib.ptr(z_in),
+              _lib.ptr(lse_in), 1, 0, _lib.ptr(empty), _lib.ptr(B), B.stride(0), B.stride(1), *win_args,
+              _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(seq_lens), int(ctx.window), float(ctx.scale), *chunk_args,
+              _lib.ptr(out), out.stride(0), out.stride(1), None, flags, stream)
     return out
 
 

@@ -187,6 +187,49 @@ def window_attention_fa(q, cache, block_table, query_start_loc, seq_lens, window
     return o, lse
 
 
+def window_history_fa(q, cache, token_block_table, ctx, window, scale, max_seqlen_k, empty):
+    """Exact window over history rows only (non-decode steps): token ``t`` reads rows ``[ctx[t] - window,
+    ctx[t])`` of the exact cache ``[nb, H, block, 2d]`` through row ``t`` of a per-token block table.
+    Rows without history give ``o = 0``, ``lse = -inf`` (reference s6_ops.py:334-350; ``max_seqlen_k``
+    and ``empty`` are accepted for signature compatibility - ``ctx == 0`` is the empty condition)."""
+    _check_cuda(q, cache, token_block_table, ctx)
+    T, H, d = q.shape
+    (nb, Hc, block, two_d), (sb, sh, sr, _) = _exact_cache_geometry(cache)
+    if Hc != H or two_d != 2 * d or q.stride(-1) != 1 or q.dtype != torch.bfloat16:
+        raise ValueError('window history: q [T,H,d] bf16 must match the exact cache [nb, H, block, 2d]')
+    if ctx.dtype != torch.int32 or token_block_table.dtype != torch.int32:
+        raise ValueError('window history: ctx and the block table must be int32')
+    o = torch.empty(T, H, d, dtype=q.dtype, device=q.device)
+    lse = torch.empty(H, T, dtype=torch.float32, device=q.device)
+    ctx_c = ctx.contiguous()
+    _lib.call('hla_s6_window_history', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(cache), nb, sb, sh, sr, block,
+              _lib.ptr(token_block_table), token_block_table.stride(0), token_block_table.shape[1], _lib.ptr(ctx_c),
+              int(window), float(scale), T, H, d, _lib.ptr(o), o.stride(0), o.stride(1), _lib.ptr(lse),
+              _lib.stream_of(q))
+    return o, lse
+
+
+# ----------------------------------------------------------------------------- causal chunk
+def chunk_attention(q, k, v, query_start_loc, max_query_len, invalid, scale, backend):
+    """Causal attention within each request's current chunk (``q, k, v`` are ``[T,H,d]``).
+
+    Returns ``(o[T,H,d] bf16, lse[H,T] fp32)``; padding tokens (``t >= query_start_loc[-1]``) give
+    ``o = 0`` and ``lse = -inf`` (reference s6_ops.py:234-259; ``max_query_len`` and ``invalid`` are
+    accepted for signature compatibility - validity follows ``query_start_loc``)."""
+    _require(backend, 'chunk')
+    _check_cuda(q, k, v, query_start_loc)
+    T, H, d = q.shape
+    for x in (q, k, v):
+        if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+            raise ValueError('chunk_attention takes bf16 q/k/v with a unit last-dim stride')
+    o = torch.empty(T, H, d, dtype=q.dtype, device=q.device)
+    lse = torch.empty(H, T, dtype=torch.float32, device=q.device)
+    _lib.call('hla_s6_chunk_attention', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(k), k.stride(0), k.stride(1),
+              _lib.ptr(v), v.stride(0), v.stride(1), _lib.ptr(query_start_loc), query_start_loc.shape[0] - 1, T, H, d,
+              float(scale), _lib.ptr(o), o.stride(0), o.stride(1), _lib.ptr(lse), _lib.stream_of(q))
+    return o, lse
+
+
 # ----------------------------------------------------------------------------- A7 merges
 def merge_states(o_hist, lse_hist, o_chunk, lse_chunk, invalid, backend):
     """LSE merge of two partial softmaxes; ``[T,H,D]`` outputs, ``[H,T]`` fp32 lse; ``invalid`` rows are

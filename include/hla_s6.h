@@ -108,6 +108,26 @@ int hla_s6_window_attention(const void* q, int64_t q_stride_t, int64_t q_stride_
                             int32_t num_tokens, int32_t num_heads, int32_t head_dim, void* out, int64_t out_stride_t,
                             int64_t out_stride_h, float* lse, void* stream);
 
+/* Exact window over history rows only, per token: token t reads rows [ctx[t] - window, ctx[t])
+ * through row t of a per-token block table (no current token; ctx[t] = 0 gives o = 0, lse = -inf).
+ * Used on prefill / mixed steps.  Replaces hla/vllm_latent/s6_ops.py:334 window_history_fa. */
+int hla_s6_window_history(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                          int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                          int64_t cache_stride_row, int32_t page, const int32_t* token_block_table,
+                          int64_t block_table_stride, int32_t max_blocks, const int32_t* ctx, int32_t window,
+                          float scale, int32_t num_tokens, int32_t num_heads, int32_t head_dim, void* out,
+                          int64_t out_stride_t, int64_t out_stride_h, float* lse, void* stream);
+
+/* Causal attention inside each request's current chunk (cu_seqlens = query_start_loc): token i
+ * attends to tokens j <= i of its request; padding tokens give o = 0, lse = -inf.  q/k/v
+ * [T, H, 128] with 16-byte aligned rows; out [T, H, 128]; lse [H, T].  Replaces
+ * hla/vllm_latent/s6_ops.py:234 chunk_attention (FA2 varlen causal; oracle :251-259). */
+int hla_s6_chunk_attention(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+                           int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
+                           int64_t v_stride_h, const int32_t* query_start_loc, int32_t num_reqs, int32_t num_tokens,
+                           int32_t num_heads, int32_t head_dim, float scale, void* out, int64_t out_stride_t,
+                           int64_t out_stride_h, float* lse, void* stream);
+
 /* LSE merge of two partial softmaxes: +inf lse counts as empty, both empty -> 0, invalid rows
  * zeroed.  Replaces s6_ops.py:262 merge_states (vLLM merge_attn_states; oracle :275-284). */
 int hla_s6_merge_states(const void* o_hist, int64_t hist_stride_t, int64_t hist_stride_h, const float* lse_hist,
@@ -210,6 +230,10 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
  * (merge_states semantics; invalid tokens zeroed).  out bf16 [T, H, 128]; lse_out (optional
  * [H, T]) receives the merged lse.  Replaces s6_layer.py:97-115 (window_attention_fa +
  * history stage 2 + einsum B + merge_states).
+ * chunk_o / chunk_lse (optional, bf16 [T, H, 128] and fp32 [H, T]): an exact part computed
+ * outside (prefill / mixed steps: hla_s6_chunk_attention merged with hla_s6_window_history),
+ * used instead of the decode window; the window arguments other than query_start_loc /
+ * num_reqs are then ignored (s6_layer.py:101-115, non-fused branch).
  * flags: HLA_S6_COMBINE_AFTER_PARTIALS declares that the immediately preceding launch on the
  * stream is the hla_s6_history_partials call that produced the partials; the combine is then
  * launched as a programmatic dependent of it, and its B prefetch and exact window (whose inputs
@@ -224,8 +248,9 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           int64_t exact_stride_head, int64_t exact_stride_row, int32_t exact_page,
                           const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
                           const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
-                          float scale, void* out, int64_t out_stride_t, int64_t out_stride_h, float* lse_out,
-                          int32_t flags, void* stream);
+                          float scale, const void* chunk_o, int64_t chunk_stride_t, int64_t chunk_stride_h,
+                          const float* chunk_lse, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                          float* lse_out, int32_t flags, void* stream);
 
 #ifdef __cplusplus
 }

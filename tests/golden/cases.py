@@ -127,6 +127,34 @@ def writer_case(seed=51, tokens=7, hidden=256, rank=512, rank1=256, loops=4, max
                 head_dim=np.int64(128), rank=np.int64(rank), rank1=np.int64(rank1))
 
 
+def chunk_case(seed=61, heads=16, d=128, qsl=(0, 37, 38, 50, 50, 91), num_tokens=94):
+    """Varlen causal chunk attention inputs (prefill 37, decode 1, prefill 12, a padded request,
+    prefill 41, three padding tokens) - the shape of test_s6_ops.py:105-120 at model widths."""
+    rng = np.random.default_rng(seed)
+    q, k, v = (_bf16(rng.standard_normal((num_tokens, heads, d), dtype=np.float32)) for _ in range(3))
+    return dict(q=q, k=k, v=v, query_start_loc=np.asarray(qsl, dtype=np.int32), num_tokens=np.int64(num_tokens))
+
+
+def window_history_case(seed=71, heads=16, d=128, page=16, window=32, ctx=(0, 5, 32, 33, 100, 0, 47)):
+    """Per-token exact window over history rows [ctx - W, ctx) (s6_ops.py:334-350 semantics)."""
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(ctx, dtype=np.int32)
+    T = ctx.shape[0]
+    need = -(-np.maximum(ctx, 1) // page)
+    mb = int(need.max()) + 1
+    nb = int(need.sum()) + 2
+    phys = _bf16(rng.standard_normal((nb, page, heads, 2 * d), dtype=np.float32))
+    phys[0] = INF
+    table = np.zeros((T, mb), dtype=np.int32)
+    free = rng.permutation(np.arange(1, nb)).astype(np.int32)
+    k = 0
+    for t in range(T):
+        table[t, :need[t]] = free[k:k + need[t]]
+        k += need[t]
+    q = _bf16(rng.standard_normal((T, heads, d), dtype=np.float32))
+    return dict(q=q, cache_phys=phys, block_table=table, ctx=ctx, window=np.int32(window))
+
+
 def meta_cases():
     """Integer metadata cases (test_s6_ops.py:16-27, 51-70)."""
     return dict(

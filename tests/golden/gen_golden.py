@@ -73,6 +73,19 @@ def main():
     lse = lse.masked_fill(invalid[None, :], -float('inf'))
     save('window_decode', w, o=o.numpy(), lse=lse.numpy(), scale=np.float64(scale))
 
+    # ---- A5 prefill pieces: causal chunk attention and the per-token window history
+    c = cases.chunk_case()
+    qsl = T_(c['query_start_loc'])
+    n = int(c['num_tokens'])
+    _, valid = s6_ops.token_requests(qsl, n)
+    o, lse = s6_ops.chunk_attention(T_(c['q']), T_(c['k']), T_(c['v']), qsl, 41, ~valid, 1 / math.sqrt(128), 'torch')
+    save('chunk', c, o=o.numpy(), lse=lse.numpy(), scale=np.float64(1 / math.sqrt(128)))
+    wh = cases.window_history_case()
+    logical = T_(wh['cache_phys']).transpose(1, 2)
+    o, lse = s6_ops.window_attention(T_(wh['q']), logical, T_(wh['block_table']), T_(wh['ctx']), int(wh['window']),
+                                     1 / math.sqrt(128))
+    save('window_history', wh, o=o.numpy(), lse=lse.numpy(), scale=np.float64(1 / math.sqrt(128)))
+
     # ---- A7 merges
     m = cases.merge_case()
     out = s6_ops.merge_states(T_(m['o_hist']), T_(m['lse_hist']), T_(m['o_chunk']), T_(m['lse_chunk']),
