@@ -31,6 +31,19 @@ __device__ __forceinline__ const int32_t* stage_qsl(const int32_t* __restrict__ 
   return buf;
 }
 
+// vLLM slot of token t at position pos: block_table[req, pos / page] * page + pos % page, or -1 for a
+// padding token, a negative position, a column past the table or a block id outside the cache.
+__device__ __forceinline__ int64_t token_slot(const int32_t* qsl, int R, int t, int64_t pos, const int32_t* bt,
+                                              int64_t bt_st, int max_blocks, int page, int64_t num_blocks) {
+  int r;
+  if (!token_request(qsl, R, t, r) || pos < 0) return -1;
+  const int64_t col = pos / page;
+  if (col >= max_blocks) return -1;
+  const int blk = bt[static_cast<int64_t>(r) * bt_st + col];
+  if (blk < 0 || blk >= num_blocks) return -1;
+  return static_cast<int64_t>(blk) * page + pos % page;
+}
+
 // Neox rotate-half pair (x1 at i, x2 at i + w/2) in the torch bf16 operation order:
 // y1 = bf16(bf16(x1*c) + bf16(-x2*s)), y2 = bf16(bf16(x2*c) + bf16(x1*s)).
 __device__ __forceinline__ void rope_pair_torch(float x1, float x2, float c, float s, float& y1, float& y2) {

@@ -18,17 +18,6 @@
 
 namespace hla {
 
-__device__ __forceinline__ int64_t token_slot(const int32_t* qsl, int R, int t, int64_t pos, const int32_t* bt,
-                                              int64_t bt_st, int max_blocks, int page, int64_t num_blocks) {
-  int r;
-  if (!token_request(qsl, R, t, r) || pos < 0) return -1;
-  const int64_t col = pos / page;
-  if (col >= max_blocks) return -1;
-  const int blk = bt[static_cast<int64_t>(r) * bt_st + col];
-  if (blk < 0 || blk >= num_blocks) return -1;
-  return static_cast<int64_t>(blk) * page + pos % page;
-}
-
 // -------------------------------------------------------------------- writer (+ commit)
 constexpr int kWKC = 128;     // k per stage
 constexpr int kWStages = 4;
@@ -141,6 +130,7 @@ __global__ void __launch_bounds__(128) writer_kernel(const WriterParams p) {
 
 int writer(const WriterParams& p, cudaStream_t s) {
   if (p.T == 0) return kStatusOk;
+  if (writer_tc_eligible(p)) return writer_tc(p, s);  // prefill-size: tcgen05 tiles
   const int smem = kWStages * (kWHBytes + kWEBytes);
   static unsigned attr_mask = 0;
   ensure_smem_limit(writer_kernel, smem, attr_mask);

@@ -27,6 +27,7 @@ struct WriterParams {
   int max_blocks;
   const int32_t* qsl;
   int R;
+  int* err;  // optional device error word (bounded waits of the tcgen05 path)
 };
 
 struct PrepareParams {
@@ -61,6 +62,8 @@ struct PrepareParams {
 };
 
 int writer(const WriterParams& p, cudaStream_t s);
+bool writer_tc_eligible(const WriterParams& p);  // writer_tc.cu
+int writer_tc(const WriterParams& p, cudaStream_t s);
 int prepare(const PrepareParams& p, cudaStream_t s);
 
 }  // namespace hla

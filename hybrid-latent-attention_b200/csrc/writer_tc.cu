@@ -1,0 +1,310 @@
+// Prefill-size writer on the 5th-generation tensor cores (tcgen05): the same operation as
+// writer_kernel in gemm_ops.cu - reg_out = bf16(reg_in + bf16(h . E^T)), optionally committed to
+// the latent cache with the K half latent-RoPE'd (register.py:45-79, s6_layer.py:124-147,
+// ouro_latent.py:127-129) - for many tokens (config 3: 8 x 4096 prompt tokens per loop), where the
+// GEMM (M = tokens, N = 1024 or 512, K = hidden) is tensor-bound.
+//
+// One CTA computes a 128 x 256 tile:
+//   warp 0      TMA producer (h tile 128 x 64, two 128 x 64 boxes of E per stage, SWIZZLE_128B),
+//               and owner of the TMEM allocation (256 fp32 columns = the accumulator)
+//   warp 1      a single thread issues tcgen05.mma (M = 128, N = 256, K = 16, bf16 -> fp32, both
+//               operands K-major from shared memory) and commits each stage back to the producer
+//   warps 2-5   epilogue: tcgen05.ld of its 32 TMEM lanes (= tile rows), bf16 rounding, the bf16
+//               register add, then either the register store or the committed-row scatter.
+// For a commit tile the two E boxes are rows [128j, 128j + 128) and [w/2 + 128j, ...), so the
+// accumulator columns c and c + 128 are a neox RoPE pair held by the same thread.
+// All mbarrier waits are bounded; a timeout records an error code and the CTA unwinds.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "decode_ops.cuh"
+#include "gemm_ops.cuh"
+#include "hla_s6_internal.h"
+
+namespace hla {
+
+constexpr int kTcM = 128, kTcN = 256, kTcK = 64, kTcStages = 4;
+constexpr int kTcABytes = kTcM * kTcK * 2;                 // 16 KB
+constexpr int kTcBBytes = kTcN * kTcK * 2;                 // 32 KB
+constexpr int kTcStageBytes = kTcABytes + kTcBBytes;       // 48 KB
+constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes + 256;
+constexpr int kTcThreads = 192;
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+  // K-major, SWIZZLE_128B canonical layout: rows of 128 B, 8-row groups 1024 B apart (SBO),
+  // LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B).
+  return static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// bf16 x bf16 -> fp32, K-major A and B, M = 128, N = 256.
+constexpr uint32_t kTcIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTcN >> 3) << 17) |
+                              (uint32_t(kTcM >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kTcIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 16 consecutive fp32 TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct TcParams {
+  WriterParams w;
+  int n_tiles;
+};
+
+// E rows of the two 128-row boxes of column tile j.
+__device__ __forceinline__ void tc_tile_rows(const WriterParams& p, int j, int& n_lo, int& n_hi) {
+  if (p.commit && j < p.w / 256) {
+    n_lo = 128 * j;
+    n_hi = p.w / 2 + 128 * j;
+  } else if (p.commit) {
+    n_lo = p.w + 256 * (j - p.w / 256);
+    n_hi = n_lo + 128;
+  } else {
+    n_lo = 256 * j;
+    n_hi = n_lo + 128;
+  }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    writer_tc_kernel(const __grid_constant__ CUtensorMap tmap_h, const __grid_constant__ CUtensorMap tmap_e,
+                     const TcParams tp) {
+  const WriterParams& p = tp.w;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
+  uint64_t* empty = full + kTcStages;
+  uint64_t* accum = empty + kTcStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kTcM, j = blockIdx.x;
+  const int NK = p.K / kTcK;
+  int n_lo, n_hi;
+  tc_tile_rows(p, j, n_lo, n_hi);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTcN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap_h);
+      prefetch_tmap(&tmap_e);
+      for (int kb = 0; kb < NK; ++kb) {
+        const int s = kb % kTcStages;
+        if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1)) {
+          record_error(p.err, kErrWaitEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* a = smem + s * kTcStageBytes;
+        uint8_t* b = a + kTcABytes;
+        mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+        tma_load_2d(a, &tmap_h, &full[s], kb * kTcK, m0);
+        tma_load_2d(b, &tmap_e, &full[s], kb * kTcK, n_lo);
+        tma_load_2d(b + kTcBBytes / 2, &tmap_e, &full[s], kb * kTcK, n_hi);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < NK && ok; ++kb) {
+        const int s = kb % kTcStages;
+        if (!mbar_wait(&full[s], (kb / kTcStages) & 1)) {
+          record_error(p.err, kErrWaitFull);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + s * kTcStageBytes), b = a + kTcABytes;
+#pragma unroll
+        for (int kk = 0; kk < kTcK / 16; ++kk)
+          tc_mma(tmem, umma_desc_sw128(a + kk * 32), umma_desc_sw128(b + kk * 32), (kb | kk) != 0);
+        tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      tc_commit(accum);  // accumulator complete (or, after a timeout, whatever was issued)
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2-5)
+    const int quarter = warp & 3;                 // TMEM lanes 32 * quarter .. + 31
+    const int row = quarter * 32 + lane;          // tile row
+    const int t = m0 + row;
+    const bool live = t < p.T;                    // rows past T only skip their stores
+    // tcgen05.ld / wait::ld are warp-collective (.sync.aligned): every lane of the warp executes them,
+    // so the wait result is made warp-uniform first
+    const bool done = __all_sync(0xffffffffu, mbar_wait(accum, 0));
+    tc_fence_after();
+    if (!done) {
+      record_error(p.err, kErrWaitFull);
+    } else {
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const bool pair_tile = p.commit && j < p.w / 256;
+      const __nv_bfloat16* tab = nullptr;
+      __nv_bfloat16* dst = nullptr;
+      if (p.commit && live) {
+        const int64_t pos = p.positions[t];
+        const int64_t slot = token_slot(p.qsl, p.R, t, pos, p.bt, p.bt_st, p.max_blocks, p.page, p.num_blocks);
+        if (slot >= 0) dst = p.cache + (slot / p.page) * p.c_sb + (slot % p.page) * p.c_sr;
+        tab = p.table + clamp_pos(pos, p.max_pos) * p.tab_st;
+      }
+      // 128 columns per half; 16 per TMEM load
+      for (int c0 = 0; c0 < 128; c0 += 16) {
+        float lo[16], hi[16];
+        tmem_ld16(tbase + c0, lo);
+        tmem_ld16(tbase + 128 + c0, hi);
+        if (!live) continue;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          lo[e] = bf16_round(lo[e]);
+          hi[e] = bf16_round(hi[e]);
+        }
+        const int clo = n_lo + c0, chi = n_hi + c0;  // global columns
+        if (p.reg_in) {
+          const __nv_bfloat16* r = p.reg_in + static_cast<int64_t>(t) * p.ri_st;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            lo[e] = bf16_round(__bfloat162float(r[clo + e]) + lo[e]);
+            hi[e] = bf16_round(__bfloat162float(r[chi + e]) + hi[e]);
+          }
+        }
+        if (p.reg_out) {
+          __nv_bfloat16* o = p.reg_out + static_cast<int64_t>(t) * p.ro_st;
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            *reinterpret_cast<__nv_bfloat162*>(o + clo + e) = __floats2bfloat162_rn(lo[e], lo[e + 1]);
+            *reinterpret_cast<__nv_bfloat162*>(o + chi + e) = __floats2bfloat162_rn(hi[e], hi[e + 1]);
+          }
+        }
+        if (dst) {
+          if (pair_tile) {
+            const int half_w = p.w / 2;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float y1, y2;
+              rope_pair_torch(lo[e], hi[e], __bfloat162float(tab[clo + e]), __bfloat162float(tab[half_w + clo + e]),
+                              y1, y2);
+              dst[clo + e] = __float2bfloat16_rn(y1);
+              dst[chi + e] = __float2bfloat16_rn(y2);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              *reinterpret_cast<__nv_bfloat162*>(dst + clo + e) = __floats2bfloat162_rn(lo[e], lo[e + 1]);
+              *reinterpret_cast<__nv_bfloat162*>(dst + chi + e) = __floats2bfloat162_rn(hi[e], hi[e + 1]);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcN));
+  }
+}
+
+// 2-D TMA map over a [rows, K] bf16 matrix with 128-row x 64-column boxes, SWIZZLE_128B.
+static int rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+      return kStatusCuda;
+    }
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcK), 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for the writer operands", static_cast<int>(r));
+    return kStatusCuda;
+  }
+  return kStatusOk;
+}
+
+// Whether writer() should use the tcgen05 path for this shape.
+bool writer_tc_eligible(const WriterParams& p) {
+  return p.T >= kTcM && p.N % kTcN == 0 && p.K % kTcK == 0 && (!p.commit || p.w % 256 == 0) &&
+         (reinterpret_cast<uintptr_t>(p.h) % 16) == 0 && (reinterpret_cast<uintptr_t>(p.E) % 16) == 0 &&
+         (p.h_st % 8) == 0 && (p.e_st % 8) == 0;
+}
+
+int writer_tc(const WriterParams& p, cudaStream_t s) {
+  CUtensorMap th, te;
+  int rc = rows_tmap(&th, p.h, p.T, p.K, p.h_st);
+  if (rc) return rc;
+  if ((rc = rows_tmap(&te, p.E, p.N, p.K, p.e_st))) return rc;
+  static unsigned attr_mask = 0;
+  ensure_smem_limit(writer_tc_kernel, kTcSmem, attr_mask);
+  TcParams tp;
+  tp.w = p;
+  tp.n_tiles = p.N / kTcN;
+  dim3 grid(p.N / kTcN, (p.T + kTcM - 1) / kTcM);
+  writer_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(th, te, tp);
+  return cuda_status(cudaGetLastError(), "writer_tc_kernel launch");
+}
+
+}  // namespace hla

@@ -259,12 +259,13 @@ def test_committed_row_in_place_matches_reference_fixture():
 
 
 # ----------------------------------------------------------------------------- fused entry points
+@pytest.mark.parametrize('T', [37, 300])          # 300 tokens: the tcgen05 path (3 M tiles, ragged tail)
 @pytest.mark.parametrize('loop', [0, 3])
-def test_writer_commit_equals_project_then_commit(loop):
+def test_writer_commit_equals_project_then_commit(loop, T):
     """The commit fused into the writer epilogue writes exactly the rows that the projection followed
     by the torch-order RoPE would (bit for bit), at exactly the vLLM slots; nothing else changes."""
-    rng = np.random.default_rng(loop + 7)
-    T, K, page, max_pos = 37, 256, 16, 4096
+    rng = np.random.default_rng(loop + 7 + T)
+    K, page, max_pos = 256, 16, 4096
     w = 256 if loop == 0 else 512
     N = 2 * w
     h = dev(orc.bf16(rng.standard_normal((T, K), dtype=np.float32)), BF16)
