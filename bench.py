@@ -1,6 +1,6 @@
 """Benchmark of the B200 S6 hybrid decode path (BASELINE config 2 by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
 
 One step = one decode step of an Ouro-1.4B-shaped S6 model's attention path: 24 layers x 4 loops
 of (writer projection, latent query, exact RoPE + window append, paged latent-history read,
@@ -15,6 +15,11 @@ copied host->device from pinned memory and its outputs read back, inside the tim
 roofline: the dominant kernel (history split) timed alone in a graph of its 96 launches.
 cpu_baseline / --impl reference: the CPU oracle (numpy fp32 restatement of the reference's
 torch path) on a bounded sample of the same workload, extrapolated to a step.
+
+--config 3 measures the latent writer of a prompt step instead (8 prompts x 4096 tokens, 24 layers x
+4 loops of writer GEMM + bf16 register add + committed-row RoPE and scatter, tcgen05): rows/s, with
+a tensor-pipe roofline; its e2e copies the four loops' hidden states in and one layer's latent
+cache out every step.
 """
 from __future__ import annotations
 
@@ -35,6 +40,8 @@ sys.path.insert(0, str(ROOT))
 PKG = 'hybrid-latent-attention_b200'
 FALLBACK_HBM_GBS = 6650.0
 METRIC = 'S6 decode tokens/s and latent-history HBM GB/s (% roofline), B=64 ctx 8K, 1/2/4/8 GPU'
+METRIC3 = 'S6 latent writer (prefill) committed rows/s and tensor TFLOP/s (% roofline), 8 x 4096 prompt tokens'
+FALLBACK_TFLOPS = 1400.0
 
 
 def dist_env():
@@ -75,6 +82,16 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d['hbm_gbs']), 'measured'
     return FALLBACK_HBM_GBS, 'fallback'
+
+
+def tensor_peak():
+    """Sustained bf16 dense TFLOP/s (a kernel timed inside a seconds-long loop)."""
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        if 'bf16_tflops_sustained' in d:
+            return float(d['bf16_tflops_sustained']), 'measured (MEASURED_PEAKS.json bf16_tflops_sustained)'
+    return FALLBACK_TFLOPS, 'fallback 1.4 PFLOP/s sustained'
 
 
 def ncu_traffic():
@@ -206,6 +223,49 @@ class CpuSample:
                 f'extrapolated x{s.layers} layers x (3+1) loops x {self.B}/{self.n}')
 
 
+class PrefillCpuSample:
+    """The oracle's writer of one layer (4 loops: fp32 GEMM rounded to bf16, bf16 register add, latent
+    RoPE of the committed K halves) on ``rows`` tokens of one prompt; ``run()`` times one pass and
+    extrapolates it to a step: layers x (T / rows) x the pass."""
+
+    def __init__(self, shape, T, rows, seed=0):
+        import numpy as np
+        from oracle import s6_oracle as orc
+        self.orc, self.np, self.shape, self.T, self.rows = orc, np, shape, T, rows
+        rng = np.random.default_rng(seed)
+        s = shape
+        self.h = [orc.bf16(rng.standard_normal((rows, s.hidden), dtype=np.float32)) for _ in range(s.loops)]
+        self.E = [orc.bf16(rng.standard_normal((2 * (s.rank1 if t == 0 else s.rank), s.hidden), dtype=np.float32)
+                           / math.sqrt(s.hidden)) for t in range(s.loops)]
+        self.pos = np.arange(rows)
+        inv = 1.0 / (s.theta ** (np.arange(0, s.head_dim, 2) / s.head_dim))
+        self.tab = {}
+        for w in (s.rank, s.rank1):
+            ang = self.pos[:, None] * inv[np.arange(w // 2) % inv.shape[0]][None]
+            self.tab[w] = orc.bf16(np.concatenate((np.cos(ang), np.sin(ang)), -1).astype(np.float32))
+        self.run()
+
+    def _layer(self):
+        orc, s = self.orc, self.shape
+        first = orc.bf16(self.h[0] @ self.E[0].T)
+        orc.committed_row(first, s.rank1, self.pos, self.tab[s.rank1])
+        reg = None
+        for t in range(1, s.loops):
+            reg = orc.write_step(reg, orc.bf16(self.h[t] @ self.E[t].T))
+        orc.committed_row(reg, s.rank, self.pos, self.tab[s.rank])
+
+    def run(self):
+        t0 = time.perf_counter()
+        self._layer()
+        return (time.perf_counter() - t0) * self.shape.layers * (self.T / self.rows)
+
+    def describe(self):
+        s = self.shape
+        return (f'oracle numpy fp32 writer of one layer (4 loops: GEMM -> bf16, bf16 register add, latent RoPE of '
+                f'the committed rows) on {self.rows} of {self.T} tokens, extrapolated x{s.layers} layers x '
+                f'{self.T}/{self.rows}')
+
+
 def cpu_threads():
     try:
         import threadpoolctl
@@ -233,6 +293,8 @@ def run_reference(args):
     dec = importlib.import_module(f'{PKG}.decode')
     shape = dec.OuroShape()
     use_all_host_threads()
+    if args.config == 3:
+        return run_reference_prefill(args, shape, world)
     ctx, scaling, _, _ = config_batch(args.config, 0, 1, args.seed)
     if scaling == 'weak':
         ctx = ctx * world          # the whole job's requests; tokens/s of the CPU path does not depend on B
@@ -253,6 +315,34 @@ def run_reference(args):
             'cpu_baseline': {'value': tok, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
                              'sample': desc},
             'e2e': {'value': tok, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def prefill_config(world):
+    return {'workload': 'BASELINE config 3: latent writer of a prompt step, 24 layers x 4 loops (GEMM + bf16 '
+                        'register add + committed-row latent RoPE and paged scatter)',
+            'global_batch': 8 * 4096 * world, 'prompts_per_gpu': 8, 'seq_len': 4096, 'hidden': 2048,
+            'parallelism': f'request-partitioned x{world} (no collectives)',
+            'l2': 'inputs larger than L2 (each loop reads a 128 MiB hidden-state matrix), no flush'}
+
+
+def run_reference_prefill(args, shape, world):
+    T = 8 * 4096
+    cs = PrefillCpuSample(shape, T, args.cpu_tokens, seed=args.seed)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        sec = cs.run()
+        if i >= args.warmup:
+            samples.append(sec)
+    sec = statistics.mean(samples)
+    rows = T * shape.layers / sec          # the CPU path's throughput does not depend on the job's size
+    line = {'metric': METRIC3, 'value': rows, 'unit': 'rows/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': sec * 1e3 * world, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded)', 'impl': 'reference',
+            'config': prefill_config(world),
+            'cpu_baseline': {'value': rows, 'unit': 'rows/s', 'cores': cpu_threads(), 'kind': 'port',
+                             'sample': cs.describe()},
+            'e2e': {'value': rows, 'unit': 'rows/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -408,22 +498,131 @@ def run_ours(args):
     return line
 
 
+def run_prefill(args):
+    """--config 3: the writer of a prompt step (8 x 4096 tokens per GPU, weak scaling)."""
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    importlib.import_module(f'{PKG}._lib').load()
+    dec = importlib.import_module(f'{PKG}.decode')
+    pre = importlib.import_module(f'{PKG}.prefill')
+    shape = dec.OuroShape()
+    model = pre.PrefillWriter(shape, 8, 4096, device='cuda', seed=args.seed + rank)
+    torch.cuda.synchronize()
+    model.step()
+    graph = model.capture()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms_total = time_graph(torch, graph, args.steps, dist)
+    clocks = clk.summary()
+    ms_step = ms_total / args.steps
+    rows_all = model.rows_per_step() * world
+    value = rows_all / (ms_step / 1e3)
+    flops = model.flops_per_step()
+    achieved = flops / (ms_step / 1e3) / 1e12
+    peak, peak_kind = tensor_peak()
+    traffic = None
+    tr = ncu_traffic()
+    if tr:
+        traffic = tr.get('writer_tc_avg_bytes_per_launch_config3')
+
+    # ---- e2e: the four loops' hidden states in from pinned memory, the last layer's main cache out
+    host_in = torch.empty(model.h.shape, dtype=model.h.dtype, pin_memory=True)
+    host_in.copy_(model.h)
+    out_dev = model.main[-1]
+    host_out = torch.empty(out_dev.shape, dtype=out_dev.dtype, pin_memory=True)
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        model.h.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(out_dev, non_blocking=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 4)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        model.h.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(out_dev, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([ms_e2e], device='cuda')
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = {'value': rows_all / (ms_e2e / 1e3), 'unit': 'rows/s',
+           'h2d_bytes_per_step': host_in.numel() * host_in.element_size(),
+           'd2h_bytes_per_step': host_out.numel() * host_out.element_size(),
+           'path': 'PrefillWriter CUDA-graph step (hla_s6_writer_project / hla_s6_writer_commit) with the hidden '
+                   'states copied in from pinned memory and one layer\'s latent cache read back'}
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            use_all_host_threads()
+            cs = PrefillCpuSample(shape, model.T, args.cpu_tokens, seed=args.seed)
+            secs = [cs.run() for _ in range(max(1, args.cpu_reps // 20))]
+            sec = statistics.median(secs)
+            cpu = {'value': model.rows_per_step() / sec, 'unit': 'rows/s', 'cores': cpu_threads(), 'kind': 'port',
+                   'sample': cs.describe() + f'; median of {len(secs)} timed passes'}
+        line = {
+            'metric': METRIC3, 'value': value, 'unit': 'rows/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded), random-init weights',
+            'config': prefill_config(world),
+            'writer': {'flops_per_step': flops, 'bytes_per_step': model.bytes_per_step(),
+                       'GBps_in_step': model.bytes_per_step() / (ms_step / 1e3) / 1e9},
+            'roofline': {'bound': 'tensor', 'kernel': 'writer_tc_kernel (96 launches per step, the whole step)',
+                         'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
+                         'peak_source': peak_kind, 'ms_per_launch': ms_step / model.launches_per_step(),
+                         'flops_per_launch': flops / model.launches_per_step(), 'traffic': traffic},
+            'cpu_baseline': cpu,
+            'e2e': e2e,
+            'gpu_launches': model.launches_per_step() * args.steps,
+            'clocks': clocks,
+        }
+        print(json.dumps(line), flush=True)
+    model.graph = None
+    del graph
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', type=int, default=2, choices=[2, 4, 5])
+    ap.add_argument('--config', type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
     ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')
+    ap.add_argument('--cpu-tokens', type=int, default=4096, help='tokens of the config-3 CPU oracle sample')
     ap.add_argument('--no-cpu', action='store_true', help='skip the CPU baseline leg')
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
     if args.impl == 'reference':
         run_reference(args)
+    elif args.config == 3:
+        run_prefill(args)
     else:
         run_ours(args)
 

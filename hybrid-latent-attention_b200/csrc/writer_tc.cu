@@ -4,13 +4,15 @@
 // ouro_latent.py:127-129) - for many tokens (config 3: 8 x 4096 prompt tokens per loop), where the
 // GEMM (M = tokens, N = 1024 or 512, K = hidden) is tensor-bound.
 //
-// One CTA computes a 128 x 256 tile:
-//   warp 0      TMA producer (h tile 128 x 64, two 128 x 64 boxes of E per stage, SWIZZLE_128B),
-//               and owner of the TMEM allocation (256 fp32 columns = the accumulator)
+// One persistent CTA per SM walks 128 x 256 output tiles:
+//   warp 0      TMA producer (h tile 128 x 64, two 128 x 64 boxes of E per stage, SWIZZLE_128B, a
+//               4-stage ring that runs across tiles), and owner of the TMEM allocation (2 x 256 fp32
+//               columns: two accumulators, so one tile's epilogue overlaps the next tile's MMAs)
 //   warp 1      a single thread issues tcgen05.mma (M = 128, N = 256, K = 16, bf16 -> fp32, both
 //               operands K-major from shared memory) and commits each stage back to the producer
 //   warps 2-5   epilogue: tcgen05.ld of its 32 TMEM lanes (= tile rows), bf16 rounding, the bf16
-//               register add, then either the register store or the committed-row scatter.
+//               register add, then the register store and/or the committed-row scatter, with
+//               16-byte vector accesses.
 // For a commit tile the two E boxes are rows [128j, 128j + 128) and [w/2 + 128j, ...), so the
 // accumulator columns c and c + 128 are a neox RoPE pair held by the same thread.
 // All mbarrier waits are bounded; a timeout records an error code and the CTA unwinds.
@@ -68,22 +70,38 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
-// 16 consecutive fp32 TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
+// 16 consecutive fp32 TMEM columns of this thread's lane (no wait; see tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 8 bf16 <-> 8 floats through one 16-byte access.
+__device__ __forceinline__ void load8(const __nv_bfloat16* src, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(b[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* dst, const float* v) {
+  uint4 u;
+  __nv_bfloat162* b = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) b[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(dst) = u;
 }
 
 struct TcParams {
   WriterParams w;
-  int n_tiles;
+  int n_tiles, m_tiles;
 };
 
 // E rows of the two 128-row boxes of column tile j.
@@ -100,6 +118,78 @@ __device__ __forceinline__ void tc_tile_rows(const WriterParams& p, int j, int& 
   }
 }
 
+// Epilogue of one 128 x 256 tile for this thread's row: 16 + 16 columns (c0 of both halves) at a time.
+__device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t tacc, int t, bool live, int j, int n_lo,
+                                              int n_hi) {
+  const bool pair_tile = p.commit && j < p.w / 256;
+  const __nv_bfloat16* tab = nullptr;
+  __nv_bfloat16* dst = nullptr;
+  if (p.commit && live) {
+    const int64_t pos = p.positions[t];
+    const int64_t slot = token_slot(p.qsl, p.R, t, pos, p.bt, p.bt_st, p.max_blocks, p.page, p.num_blocks);
+    if (slot >= 0) dst = p.cache + (slot / p.page) * p.c_sb + (slot % p.page) * p.c_sr;
+    tab = p.table + clamp_pos(pos, p.max_pos) * p.tab_st;
+  }
+  const __nv_bfloat16* rin = (p.reg_in && live) ? p.reg_in + static_cast<int64_t>(t) * p.ri_st : nullptr;
+  __nv_bfloat16* rout = (p.reg_out && live) ? p.reg_out + static_cast<int64_t>(t) * p.ro_st : nullptr;
+  for (int c0 = 0; c0 < 128; c0 += 16) {
+    uint32_t rl[16], rh[16];
+    tmem_ld16(tacc + c0, rl);  // warp-collective: every lane, live or not
+    tmem_ld16(tacc + 128 + c0, rh);
+    tmem_wait_ld();
+    if (!live) continue;
+    float lo[16], hi[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      lo[e] = bf16_round(__uint_as_float(rl[e]));
+      hi[e] = bf16_round(__uint_as_float(rh[e]));
+    }
+    const int clo = n_lo + c0, chi = n_hi + c0;  // global columns
+    if (rin) {
+      float a[16], b[16];
+      load8(rin + clo, a);
+      load8(rin + clo + 8, a + 8);
+      load8(rin + chi, b);
+      load8(rin + chi + 8, b + 8);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        lo[e] = bf16_round(a[e] + lo[e]);
+        hi[e] = bf16_round(b[e] + hi[e]);
+      }
+    }
+    if (rout) {
+      store8(rout + clo, lo);
+      store8(rout + clo + 8, lo + 8);
+      store8(rout + chi, hi);
+      store8(rout + chi + 8, hi + 8);
+    }
+    if (dst) {
+      if (pair_tile) {
+        float cs[16], sn[16];
+        load8(tab + clo, cs);
+        load8(tab + clo + 8, cs + 8);
+        load8(tab + p.w / 2 + clo, sn);
+        load8(tab + p.w / 2 + clo + 8, sn + 8);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float y1, y2;
+          rope_pair_torch(lo[e], hi[e], cs[e], sn[e], y1, y2);
+          lo[e] = y1;
+          hi[e] = y2;
+        }
+      }
+      store8(dst + clo, lo);
+      store8(dst + clo + 8, lo + 8);
+      store8(dst + chi, hi);
+      store8(dst + chi + 8, hi + 8);
+    }
+  }
+}
+
+// Persistent: CTA b takes tiles b, b + grid, ... in (m, j) order with j fastest (the four column tiles
+// of a row block run back to back and share its h tile through L2).  The smem ring runs across tile
+// boundaries; TMEM holds two 256-column accumulators so the epilogue of one tile overlaps the
+// main loop of the next.
 __global__ void __launch_bounds__(kTcThreads, 1)
     writer_tc_kernel(const __grid_constant__ CUtensorMap tmap_h, const __grid_constant__ CUtensorMap tmap_e,
                      const TcParams tp) {
@@ -108,19 +198,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
   uint64_t* empty = full + kTcStages;
-  uint64_t* accum = empty + kTcStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  uint64_t* tfull = empty + kTcStages;  // [2] accumulator ready (tcgen05.commit)
+  uint64_t* tempty = tfull + 2;         // [2] accumulator drained (one arrive per epilogue warp)
+  uint64_t* drained = tempty + 2;       // every issued MMA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kTcM, j = blockIdx.x;
   const int NK = p.K / kTcK;
-  int n_lo, n_hi;
-  tc_tile_rows(p, j, n_lo, n_hi);
+  const int num_tiles = tp.n_tiles * tp.m_tiles;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTcN));
+                 "r"(2 * kTcN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (threadIdx.x == 32) {
@@ -128,8 +217,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
-    *abort_flag = 0;
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drained, 1);
     fence_barrier_init();
   }
   tc_fence_before();
@@ -142,119 +234,92 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&tmap_h);
       prefetch_tmap(&tmap_e);
-      for (int kb = 0; kb < NK; ++kb) {
-        const int s = kb % kTcStages;
-        if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1)) {
-          record_error(p.err, kErrWaitEmpty);
-          *abort_flag = 1;
-          break;
+      uint32_t g = 0;  // k-blocks issued so far (ring position)
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / tp.n_tiles) * kTcM, j = tile % tp.n_tiles;
+        int n_lo, n_hi;
+        tc_tile_rows(p, j, n_lo, n_hi);
+        for (int kb = 0; kb < NK; ++kb, ++g) {
+          const int s = g % kTcStages;
+          if (g >= kTcStages && !mbar_wait(&empty[s], ((g / kTcStages) - 1) & 1)) {
+            record_error(p.err, kErrWaitEmpty);
+            ok = false;
+            break;
+          }
+          uint8_t* a = smem + s * kTcStageBytes;
+          uint8_t* b = a + kTcABytes;
+          mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+          tma_load_2d(a, &tmap_h, &full[s], kb * kTcK, m0);
+          tma_load_2d(b, &tmap_e, &full[s], kb * kTcK, n_lo);
+          tma_load_2d(b + kTcBBytes / 2, &tmap_e, &full[s], kb * kTcK, n_hi);
         }
-        uint8_t* a = smem + s * kTcStageBytes;
-        uint8_t* b = a + kTcABytes;
-        mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-        tma_load_2d(a, &tmap_h, &full[s], kb * kTcK, m0);
-        tma_load_2d(b, &tmap_e, &full[s], kb * kTcK, n_lo);
-        tma_load_2d(b + kTcBBytes / 2, &tmap_e, &full[s], kb * kTcK, n_hi);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
+      uint32_t g = 0;
       bool ok = true;
-      for (int kb = 0; kb < NK && ok; ++kb) {
-        const int s = kb % kTcStages;
-        if (!mbar_wait(&full[s], (kb / kTcStages) & 1)) {
-          record_error(p.err, kErrWaitFull);
-          ok = false;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int b = it & 1;
+        if (it >= 2 && !mbar_wait(&tempty[b], ((it >> 1) - 1) & 1)) {
+          record_error(p.err, kErrWaitEmpty);
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_u32(smem + s * kTcStageBytes), b = a + kTcABytes;
+        const uint32_t d = tmem + b * kTcN;
+        for (int kb = 0; kb < NK; ++kb, ++g) {
+          const int s = g % kTcStages;
+          if (!mbar_wait(&full[s], (g / kTcStages) & 1)) {
+            record_error(p.err, kErrWaitFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * kTcStageBytes), bb = a + kTcABytes;
 #pragma unroll
-        for (int kk = 0; kk < kTcK / 16; ++kk)
-          tc_mma(tmem, umma_desc_sw128(a + kk * 32), umma_desc_sw128(b + kk * 32), (kb | kk) != 0);
-        tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+          for (int kk = 0; kk < kTcK / 16; ++kk)
+            tc_mma(d, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), (kb | kk) != 0);
+          tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        tc_commit(&tfull[b]);  // accumulator b complete (after a timeout: whatever was issued)
       }
-      tc_commit(accum);  // accumulator complete (or, after a timeout, whatever was issued)
+      // nothing may still write TMEM when it is released
+      tc_commit(drained);
+      if (!mbar_wait(drained, 0)) record_error(p.err, kErrWaitFull);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2-5)
-    const int quarter = warp & 3;                 // TMEM lanes 32 * quarter .. + 31
-    const int row = quarter * 32 + lane;          // tile row
-    const int t = m0 + row;
-    const bool live = t < p.T;                    // rows past T only skip their stores
-    // tcgen05.ld / wait::ld are warp-collective (.sync.aligned): every lane of the warp executes them,
-    // so the wait result is made warp-uniform first
-    const bool done = __all_sync(0xffffffffu, mbar_wait(accum, 0));
-    tc_fence_after();
-    if (!done) {
-      record_error(p.err, kErrWaitFull);
-    } else {
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-      const bool pair_tile = p.commit && j < p.w / 256;
-      const __nv_bfloat16* tab = nullptr;
-      __nv_bfloat16* dst = nullptr;
-      if (p.commit && live) {
-        const int64_t pos = p.positions[t];
-        const int64_t slot = token_slot(p.qsl, p.R, t, pos, p.bt, p.bt_st, p.max_blocks, p.page, p.num_blocks);
-        if (slot >= 0) dst = p.cache + (slot / p.page) * p.c_sb + (slot % p.page) * p.c_sr;
-        tab = p.table + clamp_pos(pos, p.max_pos) * p.tab_st;
+    const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. + 31 (a warp reaches only its quarter)
+    const int row = quarter * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int b = it & 1;
+      const int m0 = (tile / tp.n_tiles) * kTcM, j = tile % tp.n_tiles;
+      // tcgen05.ld / wait::ld are warp-collective (.sync.aligned): the wait result is made warp-uniform
+      // and every lane runs the loads; rows past T only skip their global accesses
+      const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1));
+      tc_fence_after();
+      if (!done) {
+        record_error(p.err, kErrWaitFull);
+        break;
       }
-      // 128 columns per half; 16 per TMEM load
-      for (int c0 = 0; c0 < 128; c0 += 16) {
-        float lo[16], hi[16];
-        tmem_ld16(tbase + c0, lo);
-        tmem_ld16(tbase + 128 + c0, hi);
-        if (!live) continue;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          lo[e] = bf16_round(lo[e]);
-          hi[e] = bf16_round(hi[e]);
-        }
-        const int clo = n_lo + c0, chi = n_hi + c0;  // global columns
-        if (p.reg_in) {
-          const __nv_bfloat16* r = p.reg_in + static_cast<int64_t>(t) * p.ri_st;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            lo[e] = bf16_round(__bfloat162float(r[clo + e]) + lo[e]);
-            hi[e] = bf16_round(__bfloat162float(r[chi + e]) + hi[e]);
-          }
-        }
-        if (p.reg_out) {
-          __nv_bfloat16* o = p.reg_out + static_cast<int64_t>(t) * p.ro_st;
-#pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            *reinterpret_cast<__nv_bfloat162*>(o + clo + e) = __floats2bfloat162_rn(lo[e], lo[e + 1]);
-            *reinterpret_cast<__nv_bfloat162*>(o + chi + e) = __floats2bfloat162_rn(hi[e], hi[e + 1]);
-          }
-        }
-        if (dst) {
-          if (pair_tile) {
-            const int half_w = p.w / 2;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              float y1, y2;
-              rope_pair_torch(lo[e], hi[e], __bfloat162float(tab[clo + e]), __bfloat162float(tab[half_w + clo + e]),
-                              y1, y2);
-              dst[clo + e] = __float2bfloat16_rn(y1);
-              dst[chi + e] = __float2bfloat16_rn(y2);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              *reinterpret_cast<__nv_bfloat162*>(dst + clo + e) = __floats2bfloat162_rn(lo[e], lo[e + 1]);
-              *reinterpret_cast<__nv_bfloat162*>(dst + chi + e) = __floats2bfloat162_rn(hi[e], hi[e + 1]);
-            }
-          }
-        }
-      }
+      int n_lo, n_hi;
+      tc_tile_rows(p, j, n_lo, n_hi);
+      const int t = m0 + row;
+      tc_store_tile(p, tmem + b * kTcN + (static_cast<uint32_t>(quarter * 32) << 16), t, t < p.T, j, n_lo, n_hi);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTcN));
   }
 }
 
@@ -287,9 +352,12 @@ static int rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t c
 
 // Whether writer() should use the tcgen05 path for this shape.
 bool writer_tc_eligible(const WriterParams& p) {
-  return p.T >= kTcM && p.N % kTcN == 0 && p.K % kTcK == 0 && (!p.commit || p.w % 256 == 0) &&
-         (reinterpret_cast<uintptr_t>(p.h) % 16) == 0 && (reinterpret_cast<uintptr_t>(p.E) % 16) == 0 &&
-         (p.h_st % 8) == 0 && (p.e_st % 8) == 0;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) % 16) == 0; };
+  // TMA operands: 16-byte aligned bases and row strides; epilogue: 16-byte vector accesses
+  return p.T >= kTcM && p.N % kTcN == 0 && p.K % kTcK == 0 && (!p.commit || p.w % 256 == 0) && a16(p.h) &&
+         a16(p.E) && (p.h_st % 8) == 0 && (p.e_st % 8) == 0 && a16(p.reg_in) && (p.ri_st % 8) == 0 &&
+         a16(p.reg_out) && (p.ro_st % 8) == 0 &&
+         (!p.commit || (a16(p.cache) && a16(p.table) && p.c_sb % 8 == 0 && p.c_sr % 8 == 0 && p.tab_st % 8 == 0));
 }
 
 int writer_tc(const WriterParams& p, cudaStream_t s) {
@@ -302,8 +370,14 @@ int writer_tc(const WriterParams& p, cudaStream_t s) {
   TcParams tp;
   tp.w = p;
   tp.n_tiles = p.N / kTcN;
-  dim3 grid(p.N / kTcN, (p.T + kTcM - 1) / kTcM);
-  writer_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(th, te, tp);
+  tp.m_tiles = (p.T + kTcM - 1) / kTcM;
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+  const int tiles = tp.n_tiles * tp.m_tiles;
+  writer_tc_kernel<<<tiles < nsm ? tiles : nsm, kTcThreads, kTcSmem, s>>>(th, te, tp);
   return cuda_status(cudaGetLastError(), "writer_tc_kernel launch");
 }
 

@@ -1,0 +1,54 @@
+"""The config-3 prompt-step writer (PrefillWriter, 4 loops per layer through the tcgen05 writer) against
+the oracle: every token's committed main and loop-1 rows at its vLLM slot (reference s6_layer.py:124-147,
+register.py:45-79), nothing else written.  GPU."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import pkg
+from oracle import s6_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize('prompts,prompt_len', [(2, 300), (3, 1000)])
+def test_prefill_writer_rows_match_oracle(prompts, prompt_len):
+    dec, pre = pkg('decode'), pkg('prefill')
+    shape = dec.OuroShape(layers=2, max_position=4096)
+    m = pre.PrefillWriter(shape, prompts, prompt_len, device='cuda', seed=3)
+    m.step()
+    torch.cuda.synchronize()
+    pos = m.positions.cpu().numpy()
+    req = np.repeat(np.arange(prompts), prompt_len)
+    bt = m.block_table.cpu().numpy()
+    slots = bt[req, pos // shape.page].astype(np.int64) * shape.page + pos % shape.page
+    h = [m.h[t].float().cpu().numpy() for t in range(shape.loops)]
+    for layer in range(shape.layers):
+        lat = m.layers[layer]
+        E = [lat.writer(t).float().cpu().numpy() for t in range(shape.loops)]
+        first = orc.write_update(h[0], E[0])
+        reg = None
+        for t in range(1, shape.loops):
+            reg = orc.write_step(reg, orc.write_update(h[t], E[t]))
+        for cache, row, width in ((m.l1[layer], first, shape.rank1), (m.main[layer], reg, shape.rank)):
+            table = m.tables[width].float().cpu().numpy()
+            expect = orc.committed_row(row, width, pos, table)
+            flat = cache.view(-1, 2 * width).float().cpu().numpy()
+            # bf16 GEMM tolerance (fp32 tensor-core accumulation vs one rounding of the exact product)
+            np.testing.assert_allclose(flat[slots], expect, atol=3e-2, rtol=1e-2)
+            rest = np.ones(flat.shape[0], dtype=bool)
+            rest[slots] = False
+            assert np.isinf(flat[rest]).all()
+
+
+def test_prefill_writer_graph_replay_is_deterministic():
+    dec, pre = pkg('decode'), pkg('prefill')
+    m = pre.PrefillWriter(dec.OuroShape(layers=2, max_position=4096), 2, 512, device='cuda', seed=5)
+    m.step()
+    torch.cuda.synchronize()
+    before = [c.clone() for c in (*m.main, *m.l1)]
+    g = m.capture()
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(before, (*m.main, *m.l1)):
+        assert torch.equal(a, b)
