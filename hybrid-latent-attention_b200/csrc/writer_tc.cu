@@ -118,20 +118,66 @@ __device__ __forceinline__ void tc_tile_rows(const WriterParams& p, int j, int& 
   }
 }
 
-// Epilogue of one 128 x 256 tile for this thread's row: 16 + 16 columns (c0 of both halves) at a time.
-__device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t tacc, int t, bool live, int j, int n_lo,
-                                              int n_hi) {
-  const bool pair_tile = p.commit && j < p.w / 256;
-  const __nv_bfloat16* tab = nullptr;
-  __nv_bfloat16* dst = nullptr;
-  if (p.commit && live) {
+// Everything a thread's row of a tile needs besides the accumulator, fetched before the accumulator
+// is ready so that the loads' latency hides under the tile's MMAs: the running register's values (both
+// 128-column halves), the committed row's address (the slot lookup is a chain of dependent loads),
+// and the first half of the RoPE cos / sin for a pair tile (the second half is loaded mid-tile).
+struct TileIn {
+  uint4 lo[16], hi[16];   // reg_in
+  uint4 cs[4], sn[4];     // cos / sin of 32 pairs (the table half in flight)
+  const __nv_bfloat16* tab;
+  __nv_bfloat16* dst;
+  __nv_bfloat16* rout;
+};
+
+__device__ __forceinline__ void tc_load_rope(const TileIn& in, int col, uint4* cs, uint4* sn, int half_w) {
+  const uint4* c = reinterpret_cast<const uint4*>(in.tab + col);
+  const uint4* s = reinterpret_cast<const uint4*>(in.tab + half_w + col);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    cs[i] = c[i];
+    sn[i] = s[i];
+  }
+}
+
+__device__ __forceinline__ void tc_tile_prefetch(const WriterParams& p, int t, bool live, bool pair_tile, int n_lo,
+                                                 int n_hi, TileIn& in) {
+  in.tab = nullptr;
+  in.dst = nullptr;
+  in.rout = (p.reg_out && live) ? p.reg_out + static_cast<int64_t>(t) * p.ro_st : nullptr;
+  if (!live) return;
+  if (p.reg_in) {
+    const uint4* a = reinterpret_cast<const uint4*>(p.reg_in + static_cast<int64_t>(t) * p.ri_st + n_lo);
+    const uint4* b = reinterpret_cast<const uint4*>(p.reg_in + static_cast<int64_t>(t) * p.ri_st + n_hi);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      in.lo[i] = a[i];
+      in.hi[i] = b[i];
+    }
+  }
+  if (p.commit) {
     const int64_t pos = p.positions[t];
     const int64_t slot = token_slot(p.qsl, p.R, t, pos, p.bt, p.bt_st, p.max_blocks, p.page, p.num_blocks);
-    if (slot >= 0) dst = p.cache + (slot / p.page) * p.c_sb + (slot % p.page) * p.c_sr;
-    tab = p.table + clamp_pos(pos, p.max_pos) * p.tab_st;
+    if (slot >= 0) in.dst = p.cache + (slot / p.page) * p.c_sb + (slot % p.page) * p.c_sr;
+    in.tab = p.table + clamp_pos(pos, p.max_pos) * p.tab_st;
+    if (pair_tile && in.dst) tc_load_rope(in, n_lo, in.cs, in.sn, p.w / 2);
   }
-  const __nv_bfloat16* rin = (p.reg_in && live) ? p.reg_in + static_cast<int64_t>(t) * p.ri_st : nullptr;
-  __nv_bfloat16* rout = (p.reg_out && live) ? p.reg_out + static_cast<int64_t>(t) * p.ro_st : nullptr;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(b[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Epilogue of one 128 x 256 tile for this thread's row: 16 + 16 columns (c0 of both halves) at a time.
+__device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t tacc, bool live, bool pair_tile, int n_lo,
+                                              int n_hi, TileIn& in) {
+#pragma unroll
   for (int c0 = 0; c0 < 128; c0 += 16) {
     uint32_t rl[16], rh[16];
     tmem_ld16(tacc + c0, rl);  // warp-collective: every lane, live or not
@@ -145,31 +191,35 @@ __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t ta
       hi[e] = bf16_round(__uint_as_float(rh[e]));
     }
     const int clo = n_lo + c0, chi = n_hi + c0;  // global columns
-    if (rin) {
+    if (p.reg_in) {
       float a[16], b[16];
-      load8(rin + clo, a);
-      load8(rin + clo + 8, a + 8);
-      load8(rin + chi, b);
-      load8(rin + chi + 8, b + 8);
+      unpack8(in.lo[c0 / 8], a);
+      unpack8(in.lo[c0 / 8 + 1], a + 8);
+      unpack8(in.hi[c0 / 8], b);
+      unpack8(in.hi[c0 / 8 + 1], b + 8);
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         lo[e] = bf16_round(a[e] + lo[e]);
         hi[e] = bf16_round(b[e] + hi[e]);
       }
     }
-    if (rout) {
-      store8(rout + clo, lo);
-      store8(rout + clo + 8, lo + 8);
-      store8(rout + chi, hi);
-      store8(rout + chi + 8, hi + 8);
+    if (in.rout) {
+      store8(in.rout + clo, lo);
+      store8(in.rout + clo + 8, lo + 8);
+      store8(in.rout + chi, hi);
+      store8(in.rout + chi + 8, hi + 8);
     }
-    if (dst) {
+    if (in.dst) {
       if (pair_tile) {
+        // cos / sin of pairs [c0, c0 + 16) sit in slots (c0 % 32) / 8 .. + 1 of the half in flight;
+        // the next 32 pairs are fetched once this half's last chunk has them unpacked
         float cs[16], sn[16];
-        load8(tab + clo, cs);
-        load8(tab + clo + 8, cs + 8);
-        load8(tab + p.w / 2 + clo, sn);
-        load8(tab + p.w / 2 + clo + 8, sn + 8);
+        const int q = (c0 % 32) / 8;
+        unpack8(in.cs[q], cs);
+        unpack8(in.cs[q + 1], cs + 8);
+        unpack8(in.sn[q], sn);
+        unpack8(in.sn[q + 1], sn + 8);
+        if (c0 % 32 == 16 && c0 + 16 < 128) tc_load_rope(in, n_lo + c0 + 16, in.cs, in.sn, p.w / 2);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           float y1, y2;
@@ -178,10 +228,10 @@ __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t ta
           hi[e] = y2;
         }
       }
-      store8(dst + clo, lo);
-      store8(dst + clo + 8, lo + 8);
-      store8(dst + chi, hi);
-      store8(dst + chi + 8, hi + 8);
+      store8(in.dst + clo, lo);
+      store8(in.dst + clo + 8, lo + 8);
+      store8(in.dst + chi, hi);
+      store8(in.dst + chi + 8, hi + 8);
     }
   }
 }
@@ -298,6 +348,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int b = it & 1;
       const int m0 = (tile / tp.n_tiles) * kTcM, j = tile % tp.n_tiles;
+      int n_lo, n_hi;
+      tc_tile_rows(p, j, n_lo, n_hi);
+      const int t = m0 + row;
+      const bool pair_tile = p.commit && j < p.w / 256;
+      TileIn in;
+      tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in);
       // tcgen05.ld / wait::ld are warp-collective (.sync.aligned): the wait result is made warp-uniform
       // and every lane runs the loads; rows past T only skip their global accesses
       const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1));
@@ -306,10 +362,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         record_error(p.err, kErrWaitFull);
         break;
       }
-      int n_lo, n_hi;
-      tc_tile_rows(p, j, n_lo, n_hi);
-      const int t = m0 + row;
-      tc_store_tile(p, tmem + b * kTcN + (static_cast<uint32_t>(quarter * 32) << 16), t, t < p.T, j, n_lo, n_hi);
+      tc_store_tile(p, tmem + b * kTcN + (static_cast<uint32_t>(quarter * 32) << 16), t < p.T, pair_tile, n_lo, n_hi,
+                    in);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);

@@ -1,11 +1,16 @@
 """Run eager S6 decode steps of an Ouro-shaped model - a small, self-contained workload for profilers.
 
     python hybrid-latent-attention_b200/profile_step.py [--layers 2] [--batch 64] [--ctx 8192] [--steps 2]
+    python hybrid-latent-attention_b200/profile_step.py --prefill [--layers 1] [--prompts 8] [--steps 1]
 
 Every step issues the four launches per (layer, loop) of ``decode.S6DecodeModel.step`` in order
 (writer, prepare, history split, combine; loop 0 reads the 256-wide latent, loops 1-3 the 512-wide
 one), so ``ncu -k regex:history_split -s 1 -c 2`` selects one launch of each width.  With the
 defaults the device holds about 3 GB.
+
+``--prefill`` runs eager steps of the config-3 prompt-step writer instead (prefill.PrefillWriter: four
+writer launches per layer, N = 512 at loop 0 and 1024 at loops 1-3, 4096 tokens per prompt); with one
+layer and 8 prompts the device holds about 1 GB, the hidden states of a loop (128 MiB) exceed L2.
 """
 import argparse
 import importlib
@@ -21,9 +26,19 @@ def main():
     ap.add_argument('--batch', type=int, default=64)
     ap.add_argument('--ctx', type=int, default=8192)
     ap.add_argument('--steps', type=int, default=2)
+    ap.add_argument('--prefill', action='store_true')
+    ap.add_argument('--prompts', type=int, default=8)
     args = ap.parse_args()
     import torch
     dec = importlib.import_module('hybrid-latent-attention_b200.decode')
+    if args.prefill:
+        pre = importlib.import_module('hybrid-latent-attention_b200.prefill')
+        model = pre.PrefillWriter(dec.OuroShape(layers=args.layers), args.prompts, 4096, device='cuda', seed=0)
+        for _ in range(args.steps):
+            model.step()
+        torch.cuda.synchronize()
+        print(f'ok: {args.steps} prefill steps, {model.launches_per_step()} launches each')
+        return
     model = dec.S6DecodeModel(dec.OuroShape(layers=args.layers), dec.DecodeBatch([args.ctx] * args.batch),
                               device='cuda', seed=0)
     for _ in range(args.steps):
