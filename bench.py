@@ -583,7 +583,7 @@ def run_prefill(args):
             'config': prefill_config(world),
             'writer': {'flops_per_step': flops, 'bytes_per_step': model.bytes_per_step(),
                        'GBps_in_step': model.bytes_per_step() / (ms_step / 1e3) / 1e9},
-            'roofline': {'bound': 'tensor', 'kernel': 'writer_tc_kernel (96 launches per step, the whole step)',
+            'roofline': {'bound': 'tensor', 'kernel': 'writer_tc2_kernel (CTA-pair tcgen05 GEMM + epilogue; 96 launches per step, the whole step)',
                          'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
                          'peak_source': peak_kind, 'ms_per_launch': ms_step / model.launches_per_step(),
                          'flops_per_launch': flops / model.launches_per_step(), 'traffic': traffic},

@@ -377,6 +377,240 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Pair version (cta_group::2): a cluster of two CTAs on two SMs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256).  CTA r of the pair stages rows [128 r, 128 r + 128)
+// of the h tile and ONE of the two 128-row E boxes (r = 0: n_lo, r = 1: n_hi) - half the operand
+// bytes per output that the single-CTA tile moves - and holds rows 128 r .. + 127 of the
+// accumulator in its own TMEM, all 256 columns (columns 0-127 from E box n_lo, 128-255 from n_hi,
+// as in the single-CTA tile).  The leader (rank 0) issues the MMAs; both CTAs' TMA loads complete
+// on the leader's full barrier; the MMA commits arrive on both CTAs' empty / tfull barriers; both
+// CTAs' epilogue warps release an accumulator on the leader's tempty barrier.  Each TMA load writes
+// only its own CTA's shared memory.
+constexpr int kT2Stages = 6;
+constexpr int kT2ABytes = 128 * kTcK * 2;                  // 16 KB (this CTA's h rows)
+constexpr int kT2BBytes = 128 * kTcK * 2;                  // 16 KB (this CTA's E box)
+constexpr int kT2StageBytes = kT2ABytes + kT2BBytes;       // 32 KB
+constexpr int kT2Smem = 1024 + kT2Stages * kT2StageBytes + 256;
+// bf16 x bf16 -> fp32, K-major A and B, M = 256 (the pair), N = 256.
+constexpr uint32_t kT2Idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(256 >> 3) << 17) |
+                              (uint32_t(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of a shared variable of CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t peer_smem(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Arrive on an mbarrier of either CTA of the pair (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (arrivals come from the peer CTA too).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 255u && global_ns() - t0 > HLA_WAIT_NS) return false;
+  }
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t bar_cluster, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tc2_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kT2Idesc), "r"(accumulate));
+}
+// Arrive on the barrier at this offset in both CTAs of the pair once the MMAs issued so far complete.
+__device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    writer_tc2_kernel(const __grid_constant__ CUtensorMap tmap_h, const __grid_constant__ CUtensorMap tmap_e,
+                      const TcParams tp) {
+  const WriterParams& p = tp.w;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kT2Stages * kT2StageBytes);  // leader's are used
+  uint64_t* empty = full + kT2Stages;   // both CTAs
+  uint64_t* tfull = empty + kT2Stages;  // [2] both CTAs
+  uint64_t* tempty = tfull + 2;         // [2] leader's are used: 8 arrivals (4 epilogue warps x 2 CTAs)
+  uint64_t* drained = tempty + 2;       // leader
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int NK = p.K / kTcK;
+  const int num_tiles = tp.n_tiles * tp.m_tiles;  // m tiles of 256 rows
+  const int first = static_cast<int>(cluster_id_x()), stride = static_cast<int>(cluster_count_x());
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * kTcN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < kT2Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    mbar_init(drained, 1);
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      prefetch_tmap(&tmap_h);
+      prefetch_tmap(&tmap_e);
+      uint32_t g = 0;
+      bool ok = true;
+      for (int tile = first; tile < num_tiles && ok; tile += stride) {
+        const int m0 = (tile / tp.n_tiles) * 256 + 128 * static_cast<int>(rank), j = tile % tp.n_tiles;
+        int n_lo, n_hi;
+        tc_tile_rows(p, j, n_lo, n_hi);
+        const int n_mine = leader ? n_lo : n_hi;
+        for (int kb = 0; kb < NK; ++kb, ++g) {
+          const int s = g % kT2Stages;
+          if (g >= kT2Stages && !mbar_wait(&empty[s], ((g / kT2Stages) - 1) & 1)) {
+            record_error(p.err, kErrWaitEmpty);
+            ok = false;
+            break;
+          }
+          uint8_t* a = smem + s * kT2StageBytes;
+          // the leader's full barrier counts both CTAs' bytes
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * kT2StageBytes);
+          const uint32_t bar = peer_smem(&full[s], 0);
+          tma_load_2d_pair(a, &tmap_h, bar, kb * kTcK, m0);
+          tma_load_2d_pair(a + kT2ABytes, &tmap_e, bar, kb * kTcK, n_mine);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (leader && lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = first; tile < num_tiles && ok; tile += stride, ++it) {
+        const int b = it & 1;
+        if (it >= 2 && !mbar_wait_cluster(&tempty[b], ((it >> 1) - 1) & 1)) {
+          record_error(p.err, kErrWaitEmpty);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + b * kTcN;
+        for (int kb = 0; kb < NK; ++kb, ++g) {
+          const int s = g % kT2Stages;
+          if (!mbar_wait(&full[s], (g / kT2Stages) & 1)) {
+            record_error(p.err, kErrWaitFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * kT2StageBytes), bb = a + kT2ABytes;
+#pragma unroll
+          for (int kk = 0; kk < kTcK / 16; ++kk)
+            tc2_mma(d, umma_desc_sw128(a + kk * 32), umma_desc_sw128(bb + kk * 32), (kb | kk) != 0);
+          tc2_commit_both(&empty[s]);
+        }
+        tc2_commit_both(&tfull[b]);
+      }
+      tc2_commit_both(drained);  // the peer's copy is not waited on
+      if (!mbar_wait(drained, 0)) record_error(p.err, kErrWaitFull);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2-5, both CTAs)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int it = 0;
+    for (int tile = first; tile < num_tiles; tile += stride, ++it) {
+      const int b = it & 1;
+      const int m0 = (tile / tp.n_tiles) * 256 + 128 * static_cast<int>(rank), j = tile % tp.n_tiles;
+      int n_lo, n_hi;
+      tc_tile_rows(p, j, n_lo, n_hi);
+      const int t = m0 + row;
+      const bool pair_tile = p.commit && j < p.w / 256;
+      TileIn in;
+      tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in);
+      const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1));
+      tc_fence_after();
+      if (!done) {
+        record_error(p.err, kErrWaitFull);
+        break;
+      }
+      tc_store_tile(p, tmem + b * kTcN + (static_cast<uint32_t>(quarter * 32) << 16), t < p.T, pair_tile, n_lo, n_hi,
+                    in);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(peer_smem(&tempty[b], 0));
+    }
+  }
+  // the leader's MMAs read this CTA's shared memory and write its TMEM: neither is released before
+  // both CTAs are done (the leader's MMA thread has waited for the last MMA above)
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTcN));
+  }
+}
+
 // 2-D TMA map over a [rows, K] bf16 matrix with 128-row x 64-column boxes, SWIZZLE_128B.
 static int rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems) {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -419,17 +653,47 @@ int writer_tc(const WriterParams& p, cudaStream_t s) {
   int rc = rows_tmap(&th, p.h, p.T, p.K, p.h_st);
   if (rc) return rc;
   if ((rc = rows_tmap(&te, p.E, p.N, p.K, p.e_st))) return rc;
-  static unsigned attr_mask = 0;
-  ensure_smem_limit(writer_tc_kernel, kTcSmem, attr_mask);
+  static int sms[64] = {0}, pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool cached = dev < 64;
+  if (cached && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int nsm = cached && sms[dev] > 0 ? sms[dev] : 148;
   TcParams tp;
   tp.w = p;
   tp.n_tiles = p.N / kTcN;
+  if (p.T >= 2 * kTcM) {
+    static unsigned attr2 = 0;
+    ensure_smem_limit(writer_tc2_kernel, kT2Smem, attr2);
+    tp.m_tiles = (p.T + 2 * kTcM - 1) / (2 * kTcM);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kT2Smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cached && pairs[dev] == 0) {
+      cfg.gridDim = dim3(nsm);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, writer_tc2_kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = nsm / 2;
+      }
+      pairs[dev] = n;
+    }
+    const int max_pairs = cached ? pairs[dev] : nsm / 2;
+    const int tiles = tp.n_tiles * tp.m_tiles;
+    cfg.gridDim = dim3(2 * (tiles < max_pairs ? tiles : max_pairs));
+    return cuda_status(cudaLaunchKernelEx(&cfg, writer_tc2_kernel, th, te, tp), "writer_tc2_kernel launch");
+  }
+  static unsigned attr_mask = 0;
+  ensure_smem_limit(writer_tc_kernel, kTcSmem, attr_mask);
   tp.m_tiles = (p.T + kTcM - 1) / kTcM;
-  static int sms[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  const int nsm = dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
   const int tiles = tp.n_tiles * tp.m_tiles;
   writer_tc_kernel<<<tiles < nsm ? tiles : nsm, kTcThreads, kTcSmem, s>>>(th, te, tp);
   return cuda_status(cudaGetLastError(), "writer_tc_kernel launch");

@@ -259,8 +259,9 @@ def test_committed_row_in_place_matches_reference_fixture():
 
 
 # ----------------------------------------------------------------------------- fused entry points
-# 300 tokens: the tcgen05 path (3 row tiles, ragged tail); 20000: several tiles per persistent CTA
-@pytest.mark.parametrize('T', [37, 300, 20000])
+# 37: mma.sync path; 200: single-CTA tcgen05 tiles (ragged tail); 300: CTA-pair tiles (ragged second
+# pair tile); 20000: several pair tiles per persistent cluster
+@pytest.mark.parametrize('T', [37, 200, 300, 20000])
 @pytest.mark.parametrize('loop', [0, 3])
 def test_writer_commit_equals_project_then_commit(loop, T):
     """The commit fused into the writer epilogue writes exactly the rows that the projection followed
