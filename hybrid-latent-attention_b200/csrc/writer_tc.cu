@@ -80,25 +80,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 8 bf16 <-> 8 floats through one 16-byte access.
-__device__ __forceinline__ void load8(const __nv_bfloat16* src, float* v) {
-  const uint4 u = *reinterpret_cast<const uint4*>(src);
-  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(b[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-__device__ __forceinline__ void store8(__nv_bfloat16* dst, const float* v) {
-  uint4 u;
-  __nv_bfloat162* b = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) b[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(dst) = u;
-}
-
 struct TcParams {
   WriterParams w;
   int n_tiles, m_tiles;
@@ -164,17 +145,20 @@ __device__ __forceinline__ void tc_tile_prefetch(const WriterParams& p, int t, b
   }
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
-  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(b[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
+// Epilogue of one 128 x 256 tile for this thread's row: 16 + 16 columns (c0 of both halves) at a time,
+// in packed bf16x2 arithmetic (the _rn forms, which are never contracted into an fma).  Each packed
+// operation rounds its exact result once to bf16; on bf16
+// inputs that equals the reference's fp32 operation followed by a rounding to bf16 (a product of two
+// bf16 values is exact in fp32, and rounding a sum first to fp32's 24 bits and then to bf16's 8 is
+// innocuous since 24 >= 2 * 8 + 2), so the values are those of the torch order bit for bit:
+//   acc -> bf16,  reg = bf16(reg_in + acc),  y1 = bf16(bf16(x1 c) + bf16(-x2 s)),
+//   y2 = bf16(bf16(x2 c) + bf16(x1 s)).
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ uint32_t word(const uint4& u, int i) {
+  return i == 0 ? u.x : (i == 1 ? u.y : (i == 2 ? u.z : u.w));
 }
 
-// Epilogue of one 128 x 256 tile for this thread's row: 16 + 16 columns (c0 of both halves) at a time.
 __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t tacc, bool live, bool pair_tile, int n_lo,
                                               int n_hi, TileIn& in) {
 #pragma unroll
@@ -184,54 +168,60 @@ __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t ta
     tmem_ld16(tacc + 128 + c0, rh);
     tmem_wait_ld();
     if (!live) continue;
-    float lo[16], hi[16];
+    __nv_bfloat162 lo[8], hi[8];  // columns c0 + 2i, c0 + 2i + 1 of each half
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      lo[e] = bf16_round(__uint_as_float(rl[e]));
-      hi[e] = bf16_round(__uint_as_float(rh[e]));
+    for (int i = 0; i < 8; ++i) {
+      lo[i] = __floats2bfloat162_rn(__uint_as_float(rl[2 * i]), __uint_as_float(rl[2 * i + 1]));
+      hi[i] = __floats2bfloat162_rn(__uint_as_float(rh[2 * i]), __uint_as_float(rh[2 * i + 1]));
     }
     const int clo = n_lo + c0, chi = n_hi + c0;  // global columns
     if (p.reg_in) {
-      float a[16], b[16];
-      unpack8(in.lo[c0 / 8], a);
-      unpack8(in.lo[c0 / 8 + 1], a + 8);
-      unpack8(in.hi[c0 / 8], b);
-      unpack8(in.hi[c0 / 8 + 1], b + 8);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        lo[e] = bf16_round(a[e] + lo[e]);
-        hi[e] = bf16_round(b[e] + hi[e]);
+      for (int i = 0; i < 8; ++i) {
+        lo[i] = __hadd2_rn(as_bf2(word(in.lo[c0 / 8 + i / 4], i % 4)), lo[i]);
+        hi[i] = __hadd2_rn(as_bf2(word(in.hi[c0 / 8 + i / 4], i % 4)), hi[i]);
       }
     }
+    uint4 olo[2], ohi[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      olo[i] = make_uint4(as_u32(lo[4 * i]), as_u32(lo[4 * i + 1]), as_u32(lo[4 * i + 2]), as_u32(lo[4 * i + 3]));
+      ohi[i] = make_uint4(as_u32(hi[4 * i]), as_u32(hi[4 * i + 1]), as_u32(hi[4 * i + 2]), as_u32(hi[4 * i + 3]));
+    }
     if (in.rout) {
-      store8(in.rout + clo, lo);
-      store8(in.rout + clo + 8, lo + 8);
-      store8(in.rout + chi, hi);
-      store8(in.rout + chi + 8, hi + 8);
+      uint4* r1 = reinterpret_cast<uint4*>(in.rout + clo);
+      uint4* r2 = reinterpret_cast<uint4*>(in.rout + chi);
+      r1[0] = olo[0];
+      r1[1] = olo[1];
+      r2[0] = ohi[0];
+      r2[1] = ohi[1];
     }
     if (in.dst) {
       if (pair_tile) {
         // cos / sin of pairs [c0, c0 + 16) sit in slots (c0 % 32) / 8 .. + 1 of the half in flight;
-        // the next 32 pairs are fetched once this half's last chunk has them unpacked
-        float cs[16], sn[16];
+        // the next 32 pairs are fetched once this chunk has read its own
         const int q = (c0 % 32) / 8;
-        unpack8(in.cs[q], cs);
-        unpack8(in.cs[q + 1], cs + 8);
-        unpack8(in.sn[q], sn);
-        unpack8(in.sn[q + 1], sn + 8);
+        const uint4 cs[2] = {in.cs[q], in.cs[q + 1]}, sn[2] = {in.sn[q], in.sn[q + 1]};
         if (c0 % 32 == 16 && c0 + 16 < 128) tc_load_rope(in, n_lo + c0 + 16, in.cs, in.sn, p.w / 2);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float y1, y2;
-          rope_pair_torch(lo[e], hi[e], cs[e], sn[e], y1, y2);
-          lo[e] = y1;
-          hi[e] = y2;
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 c = as_bf2(word(cs[i / 4], i % 4)), sv = as_bf2(word(sn[i / 4], i % 4));
+          const __nv_bfloat162 x1 = lo[i], x2 = hi[i];
+          lo[i] = __hadd2_rn(__hmul2_rn(x1, c), __hneg2(__hmul2_rn(x2, sv)));
+          hi[i] = __hadd2_rn(__hmul2_rn(x2, c), __hmul2_rn(x1, sv));
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          olo[i] = make_uint4(as_u32(lo[4 * i]), as_u32(lo[4 * i + 1]), as_u32(lo[4 * i + 2]), as_u32(lo[4 * i + 3]));
+          ohi[i] = make_uint4(as_u32(hi[4 * i]), as_u32(hi[4 * i + 1]), as_u32(hi[4 * i + 2]), as_u32(hi[4 * i + 3]));
         }
       }
-      store8(in.dst + clo, lo);
-      store8(in.dst + clo + 8, lo + 8);
-      store8(in.dst + chi, hi);
-      store8(in.dst + chi + 8, hi + 8);
+      uint4* d1 = reinterpret_cast<uint4*>(in.dst + clo);
+      uint4* d2 = reinterpret_cast<uint4*>(in.dst + chi);
+      d1[0] = olo[0];
+      d1[1] = olo[1];
+      d2[0] = ohi[0];
+      d2[1] = ohi[1];
     }
   }
 }
