@@ -386,7 +386,7 @@ def run_ours(args):
     shape = dec.OuroShape(max_position=max_pos)
     exchange = (rank, world, dist.group.WORLD) if (args.config == 5 and world > 1) else None
     model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=args.seed + rank,
-                              latent_rows=latent_rows, exchange=exchange)
+                              latent_rows=latent_rows, exchange=exchange, exchange_mode=args.exchange)
     torch.cuda.synchronize()
     model.step()                       # eager warm-up: descriptor caches, occupancy
     graph = model.capture()
@@ -464,12 +464,17 @@ def run_ours(args):
             'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded), random-init weights',
             'config': {'workload': f'BASELINE config {args.config}: Ouro-1.4B-shaped S6 decode step, attention path '
                                    f'(24 layers x 4 loops), dense body excluded' +
-                                   (', latent history sequence-split across GPUs, NCCL all-gather of (z, lse) '
-                                    'per (layer, loop)' if exchange is not None else ''),
+                                   ((', latent history sequence-split across GPUs, (z, lse) parts stored into '
+                                     'every GPU by the reduce kernel over NVLink (peer memory + flags) per (layer, '
+                                     'loop)' if args.exchange == 'peer' else
+                                     ', latent history sequence-split across GPUs, NCCL all-gather of (z, lse) per '
+                                     '(layer, loop)') if exchange is not None else ''),
                        'global_batch': tokens_all, 'batch_per_gpu': len(ctx), 'ctx': max(ctx),
                        'seq_len': max(ctx) + 1, 'page': shape.page, 'window': shape.window,
-                       'parallelism': (f'sequence-split x{world} (NCCL all_gather per layer x loop)' if exchange
-                                       is not None else f'request-partitioned x{world} (no collectives)'),
+                       'parallelism': ((f'sequence-split x{world} (fused reduce + peer stores per layer x loop)'
+                                        if args.exchange == 'peer' else
+                                        f'sequence-split x{world} (NCCL all_gather per layer x loop)')
+                                       if exchange is not None else f'request-partitioned x{world} (no collectives)'),
                        'l2': 'inputs larger than L2 (latent caches ~40 GB per GPU), no flush'},
             'latent_history': {'bytes_per_step': bytes_hist, 'GBps_in_step': bytes_hist / (ms_step / 1e3) / 1e9,
                                'attention_bytes_per_step': attn_bytes,
@@ -492,6 +497,7 @@ def run_ours(args):
     import gc
     gc.collect()
     torch.cuda.synchronize()
+    model.close_exchange()             # peer mappings: every rank, after its last launch
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -615,6 +621,8 @@ def main():
     ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
     ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')
     ap.add_argument('--cpu-tokens', type=int, default=4096, help='tokens of the config-3 CPU oracle sample')
+    ap.add_argument('--exchange', default='peer', choices=['peer', 'nccl'],
+                    help='config 5 on several GPUs: how the (z, lse) parts move')
     ap.add_argument('--no-cpu', action='store_true', help='skip the CPU baseline leg')
     args = ap.parse_args()
     if args.warmup < 3:

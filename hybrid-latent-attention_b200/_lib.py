@@ -17,6 +17,8 @@ ABI_VERSION = 1
 
 OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
 COMBINE_AFTER_PARTIALS = 1   # hla_s6_decode_combine flag (include/hla_s6.h)
+REDUCE_AFTER_PARTIALS = 1    # hla_s6_history_reduce_exchange flag
+PEER_HANDLE_BYTES = 64       # HLA_S6_PEER_HANDLE_BYTES
 
 _c_void_p, _i32, _i64, _f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 P = _c_void_p
@@ -45,10 +47,15 @@ SIGNATURES = {
                               _i32, P, _i64, _i32, P, _i32, P, P],
     'hla_s6_commit_rows': [P, _i64, _i32, P, P, _i64, _i64, P, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _i32,
                            P, P],
-    'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i32, _i64, P, P, _i64, _i64, P, _i64,
-                              _i64, P, _i64,
+    'hla_s6_decode_combine': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i32, _i64, P, P, P, P, _i64, _i64, P,
+                              _i64, _i64, P, _i64,
                               _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, P,
-                              _i64, _i64, P, _i32, P],
+                              _i64, _i64, P, _i32, P, P],
+    'hla_s6_peer_alloc': [_i64, P, P],
+    'hla_s6_peer_open': [P, P],
+    'hla_s6_peer_close': [P],
+    'hla_s6_peer_free': [P],
+    'hla_s6_history_reduce_exchange': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, P, _i32, _i32, P],
     'hla_s6_window_history': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _f32, _i32,
                               _i32, _i32, P, _i64, _i64, P, P],
     'hla_s6_chunk_attention': [P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i32, _i32, _i32, _i32, _f32, P, _i64,
@@ -94,8 +101,17 @@ def call(name: str, *args):
 
 
 def ptr(t):
-    """Device pointer of a tensor (None -> NULL)."""
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """Device pointer of a tensor (None -> NULL; a ctypes pointer or an int passes through)."""
+    if t is None or isinstance(t, ctypes.c_void_p):
+        return t
+    if isinstance(t, int):
+        return ctypes.c_void_p(t)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def pointer_array(ptrs):
+    """Host array of device pointers (ints or None) for the ``T* const*`` arguments."""
+    return (ctypes.c_void_p * len(ptrs))(*[None if p is None else int(p) for p in ptrs])
 
 
 def stream_of(t: torch.Tensor):

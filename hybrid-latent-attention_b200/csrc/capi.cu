@@ -209,6 +209,35 @@ int hla_s6_history_reduce(int32_t num_tokens, int32_t num_heads, int32_t width, 
                         static_cast<cudaStream_t>(stream));
 }
 
+int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,
+                                   int32_t num_kv_splits, float* workspace, int64_t workspace_floats,
+                                   const uint8_t* empty, float* const* parts, int32_t* const* flags, int32_t* done,
+                                   int32_t world, int32_t launch_flags, void* stream) {
+  if (world < 1 || world > kMaxExchangeRanks || !parts || !flags || !done) {
+    set_error("history reduce exchange needs 1..%d ranks, their part and flag pointers and a counter",
+              kMaxExchangeRanks);
+    return kStatusInvalid;
+  }
+  ExchangeTargets x{};
+  for (int d = 0; d < world; ++d) {
+    if (!parts[d] || !flags[d] || (reinterpret_cast<uintptr_t>(parts[d]) % 16)) {
+      set_error("history reduce exchange: rank %d's part must be 16-byte aligned and its flag set", d);
+      return kStatusInvalid;
+    }
+    x.part[d] = parts[d];
+    x.flag[d] = flags[d];
+  }
+  x.done = done;
+  x.world = world;
+  HistoryArgs a = make_history_args(nullptr, 0, 0, nullptr, 0, 0, 0, nullptr, 0, 0, nullptr, num_tokens, num_heads,
+                                    width, page, 1.f, num_kv_splits, workspace, workspace_floats, nullptr);
+  HistoryPlan plan;
+  int rc = history_plan(a, &plan);
+  if (rc) return rc;
+  return history_reduce_exchange(a, plan, empty, x, (launch_flags & HLA_S6_REDUCE_AFTER_PARTIALS) != 0,
+                                 static_cast<cudaStream_t>(stream));
+}
+
 int hla_s6_history_plan(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, int32_t num_kv_splits,
                         int64_t workspace_floats, int32_t* stream_mode, int32_t* grid, int32_t* slots) {
   HistoryArgs a = make_history_args(nullptr, 0, 0, nullptr, 0, 0, 0, nullptr, 0, 0, nullptr, num_tokens, num_heads,

@@ -367,7 +367,8 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
 
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
                           int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
-                          const float* lse_in, int32_t num_parts, int64_t part_stride, const uint8_t* empty,
+                          const float* lse_in, int32_t num_parts, int64_t part_stride, int32_t* part_flags,
+                          int32_t* part_seen, const uint8_t* empty,
                           const void* B, int64_t b_stride_h,
                           int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
                           const void* exact_cache, int64_t exact_num_blocks, int64_t exact_stride_block,
@@ -376,7 +377,7 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
                           float scale, const void* chunk_o, int64_t chunk_stride_t, int64_t chunk_stride_h,
                           const float* chunk_lse, void* out, int64_t out_stride_t, int64_t out_stride_h,
-                          float* lse_out, int32_t flags, void* stream) {
+                          float* lse_out, int32_t flags, int* error_flag, void* stream) {
   CombineParams p;
   p.win = make_window(q_rope, q_stride_t, q_stride_h, exact_cache, exact_num_blocks, exact_stride_block,
                       exact_stride_head, exact_stride_row, exact_page, block_table, block_table_stride, max_blocks,
@@ -427,6 +428,13 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
   p.lse_in = lse_in;
   p.num_parts = z_in ? num_parts : 0;
   p.part_stride = part_stride;
+  if (part_flags && (!z_in || !part_seen)) {
+    set_error("decode combine: part flags need reduced parts (z_in) and a CTA counter");
+    return kStatusInvalid;
+  }
+  p.part_flags = z_in ? part_flags : nullptr;
+  p.part_seen = part_seen;
+  p.err = error_flag;
   p.empty = empty;
   p.T = num_tokens;
   p.H = num_heads;
@@ -437,7 +445,7 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
   p.o_st = out_stride_t;
   p.o_sh = out_stride_h;
   p.lse_out = lse_out;
-  const bool pdl = (flags & HLA_S6_COMBINE_AFTER_PARTIALS) && !z_in;
+  const bool pdl = (flags & HLA_S6_COMBINE_AFTER_PARTIALS) != 0;
   return decode_combine(p, width, pdl, static_cast<cudaStream_t>(stream));
 }
 

@@ -80,6 +80,19 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
       lse_w = -INFINITY;
     }
     griddep_wait();
+    if (p.part_flags) {
+      // every rank's part of this exchange slot has landed (bounded wait); the last CTA through
+      // clears the flags for the slot's next use
+      if (threadIdx.x == 0) {
+        if (!wait_flags_sys(p.part_flags, p.num_parts)) record_error(p.err, kErrWaitPeer);
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        if (atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(p.part_seen), 1u) == total - 1) {
+          for (int q = 0; q < p.num_parts; ++q) p.part_flags[q] = 0;
+          *p.part_seen = 0;
+        }
+      }
+      __syncthreads();
+    }
     constexpr int NV = W / 128;  // float4 per lane
     float4 acc[NV];
 #pragma unroll
@@ -89,12 +102,13 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
       if (p.z_in) {
         // num_parts reduced partials (e.g. one per GPU of a sequence split): LSE-merge them
         float mx = -INFINITY;
+        // L2-coherent loads (.cg): parts may have been stored by other GPUs during this kernel
         for (int q = 0; q < p.num_parts; ++q)
-          mx = fmaxf(mx, p.lse_in[q * p.part_stride + static_cast<int64_t>(h) * T + t]);
+          mx = fmaxf(mx, __ldcg(p.lse_in + q * p.part_stride + static_cast<int64_t>(h) * T + t));
         if (mx != -INFINITY) {
           float wsum = 0.f;
           for (int q = 0; q < p.num_parts; ++q) {
-            const float lq = p.lse_in[q * p.part_stride + static_cast<int64_t>(h) * T + t];
+            const float lq = __ldcg(p.lse_in + q * p.part_stride + static_cast<int64_t>(h) * T + t);
             if (lq == -INFINITY) continue;
             const float wgt = expf(lq - mx);
             wsum += wgt;
@@ -102,7 +116,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
                 reinterpret_cast<const float4*>(p.z_in + q * p.part_stride + (static_cast<int64_t>(t) * H + h) * W);
 #pragma unroll
             for (int i = 0; i < NV; ++i) {
-              const float4 v = src[i * 32 + lane];
+              const float4 v = __ldcg(src + i * 32 + lane);
               acc[i].x += wgt * v.x; acc[i].y += wgt * v.y; acc[i].z += wgt * v.z; acc[i].w += wgt * v.w;
             }
           }

@@ -16,6 +16,11 @@ struct CombineParams {
   const float* lse_in;  // part q: lse [H, T] at lse_in + q * part_stride
   int num_parts;
   int64_t part_stride;  // floats between consecutive parts
+  // parts written by other GPUs (history_reduce_exchange): wait until part_flags[0 .. num_parts)
+  // are all set, then clear them once every CTA has passed (part_seen counts the CTAs)
+  int* part_flags;
+  int* part_seen;
+  int* err;  // optional device error word (a peer that never delivers)
   const uint8_t* empty;  // optional [T]: rows whose latent history is empty
   int T, H;
   const __nv_bfloat16* B;  // [H, W, 128] up-projection

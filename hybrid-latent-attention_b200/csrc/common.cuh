@@ -21,6 +21,7 @@ enum : int {
   kErrWaitFull = 1,    // consumer gave up waiting for a page copy
   kErrWaitEmpty = 2,   // producer gave up waiting for a free stage
   kErrSlots = 3,       // a partial would land outside the workspace
+  kErrWaitPeer = 4,    // gave up waiting for another GPU's part of a sequence-split exchange
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -33,6 +34,21 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// ---------------------------------------------------------------- cross-GPU flags (peer memory)
+// System-scope release / acquire on a flag word that another GPU writes or reads over NVLink.
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -81,6 +97,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 255u && global_ns() - t0 > HLA_WAIT_NS) return false;
   }
+}
+
+// Bounded wait until flags[0 .. n) are all nonzero (HLA_WAIT_NS of device time in total).
+__device__ __forceinline__ bool wait_flags_sys(const int* flags, int n) {
+  const uint64_t t0 = global_ns();
+  for (int q = 0; q < n; ++q) {
+    for (uint32_t it = 0; ld_acquire_sys(flags + q) == 0; ++it) {
+      if ((it & 63u) == 63u && global_ns() - t0 > HLA_WAIT_NS) return false;
+    }
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- TMA

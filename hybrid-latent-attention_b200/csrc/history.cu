@@ -390,15 +390,26 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
 }
 
 // Stage-2 reduce: partials of row t -> o[t, h, :] (bf16 and/or fp32) and lse[h, t].
+// Stage-2 merge of one (row t, head h), 128 columns (chunk blockIdx.z) per CTA: the LSE-weighted
+// mean of the row's split partials (slots [lo, hi) from meta in stream mode, else slot t) and its
+// lse.  A long row can have ~100 partials (a few rows over a whole GPU), so the slots are spread
+// over kReduceLanes slot-lanes of 32 threads: the lse's max and the slot weights are computed once
+// into shared memory, every thread accumulates its float4 column over its lane's slots with four
+// loads in flight, and the lanes are summed through shared memory.  Thread (lane 0, c) returns
+// columns 128 z + 4c .. + 3 (other lanes return zeros).  An empty row (flagged, or no partial with
+// a finite lse) gives 0 and -inf.
+constexpr int kReduceLanes = 8, kReduceCols = 32, kReduceThreads = kReduceLanes * kReduceCols;
+constexpr int kReduceWBuf = 1024;  // slot weights per pass
+
 template <int W>
-__global__ void __launch_bounds__(W / 4) history_reduce_kernel(const float* __restrict__ ws_o,
-                                                                const float* __restrict__ ws_lse,
-                                                                const int2* __restrict__ meta, int stream_mode,
-                                                                int T, int H, const uint8_t* __restrict__ empty,
-                                                                __nv_bfloat16* __restrict__ out, int64_t o_st,
-                                                                int64_t o_sh, float* __restrict__ out_f32,
-                                                                float* __restrict__ lse_out) {
-  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+__device__ __forceinline__ float4 reduce_row(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
+                                             const int2* __restrict__ meta, int stream_mode, int t, int h, int H,
+                                             const uint8_t* __restrict__ empty, float& lse) {
+  __shared__ float wbuf[kReduceWBuf];
+  __shared__ float red[kReduceThreads / 32];
+  __shared__ float4 part[(kReduceLanes - 1) * kReduceCols];
+  const int tid = threadIdx.x, col = tid % kReduceCols, lane = tid / kReduceCols;
+  const int colg = blockIdx.z * kReduceCols + col;  // float4 column of the row
   int lo, hi;
   if (stream_mode) {
     const int2 m = meta[t];
@@ -408,28 +419,130 @@ __global__ void __launch_bounds__(W / 4) history_reduce_kernel(const float* __re
     lo = t;
     hi = t + 1;
   }
+  const int n = hi - lo;
   float mx = -INFINITY;
-  for (int s = lo; s < hi; ++s) mx = fmaxf(mx, ws_lse[static_cast<int64_t>(s) * H + h]);
+  for (int i = tid; i < n; i += kReduceThreads) mx = fmaxf(mx, ws_lse[static_cast<int64_t>(lo + i) * H + h]);
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int i = 1; i < kReduceThreads / 32; ++i) mx = fmaxf(mx, red[i]);
   const bool is_empty = (empty && empty[t]) || mx == -INFINITY;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float wsum = 0.f;
   if (!is_empty) {
-    for (int s = lo; s < hi; ++s) {
-      const float w = expf(ws_lse[static_cast<int64_t>(s) * H + h] - mx);
-      const float4 v = reinterpret_cast<const float4*>(ws_o + (static_cast<int64_t>(s) * H + h) * W)[tid];
-      wsum += w;
-      acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+    for (int base = 0; base < n; base += kReduceWBuf) {
+      const int m = min(n - base, kReduceWBuf);
+      __syncthreads();  // the previous pass's weights are consumed
+      for (int i = tid; i < m; i += kReduceThreads)
+        wbuf[i] = expf(ws_lse[static_cast<int64_t>(lo + base + i) * H + h] - mx);
+      __syncthreads();
+      for (int i = 0; i < m; ++i) wsum += wbuf[i];  // same order in every thread
+      int i = lane;
+      for (; i + 3 * kReduceLanes < m; i += 4 * kReduceLanes) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = reinterpret_cast<const float4*>(
+              ws_o + (static_cast<int64_t>(lo + base + i + u * kReduceLanes) * H + h) * W)[colg];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float w = wbuf[i + u * kReduceLanes];
+          acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
+        }
+      }
+      for (; i < m; i += kReduceLanes) {
+        const float4 v =
+            reinterpret_cast<const float4*>(ws_o + (static_cast<int64_t>(lo + base + i) * H + h) * W)[colg];
+        const float w = wbuf[i];
+        acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+      }
     }
-    const float inv = 1.f / wsum;
-    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
   }
+  if (lane > 0) part[(lane - 1) * kReduceCols + col] = acc;
+  __syncthreads();
+  if (lane == 0) {
+#pragma unroll
+    for (int l = 1; l < kReduceLanes; ++l) {
+      const float4 v = part[(l - 1) * kReduceCols + col];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if (!is_empty) {
+      const float inv = 1.f / wsum;
+      acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+    }
+  }
+  lse = is_empty ? -INFINITY : mx + logf(wsum);
+  return acc;
+}
+
+template <int W>
+__global__ void __launch_bounds__(kReduceThreads, 1) history_reduce_kernel(const float* __restrict__ ws_o,
+                                                                         const float* __restrict__ ws_lse,
+                                                                         const int2* __restrict__ meta,
+                                                                         int stream_mode, int T, int H,
+                                                                         const uint8_t* __restrict__ empty,
+                                                                         __nv_bfloat16* __restrict__ out,
+                                                                         int64_t o_st, int64_t o_sh,
+                                                                         float* __restrict__ out_f32,
+                                                                         float* __restrict__ lse_out) {
+  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  float lse;
+  const float4 acc = reduce_row<W>(ws_o, ws_lse, meta, stream_mode, t, h, H, empty, lse);
+  if (tid >= kReduceCols) return;
+  const int c = (blockIdx.z * kReduceCols + tid) * 4;
   if (out) {
-    __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + tid * 4;
+    __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + c;
     reinterpret_cast<__nv_bfloat162*>(dst)[0] = __floats2bfloat162_rn(acc.x, acc.y);
     reinterpret_cast<__nv_bfloat162*>(dst)[1] = __floats2bfloat162_rn(acc.z, acc.w);
   }
-  if (out_f32) reinterpret_cast<float4*>(out_f32 + (static_cast<int64_t>(t) * H + h) * W)[tid] = acc;
-  if (tid == 0 && lse_out) lse_out[static_cast<int64_t>(h) * T + t] = is_empty ? -INFINITY : mx + logf(wsum);
+  if (out_f32) *reinterpret_cast<float4*>(out_f32 + (static_cast<int64_t>(t) * H + h) * W + c) = acc;
+  if (tid == 0 && blockIdx.z == 0 && lse_out) lse_out[static_cast<int64_t>(h) * T + t] = lse;
+}
+
+// The sequence-split exchange fused into the reduce: this GPU's part - z fp32 [T, H, W] followed by
+// lse [H, T] - is stored straight into every rank's receive slot (peer memory over NVLink, this
+// GPU's own slot included).  Once every CTA's stores are visible system-wide, the last CTA to
+// finish raises this rank's flag word in every rank's flag array for the slot (release, system
+// scope); the consuming combine waits for all ranks' flags (acquire) and clears them.  Launched as
+// a programmatic dependent of the history kernel (griddepcontrol), it lets its own dependent - the
+// combine - start at once, so the combine's window phase overlaps this reduce.
+template <int W>
+__global__ void __launch_bounds__(kReduceThreads)
+    history_reduce_exchange_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
+                                   const int2* __restrict__ meta, int stream_mode, int T, int H,
+                                   const uint8_t* __restrict__ empty, const ExchangeTargets x) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  float lse;
+  const float4 acc = reduce_row<W>(ws_o, ws_lse, meta, stream_mode, t, h, H, empty, lse);
+  if (tid < kReduceCols) {
+    const int64_t zoff = (static_cast<int64_t>(t) * H + h) * W + (blockIdx.z * kReduceCols + tid) * 4;
+    const int64_t loff = static_cast<int64_t>(T) * H * W + static_cast<int64_t>(h) * T + t;
+    const bool lse_here = tid == 0 && blockIdx.z == 0;
+#pragma unroll
+    for (int d = 0; d < kMaxExchangeRanks; ++d) {  // constant indices keep the targets in registers
+      if (d >= x.world) break;
+      *reinterpret_cast<float4*>(x.part[d] + zoff) = acc;
+      if (lse_here) x.part[d][loff] = lse;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    if (atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(x.done), 1u) == total - 1) {
+      *x.done = 0;  // the slot's next use is a later launch (stream order)
+      __threadfence_system();
+#pragma unroll
+      for (int d = 0; d < kMaxExchangeRanks; ++d) {
+        if (d >= x.world) break;
+        st_release_sys(x.flag[d], 1);
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -563,19 +676,51 @@ int history_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t st
 int history_reduce(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out, int64_t o_st,
                    int64_t o_sh, float* out_f32, float* lse, cudaStream_t stream) {
   if (a.T == 0) return kStatusOk;
-  dim3 grid(a.T, a.H);
-#define HLA_REDUCE(WW)                                                                                   \
-  history_reduce_kernel<WW><<<grid, WW / 4, 0, stream>>>(plan.ws_o, plan.ws_lse, plan.meta, plan.stream_mode, \
-                                                         a.T, a.H, empty, static_cast<__nv_bfloat16*>(out), o_st, \
-                                                         o_sh, out_f32, lse)
+  if (a.W != 256 && a.W != 512 && a.W != 1024) {
+    set_error("unsupported latent width %d", a.W);
+    return kStatusInvalid;
+  }
+  dim3 grid(a.T, a.H, a.W / (4 * kReduceCols));
+#define HLA_REDUCE(WW)                                                                                          \
+  history_reduce_kernel<WW><<<grid, kReduceThreads, 0, stream>>>(plan.ws_o, plan.ws_lse, plan.meta,             \
+                                                                 plan.stream_mode, a.T, a.H, empty,             \
+                                                                 static_cast<__nv_bfloat16*>(out), o_st, o_sh, \
+                                                                 out_f32, lse)
   switch (a.W) {
     case 256: HLA_REDUCE(256); break;
     case 512: HLA_REDUCE(512); break;
-    case 1024: HLA_REDUCE(1024); break;
-    default: set_error("unsupported latent width %d", a.W); return kStatusInvalid;
+    default: HLA_REDUCE(1024); break;
   }
 #undef HLA_REDUCE
   return cuda_status(cudaGetLastError(), "history_reduce_kernel launch");
+}
+
+int history_reduce_exchange(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty,
+                            const ExchangeTargets& x, bool pdl, cudaStream_t stream) {
+  if (a.T == 0) return kStatusOk;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.T, a.H, a.W / (4 * kReduceCols));
+  cfg.blockDim = dim3(kReduceThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e;
+  switch (a.W) {
+    case 256: e = cudaLaunchKernelEx(&cfg, history_reduce_exchange_kernel<256>, plan.ws_o, plan.ws_lse,
+                                     static_cast<const int2*>(plan.meta), plan.stream_mode, a.T, a.H, empty, x);
+      break;
+    case 512: e = cudaLaunchKernelEx(&cfg, history_reduce_exchange_kernel<512>, plan.ws_o, plan.ws_lse,
+                                     static_cast<const int2*>(plan.meta), plan.stream_mode, a.T, a.H, empty, x);
+      break;
+    case 1024: e = cudaLaunchKernelEx(&cfg, history_reduce_exchange_kernel<1024>, plan.ws_o, plan.ws_lse,
+                                      static_cast<const int2*>(plan.meta), plan.stream_mode, a.T, a.H, empty, x);
+      break;
+    default: set_error("unsupported latent width %d", a.W); return kStatusInvalid;
+  }
+  return cuda_status(e, "history_reduce_exchange_kernel launch");
 }
 
 }  // namespace hla

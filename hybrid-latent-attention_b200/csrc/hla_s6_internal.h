@@ -67,6 +67,19 @@ struct HistoryPlan {
 
 int history_plan(const HistoryArgs& a, HistoryPlan* plan);
 int history_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t stream);
+// Targets of the fused sequence-split exchange (history_reduce_exchange): this rank's part in every
+// rank's receive slot, this rank's flag word in every rank's flag array for the slot, and the
+// local counter of finished CTAs.
+constexpr int kMaxExchangeRanks = 8;
+struct ExchangeTargets {
+  float* part[kMaxExchangeRanks];
+  int* flag[kMaxExchangeRanks];
+  int* done;
+  int world;
+};
+// pdl: launch as a programmatic dependent of the immediately preceding launch (the history split).
+int history_reduce_exchange(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty,
+                            const ExchangeTargets& x, bool pdl, cudaStream_t stream);
 int history_reduce(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out, int64_t o_st,
                    int64_t o_sh, float* out_f32, float* lse, cudaStream_t stream);
 

@@ -73,12 +73,18 @@ class S6DecodeModel:
     ``latent_rows`` (optional, per request) is the number of latent history rows this GPU holds; by
     default every request's whole latent history ``ctx - W``.  ``exchange = (rank, world, group)``
     turns on the sequence split: each GPU holds a contiguous slice of every request's latent pages,
-    reduces its slice's partials to fp32 ``(z, lse)``, all-gathers them over NCCL and merges the
-    ``world`` parts in the combine (the window, query and writer work is replicated).
+    reduces its slice's partials to fp32 ``(z, lse)``, exchanges them and merges the ``world``
+    parts in the combine (the window, query and writer work is replicated).  ``exchange_mode``:
+
+    * ``'peer'`` (default): the reduce stores its part straight into every rank's receive slot over
+      NVLink (CUDA IPC mappings of one exchange region per GPU: a slot per (layer, loop), each
+      holding ``world`` parts, plus a flag word per part) and raises the flags; the combine waits
+      for them.  No collective library call is on the step.
+    * ``'nccl'``: the reduce writes a local part and an NCCL ``all_gather_into_tensor`` moves it.
     """
 
     def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
-                 latent_rows=None, exchange=None):
+                 latent_rows=None, exchange=None, exchange_mode='peer'):
         self.s, self.device = shape, torch.device(device)
         s = shape
         B = len(batch.ctx)
@@ -158,7 +164,13 @@ class S6DecodeModel:
         self.q_lat = torch.empty(B, s.heads, s.rank, dtype=BF16, device=self.device)
         self.q_rope = torch.empty(B, s.heads, s.head_dim, dtype=BF16, device=self.device)
         self.reg = [torch.empty(B, 2 * s.rank, dtype=BF16, device=self.device) for _ in range(s.layers)]
-        if exchange is not None:
+        self.exchange_mode = exchange_mode
+        self.x_bases = None
+        if exchange is not None and exchange_mode not in ('peer', 'nccl'):
+            raise ValueError(f'unknown exchange mode {exchange_mode!r}')
+        if exchange is not None and exchange_mode == 'peer':
+            self._init_peer_exchange(*exchange)
+        elif exchange is not None:
             world = exchange[1]
             part = B * s.heads * s.rank + s.heads * B          # z [B, H, W] then lse [H, B], W <= rank
             self.xsend = torch.empty(part, dtype=torch.float32, device=self.device)
@@ -166,6 +178,56 @@ class S6DecodeModel:
         self.scale = s.head_dim ** -0.5
         self.graph = None
         self.history_graph = None
+
+    # ------------------------------------------------------------------ peer exchange
+    def _init_peer_exchange(self, rank, world, group):
+        """One exchange region per GPU, mapped by every rank: ``slots x world`` parts of ``x_part``
+        floats (z [B, H, rank] then lse [H, B]), then ``slots x world`` int32 flags; plus two local
+        counters per slot (reduce CTAs done, combine CTAs through)."""
+        import ctypes
+        import torch.distributed as dist
+        s, B = self.s, self.B
+        slots = s.layers * s.loops
+        self.x_part = -(-(B * s.heads * s.rank + s.heads * B) // 4) * 4
+        self.x_region = slots * world * self.x_part * 4
+        handle = ctypes.create_string_buffer(_lib.PEER_HANDLE_BYTES)
+        base = ctypes.c_void_p()
+        _lib.call('hla_s6_peer_alloc', self.x_region + slots * world * 4, ctypes.byref(base), handle)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        bases = []
+        try:
+            for r in range(world):
+                if r == rank:
+                    bases.append(base.value)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.call('hla_s6_peer_open', ctypes.create_string_buffer(handles[r], _lib.PEER_HANDLE_BYTES),
+                          ctypes.byref(peer))
+                bases.append(peer.value)
+        except Exception:
+            for r, b in enumerate(bases):
+                _lib.call('hla_s6_peer_close' if r != rank else 'hla_s6_peer_free', ctypes.c_void_p(b))
+            raise
+        self.x_bases = bases
+        self.x_counters = torch.zeros(2 * slots, dtype=torch.int32, device=self.device)
+
+    def close_exchange(self):
+        """Unmap the peers' regions and free this rank's (collective: every rank calls it, after its
+        last step; no rank's memory is released while another may still write it)."""
+        if self.x_bases is None:
+            return
+        import ctypes
+        import torch.distributed as dist
+        rank, world, group = self.exchange
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+        for r, b in enumerate(self.x_bases):
+            if r != rank:
+                _lib.call('hla_s6_peer_close', ctypes.c_void_p(b))
+        dist.barrier(group=group)
+        _lib.call('hla_s6_peer_free', ctypes.c_void_p(self.x_bases[rank]))
+        self.x_bases = None
 
     # ------------------------------------------------------------------ bytes
     def latent_bytes_per_step(self):
@@ -244,7 +306,24 @@ class S6DecodeModel:
         # 3b. sequence split: reduce this GPU's slice to (z, lse) and all-gather the parts
         z_in = lse_in = None
         parts, part_stride, flags = 0, 0, _lib.COMBINE_AFTER_PARTIALS
-        if self.exchange is not None:
+        part_flags = part_seen = None
+        if self.exchange is not None and self.exchange_mode == 'peer':
+            import ctypes
+            rank, world, _ = self.exchange
+            i = loop * s.layers + layer          # exchange slot of this (layer, loop)
+            part_stride = self.x_part
+            parts = [b + (i * world + rank) * part_stride * 4 for b in self.x_bases]
+            flags_out = [b + self.x_region + (i * world + rank) * 4 for b in self.x_bases]
+            _lib.call('hla_s6_history_reduce_exchange', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws),
+                      self.ws_floats, None, _lib.pointer_array(parts), _lib.pointer_array(flags_out),
+                      _lib.ptr(self.x_counters[2 * i]), world, _lib.REDUCE_AFTER_PARTIALS, stream)
+            own = self.x_bases[rank] + i * world * part_stride * 4
+            z_in = ctypes.c_void_p(own)
+            lse_in = ctypes.c_void_p(own + B * s.heads * width * 4)
+            part_flags = ctypes.c_void_p(self.x_bases[rank] + self.x_region + i * world * 4)
+            part_seen = _lib.ptr(self.x_counters[2 * i + 1])
+            parts, flags = world, _lib.COMBINE_AFTER_PARTIALS   # its producer is the reduce just launched
+        elif self.exchange is not None:
             rank, world, group = self.exchange
             zf = B * s.heads * width
             part_stride = zf + s.heads * B
@@ -257,12 +336,13 @@ class S6DecodeModel:
         # 4. fused combine -> out
         out = self.out[layer, loop]
         _lib.call('hla_s6_decode_combine', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws), self.ws_floats,
-                  _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, None, _lib.ptr(Bm), Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
+                  _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, part_flags, part_seen, None, _lib.ptr(Bm),
+                  Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
                   _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
                   _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
                   _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), None, 0, 0, None,
                   _lib.ptr(out),
-                  out.stride(0), out.stride(1), None, flags, stream)
+                  out.stride(0), out.stride(1), None, flags, None, stream)
 
     def launches_per_step(self):
         """Launches of this library per step (the sequence split adds one reduce per (layer, loop))."""

@@ -2,11 +2,17 @@
 
     python hybrid-latent-attention_b200/profile_step.py [--layers 2] [--batch 64] [--ctx 8192] [--steps 2]
     python hybrid-latent-attention_b200/profile_step.py --prefill [--layers 1] [--prompts 8] [--steps 1]
+    python hybrid-latent-attention_b200/profile_step.py --seq-split 2 [--layers 2] [--batch 4] [--ctx 131072]
 
 Every step issues the four launches per (layer, loop) of ``decode.S6DecodeModel.step`` in order
 (writer, prepare, history split, combine; loop 0 reads the 256-wide latent, loops 1-3 the 512-wide
 one), so ``ncu -k regex:history_split -s 1 -c 2`` selects one launch of each width.  With the
 defaults the device holds about 3 GB.
+
+``--seq-split N`` runs rank 0's share of an N-way sequence split (config 5: B = 4 at ctx 128K) as a
+one-rank job: the latent rows of the first of N page slices, the reduce with its peer-store exchange
+(to this GPU only) and the N = 1 flag wait in the combine; the kernel sequence and sizes per GPU are
+those of the N-GPU step, without the other ranks.
 
 ``--prefill`` runs eager steps of the config-3 prompt-step writer instead (prefill.PrefillWriter: four
 writer launches per layer, N = 512 at loop 0 and 1024 at loops 1-3, 4096 tokens per prompt); with one
@@ -28,9 +34,26 @@ def main():
     ap.add_argument('--steps', type=int, default=2)
     ap.add_argument('--prefill', action='store_true')
     ap.add_argument('--prompts', type=int, default=8)
+    ap.add_argument('--seq-split', type=int, default=0)
     args = ap.parse_args()
     import torch
     dec = importlib.import_module('hybrid-latent-attention_b200.decode')
+    if args.seq_split:
+        import torch.distributed as dist
+        dist.init_process_group('gloo', init_method='tcp://127.0.0.1:29531', rank=0, world_size=1)
+        shape = dec.OuroShape(layers=args.layers, max_position=args.ctx + 128)
+        ctx = [args.ctx] * args.batch
+        split = dec.seq_split_rows([c - shape.window for c in ctx], shape.page, 0, args.seq_split)
+        model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=0,
+                                  latent_rows=[n for _, n in split], exchange=(0, 1, dist.group.WORLD))
+        for _ in range(args.steps):
+            model.step(overlap_writer=False)
+        torch.cuda.synchronize()
+        model.close_exchange()
+        dist.destroy_process_group()
+        print(f'ok: {args.steps} steps of a 1/{args.seq_split} sequence-split slice, '
+              f'{model.launches_per_step()} launches each')
+        return
     if args.prefill:
         pre = importlib.import_module('hybrid-latent-attention_b200.prefill')
         model = pre.PrefillWriter(dec.OuroShape(layers=args.layers), args.prompts, 4096, device='cuda', seed=0)

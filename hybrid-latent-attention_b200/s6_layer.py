@@ -147,9 +147,9 @@ def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_sc
         chunk_args = (_lib.ptr(chunk_o), chunk_o.stride(0), chunk_o.stride(1), _lib.ptr(chunk_lse))
     flags = _lib.COMBINE_AFTER_PARTIALS if (use_history and fused) else 0
     _lib.call('hla_s6_decode_combine', T, H, width, lpage, int(splits), _lib.ptr(ws_ptr), ws_floats, _lib.ptr(z_in),
-              _lib.ptr(lse_in), 1, 0, _lib.ptr(empty), _lib.ptr(B), B.stride(0), B.stride(1), *win_args,
+              _lib.ptr(lse_in), 1, 0, None, None, _lib.ptr(empty), _lib.ptr(B), B.stride(0), B.stride(1), *win_args,
               _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(seq_lens), int(ctx.window), float(ctx.scale), *chunk_args,
-              _lib.ptr(out), out.stride(0), out.stride(1), None, flags, stream)
+              _lib.ptr(out), out.stride(0), out.stride(1), None, flags, None, stream)
     return out
 
 

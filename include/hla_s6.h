@@ -234,14 +234,20 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
  * outside (prefill / mixed steps: hla_s6_chunk_attention merged with hla_s6_window_history),
  * used instead of the decode window; the window arguments other than query_start_loc /
  * num_reqs are then ignored (s6_layer.py:101-115, non-fused branch).
+ * part_flags / part_seen (optional, with z_in): the parts are written by other GPUs
+ * (hla_s6_history_reduce_exchange); the combine first waits - bounded, error_flag receives 4 on
+ * a timeout - until part_flags[0 .. num_parts) are all set, and its last CTA clears them and the
+ * CTA counter part_seen (a zeroed device int) for the slot's next use.
  * flags: HLA_S6_COMBINE_AFTER_PARTIALS declares that the immediately preceding launch on the
- * stream is the hla_s6_history_partials call that produced the partials; the combine is then
- * launched as a programmatic dependent of it, and its B prefetch and exact window (whose inputs
- * must be complete before that history call) overlap the history kernel's tail. */
+ * stream produced this combine's history input - the hla_s6_history_partials call (partials) or,
+ * with z_in, the hla_s6_history_reduce_exchange call; the combine is then launched as a
+ * programmatic dependent of it, and its B prefetch and exact window (whose inputs must be complete
+ * before that launch) overlap the producer's tail. */
 #define HLA_S6_COMBINE_AFTER_PARTIALS 1
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
                           int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
-                          const float* lse_in, int32_t num_parts, int64_t part_stride, const uint8_t* empty,
+                          const float* lse_in, int32_t num_parts, int64_t part_stride, int32_t* part_flags,
+                          int32_t* part_seen, const uint8_t* empty,
                           const void* B, int64_t b_stride_h,
                           int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
                           const void* exact_cache, int64_t exact_num_blocks, int64_t exact_stride_block,
@@ -250,7 +256,37 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens, int32_t window,
                           float scale, const void* chunk_o, int64_t chunk_stride_t, int64_t chunk_stride_h,
                           const float* chunk_lse, void* out, int64_t out_stride_t, int64_t out_stride_h,
-                          float* lse_out, int32_t flags, void* stream);
+                          float* lse_out, int32_t flags, int* error_flag, void* stream);
+
+/* ---------------------------------------------------------------- sequence-split exchange
+ * The reference merges a sequence-split history through NCCL (the all_gather of (z, lse) parts
+ * planned for hla/vllm_latent on 8 GPUs); here the reduce writes its part straight into every
+ * rank's memory over NVLink and raises a flag there, and the combine waits for the flags.
+ * No counterpart call in the reference. */
+
+/* Device memory that the other processes of this node can map (CUDA IPC), zero-filled.
+ * handle receives HLA_S6_PEER_HANDLE_BYTES opaque bytes to pass to hla_s6_peer_open. */
+#define HLA_S6_PEER_HANDLE_BYTES 64
+int hla_s6_peer_alloc(int64_t bytes, void** ptr, void* handle);
+int hla_s6_peer_open(const void* handle, void** ptr);
+int hla_s6_peer_close(void* ptr);
+int hla_s6_peer_free(void* ptr);
+
+/* hla_s6_history_reduce, with this GPU's reduced part (z fp32 [T, H, width] then lse [H, T])
+ * stored into parts[d] for every rank d < world (device pointers into each rank's receive slot,
+ * this rank's own included; 16-byte aligned), after which flags[d] (this rank's flag word in rank
+ * d's flag array for the slot) is set to 1 with system-scope release.  done: a zeroed device
+ * counter private to the slot (left zeroed).  world <= 8.  Pass the same slot's receive region,
+ * flag array and a second counter to hla_s6_decode_combine (z_in, part_flags, part_seen).
+ * launch_flags: HLA_S6_REDUCE_AFTER_PARTIALS declares that the immediately preceding launch on the
+ * stream is the hla_s6_history_partials call that produced the partials (the reduce is then a
+ * programmatic dependent of it, and in turn lets a combine launched with
+ * HLA_S6_COMBINE_AFTER_PARTIALS start its window phase during the reduce). */
+#define HLA_S6_REDUCE_AFTER_PARTIALS 1
+int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,
+                                   int32_t num_kv_splits, float* workspace, int64_t workspace_floats,
+                                   const uint8_t* empty, float* const* parts, int32_t* const* flags, int32_t* done,
+                                   int32_t world, int32_t launch_flags, void* stream);
 
 #ifdef __cplusplus
 }

@@ -2,9 +2,9 @@
 
 CPU: two gloo ranks each attend over their page slice with the oracle, all-gather (z, lse) and
 LSE-merge; the result equals the oracle over the whole history, and the slices tile it exactly.
-GPU (two or more devices): two NCCL ranks run the kernel path - history split on the local slice,
-fp32 reduce, NCCL all-gather of the packed parts, N-part combine - and match the single-GPU path
-over the whole history.
+GPU (two or more devices): two ranks run the kernel path - history split on the local slice, fp32
+reduce, exchange of the packed parts (peer stores + flags, or an NCCL all-gather), N-part combine -
+and match the single-GPU path over the whole history, over two steps.
 """
 import math
 import os
@@ -22,9 +22,9 @@ from oracle import s6_oracle as orc
 PAGE = 16
 
 
-def _run_ranks(fn, world, init, out, limit_s):
+def _run_ranks(fn, world, init, out, limit_s, *extra):
     """Spawn ``world`` ranks and wait at most ``limit_s`` seconds; stragglers are terminated."""
-    ctx = mp.spawn(fn, args=(world, init, out), nprocs=world, join=False)
+    ctx = mp.spawn(fn, args=(world, init, out, *extra), nprocs=world, join=False)
     import time
     deadline = time.time() + limit_s
     while not ctx.join(timeout=5):
@@ -106,10 +106,12 @@ def test_two_gloo_ranks_merge_to_the_full_history():
 
 
 # ----------------------------------------------------------------------------- GPU, NCCL
-def _gpu_rank(rank, world, init, out):
+def _gpu_rank(rank, world, init, out, mode):
+    import datetime
     torch.cuda.set_device(rank)
     dist.init_process_group('nccl', init_method=init, rank=rank, world_size=world,
-                            device_id=torch.device('cuda', rank))
+                            device_id=torch.device('cuda', rank), timeout=datetime.timedelta(seconds=60))
+    part = None
     try:
         dec = pkg('decode')
         lib = pkg('_lib')
@@ -118,7 +120,8 @@ def _gpu_rank(rank, world, init, out):
         full = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=7)
         split = dec.seq_split_rows([max(c - 32, 0) for c in ctx], PAGE, rank, world)
         part = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=7,
-                                 latent_rows=[n for _, n in split], exchange=(rank, world, dist.group.WORLD))
+                                 latent_rows=[n for _, n in split], exchange=(rank, world, dist.group.WORLD),
+                                 exchange_mode=mode)
         # the split model attends over the same latent rows: give it this rank's pages of the full model
         for t, (p0, n) in enumerate(split):
             npg = -(-n // PAGE)
@@ -133,24 +136,35 @@ def _gpu_rank(rank, world, init, out):
         for a, b in zip(part.layers, full.layers):
             a.load_state_dict(b.state_dict())
         stream = lib.stream_of(full.out)
-        for loop in range(shape.loops):
-            acts = full.acts[0, loop].clone()
-            full.layer_loop(0, loop, stream)
-            full.acts[0, loop].copy_(acts)
-            part.layer_loop(0, loop, stream)
-        torch.cuda.synchronize()
-        torch.testing.assert_close(part.out.float(), full.out.float(), atol=2e-2, rtol=1e-2)
+        acts0 = full.acts.clone()
+        # two steps: every exchange slot (and, in peer mode, its flags and counters) is used twice
+        for step in range(2):
+            for loop in range(shape.loops):
+                full.acts[0, loop].copy_(acts0[0, loop])
+                part.acts[0, loop].copy_(acts0[0, loop])
+                full.layer_loop(0, loop, stream)
+                part.layer_loop(0, loop, stream)
+            torch.cuda.synchronize()
+            torch.testing.assert_close(part.out.float(), full.out.float(), atol=2e-2, rtol=1e-2)
+            part.out.zero_()
+        if mode == 'peer':
+            assert int(part.x_counters.abs().sum()) == 0       # counters left zeroed for the next use
         if rank == 0:
             with open(out, 'w') as f:
                 f.write('ok')
     finally:
+        if part is not None:
+            part.close_exchange()
         dist.destroy_process_group()
 
 
 @pytest.mark.gpu
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs two GPUs')
-def test_two_nccl_ranks_match_the_whole_history_path():
+@pytest.mark.parametrize('mode', ['peer', 'nccl'])
+def test_two_ranks_match_the_whole_history_path(mode):
+    """peer: the reduce stores each part into both GPUs' memory and raises flags (one GPU per rank,
+    so the flag waits never run as two launches on one GPU); nccl: all_gather of the parts."""
     with tempfile.TemporaryDirectory() as d:
         init, out = f'file://{os.path.join(d, "rdv")}', os.path.join(d, 'result')
-        _run_ranks(_gpu_rank, 2, init, out, 300)
+        _run_ranks(_gpu_rank, 2, init, out, 300, mode)
         assert open(out).read() == 'ok'
