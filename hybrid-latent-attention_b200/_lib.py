@@ -51,6 +51,8 @@ SIGNATURES = {
                               _i64, _i64, P, _i64,
                               _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32, P, _i64, _i64, P, P,
                               _i64, _i64, P, _i32, P, P],
+    'hla_s6_history_attention_contig': [P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i64, _i32, _i32, _i32,
+                                        _i32, _f32, _i32, P, _i64, P, _i64, _i64, P, P, P, P],
     'hla_s6_peer_alloc': [_i64, P, P],
     'hla_s6_peer_open': [P, P],
     'hla_s6_peer_close': [P],

@@ -101,6 +101,33 @@ int latent_cache_tmap(CUtensorMap* map, const void* cache, int64_t num_blocks, i
   return kStatusOk;
 }
 
+int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, int W, int64_t st_b, int64_t st_n,
+                     int tile) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (st_n * 2) % 16 || (st_b * 2) % 16 || st_n < W || B < 1 || N < 1) {
+    set_error("contiguous K/V need a 16-byte aligned base, row strides that are multiples of 8 elements and "
+              ">= width (key stride %lld, batch stride %lld)", static_cast<long long>(st_n),
+              static_cast<long long>(st_b));
+    return kStatusInvalid;
+  }
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return kStatusCuda;
+  }
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(W / 64), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(st_n * 2), 128, static_cast<cuuint64_t>(st_b * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tile), static_cast<cuuint32_t>(W / 64), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for contiguous K/V", static_cast<int>(r));
+    return kStatusCuda;
+  }
+  return kStatusOk;
+}
+
 static int check_history_args(const HistoryArgs& a) {
   if (a.T < 0 || a.H < 1 || a.H > 16) {
     set_error("history attention needs 1..16 query heads per KV head (got H=%d, T=%d)", a.H, a.T);
@@ -207,6 +234,55 @@ int hla_s6_history_reduce(int32_t num_tokens, int32_t num_heads, int32_t width, 
   if (rc) return rc;
   return history_reduce(a, plan, empty, out, out_stride_t, out_stride_h, out_f32, lse,
                         static_cast<cudaStream_t>(stream));
+}
+
+int hla_s6_history_attention_contig(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k,
+                                    int64_t k_stride_b, int64_t k_stride_n, const void* v, int64_t v_stride_b,
+                                    int64_t v_stride_n, const uint8_t* mask, int64_t mask_stride_b, int32_t batch,
+                                    int32_t num_keys, int32_t num_heads, int32_t width, float scale,
+                                    int32_t num_kv_splits, float* workspace, int64_t workspace_floats, void* z,
+                                    int64_t z_stride_b, int64_t z_stride_h, float* z32, float* lse, int* error_flag,
+                                    void* stream) {
+  if (batch < 0 || num_heads < 1 || num_heads > 16 || num_keys < 1 || !mask || !lse) {
+    set_error("contiguous history needs 1..16 heads, >= 1 key (a storage row), a mask and an lse output");
+    return kStatusInvalid;
+  }
+  if ((q_stride_b % 2) || (q_stride_h % 2) || (reinterpret_cast<uintptr_t>(q) % 4) || (z_stride_b % 2) ||
+      (z_stride_h % 2) || (reinterpret_cast<uintptr_t>(z) % 4) || (z32 && reinterpret_cast<uintptr_t>(z32) % 16)) {
+    set_error("contiguous history: q / z need even strides and a unit last-dim stride, z32 16-byte alignment");
+    return kStatusInvalid;
+  }
+  if (num_kv_splits < 1) {
+    set_error("num_kv_splits must be >= 1");
+    return kStatusInvalid;
+  }
+  ContigArgs c{};
+  c.q = q;
+  c.q_sb = q_stride_b;
+  c.q_sh = q_stride_h;
+  c.k = k;
+  c.k_sb = k_stride_b;
+  c.k_sn = k_stride_n;
+  c.v = v;
+  c.v_sb = v_stride_b;
+  c.v_sn = v_stride_n;
+  c.mask = mask;
+  c.m_sb = mask_stride_b;
+  c.B = batch;
+  c.N = num_keys;
+  c.H = num_heads;
+  c.W = width;
+  c.scale = scale;
+  c.splits = num_kv_splits;
+  c.ws = workspace;
+  c.ws_floats = workspace_floats;
+  c.z = z;
+  c.z_sb = z_stride_b;
+  c.z_sh = z_stride_h;
+  c.z32 = z32;
+  c.lse = lse;
+  c.err = error_flag;
+  return history_attention_contig(c, static_cast<cudaStream_t>(stream));
 }
 
 int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,

@@ -41,6 +41,11 @@ struct HistoryParams {
   int32_t grid;                // CTAs launched (stream mode)
   int32_t stream_mode;         // 1: stream-K over pages, 0: one CTA per row
   int* err;
+  // contiguous layout (the HF engines' reader): every row has contig_n keys in K/V [rows, N, W]
+  // (tile = PG consecutive keys of the row; two tensor maps, K and V) and a per-key mask
+  int32_t contig_n;
+  const uint8_t* mask;  // [rows, N], nonzero = visible
+  int64_t mask_st;
 };
 
 template <int W, int PG>
@@ -71,9 +76,14 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int key_lo, int valid)
   return v;
 }
 
-template <int W, int PG>
+// CONTIG: the contiguous-layout front end (fused_history.py:49-54, history_kernels.py:11-33):
+// `tmap` covers K [rows, N, W] and `tmap_v` V, both as (64, N, W/64, rows) boxes of PG keys, so a
+// tile lands in shared memory exactly as a page of the paged cache does (K slabs, then V slabs);
+// rows have p.contig_n keys and a per-key mask instead of a prefix length.
+template <int W, int PG, bool CONTIG = false>
 __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>::MIN_CTAS)
-    history_split_kernel(const __grid_constant__ CUtensorMap tmap, const HistoryParams p) {
+    history_split_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_v,
+                         const HistoryParams p) {
   using C = HistoryCfg<W, PG>;
   constexpr int NC = C::NC, NT = C::NT, STAGES = C::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -95,7 +105,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
 
   if (p.stream_mode) {
     for (int t = tid; t < T; t += blockDim.x) {
-      const int c = max(p.ctx[t], 0);
+      const int c = CONTIG ? p.contig_n : max(p.ctx[t], 0);
       pref[t + 1] = (c + PG - 1) / PG;
     }
     if (tid == 0) pref[0] = 0;
@@ -140,7 +150,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     row0 = lo;
   } else {
     row0 = blockIdx.x;
-    const int c = max(p.ctx[row0], 0);
+    const int c = CONTIG ? p.contig_n : max(p.ctx[row0], 0);
     p0 = 0;
     p1 = (c + PG - 1) / PG;
     if (p1 == 0) {  // empty row: its slot says so
@@ -194,8 +204,14 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
           }
         }
         mbar_arrive_expect_tx(&full[s], C::PAGE_BYTES);
-        const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
-        tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk);
+        if constexpr (CONTIG) {
+          // keys [lp * PG, lp * PG + PG) of row r; keys past N arrive zero-filled
+          tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, lp * PG, 0, r);
+          tma_load_4d(stages + s * C::PAGE_BYTES + (W / 64) * C::SLAB_BYTES, &tmap_v, &full[s], 0, lp * PG, 0, r);
+        } else {
+          const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
+          tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk);
+        }
       }
     }
     return;
@@ -223,7 +239,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     const int lp = static_cast<int>(g - base);
     if (!seg_open) {
       seg_open = true;
-      ctx_r = max(p.ctx[r], 0);
+      ctx_r = CONTIG ? p.contig_n : max(p.ctx[r], 0);
       const __nv_bfloat16* qr = p.q + static_cast<int64_t>(r) * p.q_st;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
@@ -242,6 +258,21 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       l_run[0] = l_run[1] = 0.f;
     }
     const int s = it % STAGES;
+    // contiguous mode: visibility of this thread's score keys (j * 8 + 2 c4 + e), fetched before the
+    // tile wait so the loads overlap it
+    uint32_t vis = 0xffffffffu;
+    if constexpr (CONTIG) {
+      vis = 0;
+      const int nk = min(PG, ctx_r - lp * PG);
+      const uint8_t* mrow = p.mask + static_cast<int64_t>(r) * p.mask_st + static_cast<int64_t>(lp) * PG;
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int k = j * 8 + 2 * c4 + e;
+          if (k < nk && mrow[k]) vis |= 1u << (2 * j + e);
+        }
+    }
     const bool ok = mbar_wait(&full[s], (it / STAGES) & 1);
     if (!ok) {
       record_error(p.err, kErrWaitFull);
@@ -297,7 +328,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       const int k0 = j * 8 + 2 * c4;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const bool in = (k0 + e) < valid;
+        const bool in = CONTIG ? ((vis >> (2 * j + e)) & 1u) != 0 : (k0 + e) < valid;
         sc[j][e] = in ? sc[j][e] * p.scale_log2 : -INFINITY;
         sc[j][2 + e] = in ? sc[j][2 + e] * p.scale_log2 : -INFINITY;
         mx0 = fmaxf(mx0, sc[j][e]);
@@ -309,15 +340,18 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-    const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
+    // contiguous mode: a row whose keys so far are all masked keeps max -inf; shift by 0 so it
+    // contributes 0, not NaN (paged pages always hold a visible first key, so their max is finite)
+    const float sf0 = (CONTIG && mn0 == -INFINITY) ? 0.f : mn0, sf1 = (CONTIG && mn1 == -INFINITY) ? 0.f : mn1;
+    const float al0 = exp2f(m_run[0] - sf0), al1 = exp2f(m_run[1] - sf1);
     m_run[0] = mn0;
     m_run[1] = mn1;
     float rs0 = 0.f, rs1 = 0.f;
     uint32_t pa[NT / 2][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-      const float e0 = exp2f(sc[j][0] - mn0), e1 = exp2f(sc[j][1] - mn0);
-      const float e2 = exp2f(sc[j][2] - mn1), e3 = exp2f(sc[j][3] - mn1);
+      const float e0 = exp2f(sc[j][0] - sf0), e1 = exp2f(sc[j][1] - sf0);
+      const float e2 = exp2f(sc[j][2] - sf1), e3 = exp2f(sc[j][3] - sf1);
       rs0 += e0 + e1;
       rs1 += e2 + e3;
       pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16(e0, e1);
@@ -370,7 +404,11 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       if (slot >= p.slots_cap) {
         record_error(p.err, kErrSlots);
       } else {
-        const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+        float inv0 = 1.f / l0, inv1 = 1.f / l1;
+        if constexpr (CONTIG) {  // a segment with every key masked: o = 0, lse = -inf
+          if (!(l0 > 0.f)) inv0 = 0.f;
+          if (!(l1 > 0.f)) inv1 = 0.f;
+        }
         float* base0 = p.ws_o + (static_cast<int64_t>(slot) * p.H + g8) * W;
         float* base1 = p.ws_o + (static_cast<int64_t>(slot) * p.H + g8 + 8) * W;
 #pragma unroll
@@ -486,7 +524,8 @@ __global__ void __launch_bounds__(kReduceThreads, 1) history_reduce_kernel(const
                                                                          __nv_bfloat16* __restrict__ out,
                                                                          int64_t o_st, int64_t o_sh,
                                                                          float* __restrict__ out_f32,
-                                                                         float* __restrict__ lse_out) {
+                                                                         float* __restrict__ lse_out,
+                                                                         int64_t lse_st, int64_t lse_sh) {
   const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   float lse;
   const float4 acc = reduce_row<W>(ws_o, ws_lse, meta, stream_mode, t, h, H, empty, lse);
@@ -498,7 +537,7 @@ __global__ void __launch_bounds__(kReduceThreads, 1) history_reduce_kernel(const
     reinterpret_cast<__nv_bfloat162*>(dst)[1] = __floats2bfloat162_rn(acc.z, acc.w);
   }
   if (out_f32) *reinterpret_cast<float4*>(out_f32 + (static_cast<int64_t>(t) * H + h) * W + c) = acc;
-  if (tid == 0 && blockIdx.z == 0 && lse_out) lse_out[static_cast<int64_t>(h) * T + t] = lse;
+  if (tid == 0 && blockIdx.z == 0 && lse_out) lse_out[static_cast<int64_t>(h) * lse_sh + t * lse_st] = lse;
 }
 
 // The sequence-split exchange fused into the reduce: this GPU's part - z fp32 [T, H, W] followed by
@@ -602,7 +641,10 @@ static int launch_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStrea
   p.err = a.err;
   const size_t smem = history_smem_bytes<W, PG>(plan.stream_mode ? a.T : 0);
   occupancy_for<W, PG>();
-  history_split_kernel<W, PG><<<plan.grid, C::THREADS, smem, stream>>>(tmap, p);
+  p.contig_n = 0;
+  p.mask = nullptr;
+  p.mask_st = 0;
+  history_split_kernel<W, PG><<<plan.grid, C::THREADS, smem, stream>>>(tmap, tmap, p);
   return cuda_status(cudaGetLastError(), "history_split_kernel launch");
 }
 
@@ -673,8 +715,73 @@ int history_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t st
   }
 }
 
+template <int W>
+static int launch_contig(const ContigArgs& c, const HistoryPlan& plan, cudaStream_t stream) {
+  constexpr int PG = 16;
+  using C = HistoryCfg<W, PG>;
+  CUtensorMap tk, tv;
+  int rc = contig_rows_tmap(&tk, c.k, c.B, c.N, W, c.k_sb, c.k_sn, PG);
+  if (rc) return rc;
+  if ((rc = contig_rows_tmap(&tv, c.v, c.B, c.N, W, c.v_sb, c.v_sn, PG))) return rc;
+  HistoryParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(c.q);
+  p.q_st = c.q_sb;
+  p.q_sh = c.q_sh;
+  p.T = c.B;
+  p.H = c.H;
+  p.scale_log2 = c.scale * 1.4426950408889634f;
+  p.ws_o = plan.ws_o;
+  p.ws_lse = plan.ws_lse;
+  p.meta = plan.meta;
+  p.slots_cap = plan.slots_cap;
+  p.grid = plan.grid;
+  p.stream_mode = plan.stream_mode;
+  p.err = c.err;
+  p.contig_n = c.N;
+  p.mask = c.mask;
+  p.mask_st = c.m_sb;
+  static unsigned attr_mask = 0;
+  const size_t smem = history_smem_bytes<W, PG>(plan.stream_mode ? c.B : 0);
+  ensure_smem_limit(history_split_kernel<W, PG, true>, static_cast<int>(history_smem_bytes<W, PG>(kHistoryMaxStreamRows)),
+                    attr_mask);
+  history_split_kernel<W, PG, true><<<plan.grid, C::THREADS, smem, stream>>>(tk, tv, p);
+  return cuda_status(cudaGetLastError(), "history_split_kernel (contiguous) launch");
+}
+
+int history_attention_contig(const ContigArgs& c, cudaStream_t stream) {
+  if (c.B == 0) return kStatusOk;
+  HistoryArgs a{};
+  a.T = c.B;
+  a.H = c.H;
+  a.W = c.W;
+  a.page = 16;
+  a.num_kv_splits = c.splits;
+  a.ws = c.ws;
+  a.ws_floats = c.ws_floats;
+  a.waves = 1;
+  a.err = c.err;
+  HistoryPlan plan;
+  int rc = history_plan(a, &plan);
+  if (rc) return rc;
+  switch (c.W) {
+    case 256: rc = launch_contig<256>(c, plan, stream); break;
+    case 512: rc = launch_contig<512>(c, plan, stream); break;
+    case 1024: rc = launch_contig<1024>(c, plan, stream); break;
+    default: set_error("contiguous history width %d unsupported (256, 512, 1024)", c.W); return kStatusInvalid;
+  }
+  if (rc) return rc;
+  // z [B, H, W] (bf16, strided), z32 fp32 [B, H, W] contiguous, lse [B, H]
+  return history_reduce_strided(a, plan, nullptr, c.z, c.z_sb, c.z_sh, c.z32, c.lse, c.H, 1, stream);
+}
+
 int history_reduce(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out, int64_t o_st,
                    int64_t o_sh, float* out_f32, float* lse, cudaStream_t stream) {
+  return history_reduce_strided(a, plan, empty, out, o_st, o_sh, out_f32, lse, 1, a.T, stream);
+}
+
+int history_reduce_strided(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out,
+                           int64_t o_st, int64_t o_sh, float* out_f32, float* lse, int64_t lse_st, int64_t lse_sh,
+                           cudaStream_t stream) {
   if (a.T == 0) return kStatusOk;
   if (a.W != 256 && a.W != 512 && a.W != 1024) {
     set_error("unsupported latent width %d", a.W);
@@ -685,7 +792,7 @@ int history_reduce(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t*
   history_reduce_kernel<WW><<<grid, kReduceThreads, 0, stream>>>(plan.ws_o, plan.ws_lse, plan.meta,             \
                                                                  plan.stream_mode, a.T, a.H, empty,             \
                                                                  static_cast<__nv_bfloat16*>(out), o_st, o_sh, \
-                                                                 out_f32, lse)
+                                                                 out_f32, lse, lse_st, lse_sh)
   switch (a.W) {
     case 256: HLA_REDUCE(256); break;
     case 512: HLA_REDUCE(512); break;

@@ -67,6 +67,38 @@ struct HistoryPlan {
 
 int history_plan(const HistoryArgs& a, HistoryPlan* plan);
 int history_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStream_t stream);
+int history_reduce_strided(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty, void* out,
+                           int64_t o_st, int64_t o_sh, float* out_f32, float* lse, int64_t lse_st, int64_t lse_sh,
+                           cudaStream_t stream);
+
+// Contiguous-layout reader (fused_history.history_attention): q [B, H, W], K / V [B, N, W] (row
+// strides k_sb / k_sn ...), mask [B, N] (uint8), outputs z bf16 [B, H, W] (strided), z32 fp32
+// [B, H, W] contiguous (optional), lse fp32 [B, H].
+struct ContigArgs {
+  const void* q;
+  int64_t q_sb, q_sh;
+  const void* k;
+  int64_t k_sb, k_sn;
+  const void* v;
+  int64_t v_sb, v_sn;
+  const uint8_t* mask;
+  int64_t m_sb;
+  int B, N, H, W;
+  float scale;
+  int splits;
+  float* ws;
+  int64_t ws_floats;
+  void* z;
+  int64_t z_sb, z_sh;
+  float* z32;
+  float* lse;
+  int* err;
+};
+int history_attention_contig(const ContigArgs& c, cudaStream_t stream);
+// 4-D TMA map over a [B, N, W] bf16 tensor: (64, N, W/64, B) with boxes of `tile` rows (capi.cu).
+int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, int W, int64_t st_b, int64_t st_n,
+                     int tile);
+
 // Targets of the fused sequence-split exchange (history_reduce_exchange): this rank's part in every
 // rank's receive slot, this rank's flag word in every rank's flag array for the slot, and the
 // local counter of finished CTAs.

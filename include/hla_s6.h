@@ -88,6 +88,25 @@ int hla_s6_history_reduce(int32_t num_tokens, int32_t num_heads, int32_t width, 
                           void* out, int64_t out_stride_t, int64_t out_stride_h, float* out_f32, float* lse,
                           void* stream);
 
+/* Contiguous-layout latent history reader of the HF reference engines: per row b and head h,
+ * z[b, h] = softmax_n(scale * q[b, h] . k[b, n], over keys n < num_keys with mask[b, n] != 0) . v[b, :],
+ * lse[b, h] its log-sum-exp (natural log).  Rows with no visible key give z = 0, lse = -inf.
+ * q bf16 [B, H, width]; k, v bf16 [B, N, width] (strides per row b and key n, unit last stride,
+ * multiples of 8 elements); mask uint8 [B, N]; z bf16 [B, H, width] (strided), z32 (optional) fp32
+ * [B, H, width] contiguous, lse fp32 [B, H] contiguous.  width 256, 512 or 1024; H <= 16 (MQA: one
+ * K/V row shared by the heads).  The workspace follows hla_s6_history_attention's accounting
+ * (B * num_kv_splits * H * (width + 1) floats).
+ * Replaces the forward of hla/latent/fused_history.py:49-54 (history_attention ->
+ * history_kernels.forward, history_kernels.py:11-33 and 84-89); its torch oracle is
+ * fused_history.reference (fused_history.py:11-20). */
+int hla_s6_history_attention_contig(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k,
+                                    int64_t k_stride_b, int64_t k_stride_n, const void* v, int64_t v_stride_b,
+                                    int64_t v_stride_n, const uint8_t* mask, int64_t mask_stride_b, int32_t batch,
+                                    int32_t num_keys, int32_t num_heads, int32_t width, float scale,
+                                    int32_t num_kv_splits, float* workspace, int64_t workspace_floats, void* z,
+                                    int64_t z_stride_b, int64_t z_stride_h, float* z32, float* lse, int* error_flag,
+                                    void* stream);
+
 /* Host-only: how the history kernel will partition a call (1 = stream-K over pages, 0 = one
  * CTA per row), its grid and its partial-slot capacity.  No counterpart call in the reference;
  * it exposes the split choice the reference makes in s6_ops.py:76-89 (num_kv_splits). */

@@ -155,6 +155,23 @@ def window_history_case(seed=71, heads=16, d=128, page=16, window=32, ctx=(0, 5,
     return dict(q=q, cache_phys=phys, block_table=table, ctx=ctx, window=np.int32(window))
 
 
+def contig_case(seed=81, batch=6, heads=16, width=512, keys=100):
+    """Contiguous-layout reader (hla/latent/fused_history.py:11-20): q [B,H,R], K/V [B,N,R], mask [B,N].
+    Rows: random masks, a fully masked row, a row whose only visible key is the last one, a fully
+    visible row; K at masked keys is poisoned with +inf (the mask must win before the softmax)."""
+    rng = np.random.default_rng(seed)
+    q = _bf16(rng.standard_normal((batch, heads, width), dtype=np.float32))
+    k = _bf16(rng.standard_normal((batch, keys, width), dtype=np.float32))
+    v = _bf16(rng.standard_normal((batch, keys, width), dtype=np.float32))
+    mask = rng.random((batch, keys)) < 0.6
+    mask[1] = False
+    mask[2] = False
+    mask[2, keys - 1] = True
+    mask[3] = True
+    k[~mask] = INF
+    return dict(q=q, k=k, v=v, mask=mask.astype(np.uint8))
+
+
 def meta_cases():
     """Integer metadata cases (test_s6_ops.py:16-27, 51-70)."""
     return dict(

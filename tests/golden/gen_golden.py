@@ -12,6 +12,7 @@ The reference functions called (file:line in the reference project):
   hla/vllm_latent/s6_layer.py:16 latent_inv_freq, :21 latent_rope_table, :32 latent_query,
   :124 write_rows, :135 committed_row
   hla/latent/register.py:28 LatentLayer (write_step / write1 / pack / fields)
+  hla/latent/fused_history.py:11 reference (the contiguous-layout reader's torch definition)
 """
 from __future__ import annotations
 
@@ -141,6 +142,14 @@ def main():
         packed = sl.pack(sl.write(hs)[-1], sl.write1(hs[0]), cos, sin).float().numpy()
     save('writer', wc, first=regs[0], reg1=regs[1], reg2=regs[2], reg3=regs[3], row_l1=rows[0], row_main=rows[3],
          packed=packed)
+
+    # ---- contiguous-layout reader (HF engines)
+    from hla.latent.fused_history import reference as contig_reference
+    for name, kw in (('contig_512', dict(width=512)), ('contig_256', dict(seed=82, width=256, keys=37, batch=4))):
+        cc = cases.contig_case(**kw)
+        scale = 1 / math.sqrt(128)
+        z, lse = contig_reference(T_(cc['q']), T_(cc['k']), T_(cc['v']), T_(cc['mask']).bool(), scale)
+        save(name, cc, z=z.float().numpy(), lse=lse.float().numpy(), scale=np.float64(scale))
 
     # ---- integer metadata
     mc = cases.meta_cases()

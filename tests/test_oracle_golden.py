@@ -31,6 +31,17 @@ def test_history_oracle_matches_reference(name):
     assert (o[empty] == 0).all() and (lse[:, empty] == -INF).all()
 
 
+@pytest.mark.parametrize('name,kw', [('contig_512', dict(width=512)),
+                                     ('contig_256', dict(seed=82, width=256, keys=37, batch=4))])
+def test_contiguous_reader_oracle_matches_reference(name, kw):
+    c = cases.contig_case(**kw)
+    g = load(name, c)
+    z, lse = orc.contiguous_history(c['q'], c['k'], c['v'], c['mask'].astype(bool), float(g['scale']))
+    np.testing.assert_allclose(z, g['z'], rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(lse, g['lse'], rtol=1e-5, atol=2e-6)
+    assert (z[1] == 0).all() and (lse[1] == -INF).all()          # fully masked row
+
+
 def test_window_decode_oracle_matches_reference():
     w = cases.window_case()
     g = load('window_decode', w)
