@@ -307,6 +307,22 @@ int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_
                                    const uint8_t* empty, float* const* parts, int32_t* const* flags, int32_t* done,
                                    int32_t world, int32_t launch_flags, void* stream);
 
+/* Rollout cache export: the latent rows of one finished request - positions 0 .. length-1 of every
+ * layer's main cache [nb, 1, bs, main_width] and loop-1 cache [nb, 1, bs', l1_width] (bf16,
+ * strides per block / row) through each kv group's physical block list (int32, device, *_blocks_len
+ * entries, which must cover ceil(length / block size)) - gathered
+ * into out bf16 [num_layers, length, main_width + l1_width] (main | l1 per row, contiguous), i.e.
+ * the rows of the s6-rollout-cache-v1 snapshot before its device-to-host copy.  main_caches /
+ * l1_caches: host arrays of num_layers (<= 64) device pointers.  A block id outside the cache sets
+ * error_flag (3) and zeroes that part of the row.
+ * Replaces the gather of hla/vllm_latent/cache_export.py:160-174 (RolloutCacheExporter.export). */
+int hla_s6_export_rows(const void* const* main_caches, const void* const* l1_caches, int32_t num_layers,
+                       int64_t main_num_blocks, int64_t main_stride_block, int64_t main_stride_row,
+                       int32_t main_width, int32_t main_block_size, const int32_t* main_blocks, int64_t main_blocks_len,
+                       int64_t l1_num_blocks, int64_t l1_stride_block, int64_t l1_stride_row, int32_t l1_width,
+                       int32_t l1_block_size, const int32_t* l1_blocks, int64_t l1_blocks_len, int64_t length, void* out, int* error_flag,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

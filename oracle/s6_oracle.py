@@ -392,6 +392,26 @@ def scatter_rows(cache, rows, slots):
     return cache
 
 
+# ----------------------------------------------------------------------------- rollout cache export
+ROLLOUT_SCHEMA = 's6-rollout-cache-v1'      # cache_export.py:10
+
+
+def export_rows(main_caches, l1_caches, main_blocks, l1_blocks, block_size, length):
+    """Rows of one finished request as RolloutCacheExporter.export gathers them (cache_export.py:
+    160-174): per layer, positions 0 .. length-1 of the main cache [nb, 1, bs, 2 rank] and of the
+    loop-1 cache [nb, 1, bs, 2 rank1], each through its own kv group's physical block list
+    (``blocks[pos // bs]``, row ``pos % bs``), concatenated main | l1 -> [1, length, 2 rank + 2 rank1]."""
+    pos = np.arange(int(length))
+    rows = []
+    for main, l1 in zip(main_caches, l1_caches):
+        parts = []
+        for cache, blocks in ((main, main_blocks), (l1, l1_blocks)):
+            phys = np.asarray(blocks, dtype=np.int64)[pos // block_size]
+            parts.append(np.asarray(cache)[phys, 0, pos % block_size, :])
+        rows.append(np.concatenate(parts, -1)[None])
+    return tuple(rows)
+
+
 # ----------------------------------------------------------------------------- A8 decode attend
 def attend_decode(q_lat, q_rope, latent_cache, latent_bt, ctx_latent, exact_cache, exact_bt, query_start_loc,
                   seq_lens, window, B, scale, invalid, dt=np.float64):

@@ -172,6 +172,19 @@ def contig_case(seed=81, batch=6, heads=16, width=512, keys=100):
     return dict(q=q, k=k, v=v, mask=mask.astype(np.uint8))
 
 
+def export_case(seed=91, layers=2, blocks=6, block_size=16, main_w=1024, l1_w=512, length=37):
+    """One finished request's rows (cache_export.py:160-174): per-layer bf16 caches, shuffled physical
+    block lists per kv group (main and loop-1 use different blocks), a length that ends mid-block."""
+    rng = np.random.default_rng(seed)
+    main = _bf16(rng.standard_normal((layers, blocks, 1, block_size, main_w), dtype=np.float32))
+    l1 = _bf16(rng.standard_normal((layers, blocks, 1, block_size, l1_w), dtype=np.float32))
+    need = -(-length // block_size)
+    main_blocks = rng.permutation(blocks)[:need].astype(np.int64)
+    l1_blocks = rng.permutation(blocks)[:need].astype(np.int64)
+    return dict(main=main, l1=l1, main_blocks=main_blocks, l1_blocks=l1_blocks, block_size=np.int64(block_size),
+                length=np.int64(length))
+
+
 def meta_cases():
     """Integer metadata cases (test_s6_ops.py:16-27, 51-70)."""
     return dict(

@@ -13,6 +13,8 @@ The reference functions called (file:line in the reference project):
   :124 write_rows, :135 committed_row
   hla/latent/register.py:28 LatentLayer (write_step / write1 / pack / fields)
   hla/latent/fused_history.py:11 reference (the contiguous-layout reader's torch definition)
+  hla/vllm_latent/cache_export.py:13 RolloutCacheExporter (begin / observe / export / finish), driven
+  through a stand-in runner that exposes the attributes the exporter reads
 """
 from __future__ import annotations
 
@@ -150,6 +152,41 @@ def main():
         scale = 1 / math.sqrt(128)
         z, lse = contig_reference(T_(cc['q']), T_(cc['k']), T_(cc['v']), T_(cc['mask']).bool(), scale)
         save(name, cc, z=z.float().numpy(), lse=lse.float().numpy(), scale=np.float64(scale))
+
+    # ---- rollout cache export (the reference exporter on a stand-in runner)
+    import tempfile
+    from types import SimpleNamespace as NS
+    from hla.vllm_latent.cache_export import RolloutCacheExporter
+    ec = cases.export_case()
+    L, bs, length = ec['main'].shape[0], int(ec['block_size']), int(ec['length'])
+    main = [T_(ec['main'][i]).bfloat16() for i in range(L)]
+    l1 = [T_(ec['l1'][i]).bfloat16() for i in range(L)]
+    names = [f'{i}.{kind}' for i in range(L) for kind in ('main', 'l1')]
+    layers = [NS(self_attn=NS(attn_main=NS(layer_name=f'{i}.main', kv_cache=main[i]),
+                              attn_l1=NS(layer_name=f'{i}.l1', kv_cache=l1[i]))) for i in range(L)]
+    body = NS(latent_cfg=dict(num_layers=L), layers=layers)
+    group_tables = [T_(ec['main_blocks'])[None], T_(ec['l1_blocks'])[None]]
+    tables = [NS(num_blocks_per_row=[t.shape[1]], block_size=bs, get_cpu_tensor=(lambda t=t: t))
+              for t in group_tables]
+    batch = NS(req_id_to_index={'r': 0}, req_ids=['r'], num_computed_tokens_cpu=[0], block_table=tables)
+    runner = NS(get_model=lambda: NS(model=body), speculative_config=None, input_batch=batch,
+                kv_cache_config=NS(kv_cache_groups=[NS(layer_names=[n for n in names if n.endswith('main')]),
+                                                    NS(layer_names=[n for n in names if n.endswith('l1')])]),
+                requests={'r': NS(prompt_token_ids=list(range(length)))})
+    runner._update_states = lambda schedule: None
+    def execute(schedule):
+        runner._update_states(schedule)
+        runner.execute_model_state = NS(logits=torch.zeros(1, 4))
+    runner.execute_model = execute
+    with tempfile.TemporaryDirectory() as d:
+        exporter = RolloutCacheExporter(runner)
+        exporter.begin(Path(d) / 'v0', 0)
+        runner.execute_model(NS(finished_req_ids=set(), num_scheduled_tokens={'r': length},
+                                total_num_scheduled_tokens=length))
+        ref = exporter.finish()['snapshots']['r']
+        payload = torch.load(ref['path'], map_location='cpu', weights_only=True)
+    assert payload['schema'] == 's6-rollout-cache-v1' and payload['length'] == length
+    save('export', ec, rows=np.stack([r.float().numpy() for r in payload['rows']]))
 
     # ---- integer metadata
     mc = cases.meta_cases()

@@ -42,6 +42,26 @@ def test_contiguous_reader_oracle_matches_reference(name, kw):
     assert (z[1] == 0).all() and (lse[1] == -INF).all()          # fully masked row
 
 
+def test_export_oracle_matches_reference_known_answer():
+    """The reference's own known answer (hla/tests/test_rollout_cache.py:36-37): fp32 caches
+    arange(3*1*2*w) of widths 4 and 2, main blocks [2, 0], loop-1 blocks [1, 2], block size 2,
+    three positions."""
+    main = np.arange(3 * 1 * 2 * 4, dtype=np.float32).reshape(3, 1, 2, 4)
+    l1 = np.arange(3 * 1 * 2 * 2, dtype=np.float32).reshape(3, 1, 2, 2)
+    expected = np.concatenate([main[[2, 2, 0], 0, [0, 1, 0]], l1[[1, 1, 2], 0, [0, 1, 0]]], -1)[None]
+    rows = orc.export_rows([main], [l1], [2, 0], [1, 2], 2, 3)
+    assert len(rows) == 1
+    np.testing.assert_array_equal(rows[0], expected)
+
+
+def test_export_oracle_matches_reference_exporter():
+    ec = cases.export_case()
+    g = load('export', ec)
+    rows = orc.export_rows(list(ec['main']), list(ec['l1']), ec['main_blocks'], ec['l1_blocks'],
+                           int(ec['block_size']), int(ec['length']))
+    np.testing.assert_array_equal(np.stack(rows), g['rows'])
+
+
 def test_window_decode_oracle_matches_reference():
     w = cases.window_case()
     g = load('window_decode', w)
