@@ -1,6 +1,6 @@
 """Benchmark of the B200 S6 hybrid decode path (BASELINE config 2 by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5|contig|export]
 
 One step = one decode step of an Ouro-1.4B-shaped S6 model's attention path: 24 layers x 4 loops
 of (writer projection, latent query, exact RoPE + window append, paged latent-history read,
@@ -15,6 +15,9 @@ copied host->device from pinned memory and its outputs read back, inside the tim
 roofline: the dominant kernel (history split) timed alone in a graph of its 96 launches.
 cpu_baseline / --impl reference: the CPU oracle (numpy fp32 restatement of the reference's
 torch path) on a bounded sample of the same workload, extrapolated to a step.
+
+--config contig measures the HF engines' contiguous-layout reader (fused_history.history_attention) at
+config-2 scale; --config export the rollout cache export of one 8192-token request (24 layers).
 
 --config 3 measures the latent writer of a prompt step instead (8 prompts x 4096 tokens, 24 layers x
 4 loops of writer GEMM + bf16 register add + committed-row RoPE and scatter, tcgen05): rows/s, with
@@ -41,6 +44,8 @@ PKG = 'hybrid-latent-attention_b200'
 FALLBACK_HBM_GBS = 6650.0
 METRIC = 'S6 decode tokens/s and latent-history HBM GB/s (% roofline), B=64 ctx 8K, 1/2/4/8 GPU'
 METRIC3 = 'S6 latent writer (prefill) committed rows/s and tensor TFLOP/s (% roofline), 8 x 4096 prompt tokens'
+METRIC_CONTIG = 'contiguous-layout latent history reader tokens/s and HBM GB/s (% roofline), B=64, 8160 keys'
+METRIC_EXPORT = 'rollout cache export rows/s and HBM GB/s (% roofline), one 8192-token request, 24 layers'
 FALLBACK_TFLOPS = 1400.0
 
 
@@ -610,13 +615,206 @@ def run_prefill(args):
     return line
 
 
+def _events_ms(torch, fn, reps):
+    """Device time of ``reps`` calls of fn on the current stream (ms per call), synchronized around."""
+    st = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(reps):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_contig(args):
+    """--config contig: the contiguous-layout reader of the HF engines (fused_history.history_attention)
+    at config-2 scale - 64 rows, 8160 visible keys (ctx 8192 minus the 32-row window) - for the 96
+    reads of a decode step (24 layers x 3 reads at width 512 + 1 at width 256), one GPU."""
+    import numpy as np
+    import torch
+    rank, world, local = dist_env()
+    if world > 1 and rank != 0:
+        return None
+    torch.cuda.set_device(local)
+    importlib.import_module(f'{PKG}._lib').load()
+    fh = importlib.import_module(f'{PKG}.fused_history')
+    dec = importlib.import_module(f'{PKG}.decode')
+    s = dec.OuroShape()
+    B, N, H = 64, 8192 - s.window, s.heads
+    g = torch.Generator(device='cuda').manual_seed(args.seed)
+    kv = {w: [(torch.randn(B, N, w, generator=g, device='cuda').to(torch.bfloat16),
+               torch.randn(B, N, w, generator=g, device='cuda').to(torch.bfloat16)) for _ in range(s.layers)]
+          for w in (s.rank, s.rank1)}
+    q = {w: torch.randn(B, H, w, generator=g, device='cuda').to(torch.bfloat16) for w in (s.rank, s.rank1)}
+    mask = torch.ones(B, N, dtype=torch.bool, device='cuda')
+    scale = s.head_dim ** -0.5
+
+    def step():
+        for loop in range(s.loops):
+            w = s.rank1 if loop == 0 else s.rank
+            for layer in range(s.layers):
+                k, v = kv[w][layer]
+                fh.history_attention(q[w], k, v, mask, scale)
+
+    step()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    with ClockSampler(local) as clk:
+        ms = time_graph(torch, graph, args.steps, None) / args.steps
+    bytes_step = s.layers * B * N * 2 * 2 * ((s.loops - 1) * s.rank + s.rank1)
+    peak, peak_kind = peaks()
+    achieved = bytes_step / (ms / 1e3) / 1e9
+    # e2e: q and mask in from pinned memory, z and lse out, each read of the step
+    hq = {w: q[w].cpu().pin_memory() for w in q}
+    hm = mask.cpu().pin_memory()
+    outs = []
+
+    def e2e_step():
+        outs.clear()
+        for loop in range(s.loops):
+            w = s.rank1 if loop == 0 else s.rank
+            qq = hq[w].to('cuda', non_blocking=True)
+            mm = hm.to('cuda', non_blocking=True)
+            for layer in range(s.layers):
+                k, v = kv[w][layer]
+                z, lse = fh.history_attention(qq, k, v, mm, scale)
+                outs.append((z.to('cpu', non_blocking=True), lse.to('cpu', non_blocking=True)))
+    e2e_step()
+    ms_e2e = _events_ms(torch, e2e_step, max(3, args.steps // 4))
+    h2d = s.loops * (B * H * s.rank * 2 + B * N)
+    d2h = s.layers * s.loops * B * H * (s.rank * 2 + 4)
+    cpu = None
+    if not args.no_cpu:
+        from oracle import s6_oracle as orc
+        use_all_host_threads()
+        rows = 1
+        kk = kv[s.rank][0][0][:rows].float().cpu().numpy()
+        vv = kv[s.rank][0][1][:rows].float().cpu().numpy()
+        qq = q[s.rank][:rows].float().cpu().numpy()
+        mm = np.ones((rows, N), dtype=bool)
+        orc.contiguous_history(qq, kk, vv, mm, scale, dt=np.float32)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            orc.contiguous_history(qq, kk, vv, mm, scale, dt=np.float32)
+        sec_row = (time.perf_counter() - t0) / 3 / rows
+        sec = sec_row * B * s.layers * ((s.loops - 1) + s.rank1 / s.rank)
+        cpu = {'value': B / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
+               'sample': f'oracle numpy fp32 contiguous reader, {rows} of {B} rows at width {s.rank} x {N} keys, '
+                         f'extrapolated to 96 reads of a step (the width-256 read scaled by width)'}
+    line = {'metric': METRIC_CONTIG, 'value': B / (ms / 1e3), 'unit': 'tokens/s', 'n_gpus': 1, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
+            'config': {'workload': 'contiguous-layout latent history reader (fused_history.history_attention '
+                                   'forward): 96 reads of a decode step, K/V [64, 8160, R] per layer, all keys '
+                                   'visible', 'global_batch': B, 'keys': N, 'widths': [s.rank, s.rank1],
+                       'l2': 'inputs larger than L2 (K/V ~38 GB), no flush'},
+            'roofline': {'bound': 'hbm', 'kernel': 'history_split_kernel (contiguous front end) + reduce, the whole '
+                                                   'step', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
+                         'frac': achieved / peak, 'peak_source': peak_kind, 'bytes_per_step': bytes_step,
+                         'traffic': None},
+            'cpu_baseline': cpu,
+            'e2e': {'value': B / (ms_e2e / 1e3), 'unit': 'tokens/s', 'h2d_bytes_per_step': h2d,
+                    'd2h_bytes_per_step': d2h,
+                    'path': 'fused_history.history_attention per read, q and mask copied in from pinned memory per '
+                            'loop, z and lse copied out per read'},
+            'gpu_launches': 2 * s.layers * s.loops * args.steps, 'clocks': clk.summary()}
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def run_export(args):
+    """--config export: the rollout cache export of one finished 8192-token request over 24 layers
+    (cache_export.export_rows: one gather launch, one pinned copy out), one GPU."""
+    import numpy as np
+    import torch
+    rank, world, local = dist_env()
+    if world > 1 and rank != 0:
+        return None
+    torch.cuda.set_device(local)
+    lib = importlib.import_module(f'{PKG}._lib')
+    lib.load()
+    ce = importlib.import_module(f'{PKG}.cache_export')
+    dec = importlib.import_module(f'{PKG}.decode')
+    s = dec.OuroShape()
+    L, bs, length = s.layers, s.page, 8192
+    need = length // bs
+    nb = 4 * need                          # the request's blocks among others' (shuffled)
+    g = torch.Generator(device='cuda').manual_seed(args.seed)
+    main = [torch.randn(nb, 1, bs, 2 * s.rank, generator=g, device='cuda').to(torch.bfloat16) for _ in range(L)]
+    l1 = [torch.randn(nb, 1, bs, 2 * s.rank1, generator=g, device='cuda').to(torch.bfloat16) for _ in range(L)]
+    rng = np.random.default_rng(args.seed)
+    mb = torch.from_numpy(rng.permutation(nb)[:need].astype(np.int32)).cuda()
+    lb = torch.from_numpy(rng.permutation(nb)[:need].astype(np.int32)).cuda()
+    W = 2 * s.rank + 2 * s.rank1
+    out = torch.empty(L, length, W, dtype=torch.bfloat16, device='cuda')
+    mp = lib.pointer_array([c.data_ptr() for c in main])
+    lp = lib.pointer_array([c.data_ptr() for c in l1])
+    st = lib.stream_of(out)
+
+    def gather():
+        lib.call('hla_s6_export_rows', mp, lp, L, nb, main[0].stride(0), main[0].stride(2), 2 * s.rank, bs,
+                 lib.ptr(mb), mb.numel(), nb, l1[0].stride(0), l1[0].stride(2), 2 * s.rank1, bs, lib.ptr(lb),
+                 lb.numel(), length, lib.ptr(out), None, st)
+    for _ in range(args.warmup):
+        gather()
+    with ClockSampler(local) as clk:
+        ms = _events_ms(torch, gather, args.steps)
+    bytes_step = 2 * L * length * W * 2          # read + write
+    peak, peak_kind = peaks()
+    achieved = bytes_step / (ms / 1e3) / 1e9
+    for _ in range(2):
+        ce.export_rows(main, l1, mb, lb, length, bs)
+    ms_e2e = _events_ms(torch, lambda: ce.export_rows(main, l1, mb, lb, length, bs), max(3, args.steps // 10))
+    cpu = None
+    if not args.no_cpu:
+        from oracle import s6_oracle as orc
+        layers = 2
+        mh = [m.view(torch.int16).cpu().numpy() for m in main[:layers]]   # bf16 bits: a byte copy
+        lh = [x.view(torch.int16).cpu().numpy() for x in l1[:layers]]
+        mbh, lbh = mb.cpu().numpy(), lb.cpu().numpy()
+        orc.export_rows(mh, lh, mbh, lbh, bs, length)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            orc.export_rows(mh, lh, mbh, lbh, bs, length)
+        sec = (time.perf_counter() - t0) / 3 * (L / layers)
+        cpu = {'value': L * length / sec, 'unit': 'rows/s', 'cores': 1, 'kind': 'port',
+               'sample': f'oracle numpy gather (the reference exporter\'s indexing) of {layers} of {L} layers, '
+                         f'host-resident caches, extrapolated'}
+    line = {'metric': METRIC_EXPORT, 'value': L * length / (ms / 1e3), 'unit': 'rows/s', 'n_gpus': 1,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
+            'config': {'workload': 'rollout cache export gather of one finished request: 24 layers x 8192 positions '
+                                   'x (1024 main + 512 loop-1) bf16, shuffled blocks', 'length': length,
+                       'layers': L, 'l2': 'caches 1.2 GB (larger than L2), no flush'},
+            'roofline': {'bound': 'hbm', 'kernel': 'export_rows_kernel', 'achieved': achieved, 'peak': peak,
+                         'unit': 'GB/s', 'frac': achieved / peak, 'peak_source': peak_kind,
+                         'bytes_per_step': bytes_step, 'traffic': None},
+            'cpu_baseline': cpu,
+            'e2e': {'value': L * length / (ms_e2e / 1e3), 'unit': 'rows/s', 'h2d_bytes_per_step': 2 * need * 4,
+                    'd2h_bytes_per_step': L * length * W * 2,
+                    'path': 'cache_export.export_rows: block lists in, rows out into pinned host memory'},
+            'gpu_launches': args.steps, 'clocks': clk.summary()}
+    print(json.dumps(line), flush=True)
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', type=int, default=2, choices=[2, 3, 4, 5])
+    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5', 'contig', 'export'])
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
     ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')
@@ -627,6 +825,14 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
+    if args.config in ('contig', 'export'):
+        if args.impl == 'reference':
+            print(json.dumps({'impl': 'reference', 'unavailable': f'--config {args.config} has no reference arm; '
+                              'its line carries the oracle as cpu_baseline'}), flush=True)
+            return
+        (run_contig if args.config == 'contig' else run_export)(args)
+        return
+    args.config = int(args.config)
     if args.impl == 'reference':
         run_reference(args)
     elif args.config == 3:
