@@ -55,6 +55,8 @@ SIGNATURES = {
                                         _i32, _f32, _i32, P, _i64, P, _i64, _i64, P, P, P, P],
     'hla_s6_export_rows': [P, P, _i32, _i64, _i64, _i64, _i32, _i32, P, _i64, _i64, _i64, _i64, _i32, _i32, P, _i64,
                            _i64, P, P, P],
+    'hla_s6_history_attention_heads': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32, P, _i64,
+                                       _i32, P, _i32, _i32, _f32, _i32, P, _i64, P, P, _i64, _i64, P, P, P],
     'hla_s6_peer_alloc': [_i64, P, P],
     'hla_s6_peer_open': [P, P],
     'hla_s6_peer_close': [P],

@@ -136,19 +136,59 @@ def history_attention(q_lat, cache, block_table, ctx, scale, num_kv_splits, work
 
 def history_attention_kv(q, k, v, block_table, ctx, scale, num_kv_splits, workspace, k_scale, v_scale, backend,
                          empty=None, mla=False):
-    """Paged attention of ``q[T,H,Lk]`` over ``k[num_blocks,kvH,block,Lk]`` / ``v[...,Lv]`` (reference
-    s6_ops.py:128-161).  The B200 kernel serves the S6 MQA layout: ``kvH == 1`` with ``k`` and
-    ``v`` the two halves of one ``[num_blocks, 1, block, 2W]`` cache (``Lk == Lv``).  Other
-    layouts (per-head caches, the LLA ``mla`` row) raise ``ValueError``."""
+    """Paged attention of ``q[T,H,Lk]`` over the first ``ctx[t]`` rows of ``k[num_blocks,kvH,block,Lk]`` /
+    ``v[...,Lv]`` (reference s6_ops.py:128-161), ``H`` a multiple of ``kvH``.  Two layouts run on B200:
+
+    * the S6 MQA cache: ``kvH == 1`` with ``k`` and ``v`` the two halves of one ``[num_blocks, 1,
+      block, 2W]`` cache (``Lk == Lv``) -> the paged MQA reader (``history_attention``);
+    * a per-head cache read MLA-style (``mla=True``, LLA: ``k = cache[..., :r + d_rope]``,
+      ``v = cache[..., :r]``): ``v`` must be the first ``Lv`` columns of ``k``'s rows -> the per-head
+      reader, which reads each row once.
+
+    Returns ``(o[T,H,Lv] bf16, lse[H,T] fp32)``; empty rows give ``o = 0``, ``lse = -inf``.  Other
+    layouts raise ``ValueError``."""
     _require(backend, 'history')
+    prefix_view = (v.data_ptr() == k.data_ptr() and v.stride() == k.stride() and v.shape[:3] == k.shape[:3]
+                   and v.shape[-1] <= k.shape[-1])
+    if mla or k.shape[1] != 1:
+        if not prefix_view:
+            raise ValueError('b200 per-head history reads the MLA row layout: v must be the first Lv columns of k')
+        return _history_heads(q, k, v.shape[-1], block_table, ctx, scale, num_kv_splits, workspace, empty)
     W = q.shape[-1]
-    if mla or k.shape[1] != 1 or v.shape[-1] != W or k.shape[-1] != W:
-        raise ValueError('b200 history kernel supports the MQA S6 cache (kvH = 1, Lk = Lv) only')
+    if v.shape[-1] != W or k.shape[-1] != W:
+        raise ValueError('b200 MQA history needs Lk == Lv == q width')
     if k.stride() != v.stride() or v.data_ptr() != k.data_ptr() + W * k.element_size():
         raise ValueError('b200 history kernel needs k and v to be the K/V halves of one latent cache')
     cache = torch.as_strided(k, (k.shape[0], 1, k.shape[2], 2 * W), k.stride())
     return history_attention(q, cache, block_table, ctx, scale, num_kv_splits, workspace, k_scale, v_scale,
                              backend, empty)
+
+
+def _history_heads(q, k, Lv, block_table, ctx, scale, num_kv_splits, workspace, empty):
+    _check_cuda(q, k, block_table, ctx)
+    if q.dim() != 3 or q.stride(-1) != 1 or q.dtype != torch.bfloat16:
+        raise ValueError('q must be bf16 [T, H, Lk] with a unit last-dim stride')
+    if k.dim() != 4 or k.dtype != torch.bfloat16 or k.stride(-1) != 1:
+        raise ValueError('the per-head cache must be a bf16 [num_blocks, kvH, block, Lk] view with unit last stride')
+    if block_table.dtype != torch.int32 or ctx.dtype != torch.int32 or block_table.stride(-1) != 1:
+        raise ValueError('block_table and ctx must be int32 (table with a unit last-dim stride)')
+    T, H, Lk = q.shape
+    nb, kvh, page, _ = k.shape
+    if k.shape[-1] != Lk or H % kvh:
+        raise ValueError(f'q [T, H, {Lk}] does not match the cache rows ({k.shape[-1]}) / {kvh} KV heads')
+    o = torch.empty(T, H, Lv, dtype=q.dtype, device=q.device)
+    lse = torch.empty(H, T, dtype=torch.float32, device=q.device)
+    ws = workspace.attn_logits(T, H, num_kv_splits, Lv, q.device)
+    emp = None
+    if empty is not None:
+        emp = empty.to(torch.uint8) if empty.dtype != torch.bool else empty
+    ctx_c = ctx.contiguous()
+    _lib.call('hla_s6_history_attention_heads', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(k), nb, k.stride(0),
+              k.stride(1), k.stride(2), kvh, Lk, Lv, page, _lib.ptr(block_table), block_table.stride(0),
+              block_table.shape[1], _lib.ptr(ctx_c), T, H, float(scale), int(num_kv_splits), _lib.ptr(workspace.buffer),
+              ws.numel(), _lib.ptr(emp), _lib.ptr(o), o.stride(0), o.stride(1), _lib.ptr(lse), None,
+              _lib.stream_of(q))
+    return o, lse
 
 
 def _bool_ptr(mask):

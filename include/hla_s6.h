@@ -107,6 +107,26 @@ int hla_s6_history_attention_contig(const void* q, int64_t q_stride_b, int64_t q
                                     int64_t z_stride_b, int64_t z_stride_h, float* z32, float* lse, int* error_flag,
                                     void* stream);
 
+/* Per-head paged history (the LLA MLA-style serving path): query head h of token t attends over the
+ * first ctx[t] rows of KV head h / (H / kv_heads) of cache [num_blocks, kv_heads, page, >= key_width]
+ * (bf16, strides per block / head / row, unit last stride, multiples of 8 elements), scoring the
+ * whole key_width row against q [T, H, key_width] and averaging its first value_width columns (the
+ * row [c | rotated k_rope] read once; value_width <= 512, key_width <= 1024, page 16).
+ * out bf16 [T, H, value_width] (strided), lse fp32 [H, T]; empty rows (ctx 0 or empty[t]) give
+ * o = 0, lse = -inf.  Workspace: T * H * num_kv_splits * (value_width + 1) floats, the reference's
+ * attn_logits layout.  A block id outside the cache sets error_flag (3) and reads as zeros.
+ * Replaces hla/vllm_latent/s6_ops.py:128-161 history_attention_kv(..., mla=True) (vLLM
+ * decode_attention_fwd_grouped with IS_MLA), as lla_layer.attend calls it (lla_layer.py:67-74). */
+int hla_s6_history_attention_heads(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
+                                   int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
+                                   int64_t cache_stride_row, int32_t kv_heads, int32_t key_width,
+                                   int32_t value_width, int32_t page, const int32_t* block_table,
+                                   int64_t block_table_stride, int32_t max_blocks, const int32_t* ctx,
+                                   int32_t num_tokens, int32_t num_heads, float scale, int32_t num_kv_splits,
+                                   float* workspace, int64_t workspace_floats, const uint8_t* empty, void* out,
+                                   int64_t out_stride_t, int64_t out_stride_h, float* lse, int* error_flag,
+                                   void* stream);
+
 /* Host-only: how the history kernel will partition a call (1 = stream-K over pages, 0 = one
  * CTA per row), its grid and its partial-slot capacity.  No counterpart call in the reference;
  * it exposes the split choice the reference makes in s6_ops.py:76-89 (num_kv_splits). */

@@ -185,6 +185,30 @@ def export_case(seed=91, layers=2, blocks=6, block_size=16, main_w=1024, l1_w=51
                 length=np.int64(length))
 
 
+def heads_case(seed=101, heads=16, kv_heads=16, rank=128, d_rope=32, page=16, ctx=(0, 1, 17, 100, 250)):
+    """Per-head cache read MLA-style (lla_layer.py:67-74 -> s6_ops.py:128-161, mla=True): q [T,H,r+d_rope],
+    cache [nb, kvH, page, r + d_rope], v = the first r columns of each row.  Block 0 (+inf) sits under the
+    stale table columns and the rows past ctx are +inf, so only visible rows may be read."""
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(ctx, dtype=np.int32)
+    T, Lk = ctx.shape[0], rank + d_rope
+    need = -(-np.maximum(ctx, 1) // page)
+    mb = int(need.max()) + 2
+    nb = int(need.sum()) + 1
+    cache = _bf16(rng.standard_normal((nb, kv_heads, page, Lk), dtype=np.float32))
+    cache[0] = INF
+    table = np.zeros((T, mb), dtype=np.int32)
+    free = rng.permutation(np.arange(1, nb)).astype(np.int32)
+    k = 0
+    for t in range(T):
+        table[t, :need[t]] = free[k:k + need[t]]
+        if ctx[t] % page:
+            cache[table[t, need[t] - 1], :, ctx[t] % page:] = INF      # rows past ctx in the last page
+        k += need[t]
+    q = _bf16(rng.standard_normal((T, heads, Lk), dtype=np.float32))
+    return dict(q=q, cache=cache, block_table=table, ctx=ctx, rank=np.int32(rank))
+
+
 def meta_cases():
     """Integer metadata cases (test_s6_ops.py:16-27, 51-70)."""
     return dict(

@@ -153,6 +153,18 @@ def main():
         z, lse = contig_reference(T_(cc['q']), T_(cc['k']), T_(cc['v']), T_(cc['mask']).bool(), scale)
         save(name, cc, z=z.float().numpy(), lse=lse.float().numpy(), scale=np.float64(scale))
 
+    # ---- per-head history read MLA-style (the LLA serving path)
+    for name, kw in (('heads_lla', dict()), ('heads_gqa', dict(seed=102, kv_heads=4, rank=64, d_rope=32,
+                                                              ctx=(40, 0, 16, 333)))):
+        hc = cases.heads_case(**kw)
+        r = int(hc['rank'])
+        cache = T_(hc['cache'])
+        ctx = T_(hc['ctx'])
+        ws = s6_ops.S6Workspace(16, r, 64)          # unused by the torch backend
+        o, lse = s6_ops.history_attention_kv(T_(hc['q']), cache, cache[..., :r], T_(hc['block_table']), ctx,
+                                             1 / math.sqrt(128), 4, ws, None, None, 'torch', mla=True)
+        save(name, hc, o=o.numpy(), lse=lse.numpy(), scale=np.float64(1 / math.sqrt(128)))
+
     # ---- rollout cache export (the reference exporter on a stand-in runner)
     import tempfile
     from types import SimpleNamespace as NS

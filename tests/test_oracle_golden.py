@@ -62,6 +62,19 @@ def test_export_oracle_matches_reference_exporter():
     np.testing.assert_array_equal(np.stack(rows), g['rows'])
 
 
+@pytest.mark.parametrize('name,kw', [('heads_lla', dict()),
+                                     ('heads_gqa', dict(seed=102, kv_heads=4, rank=64, d_rope=32, ctx=(40, 0, 16, 333)))])
+def test_per_head_history_oracle_matches_reference(name, kw):
+    hc = cases.heads_case(**kw)
+    g = load(name, hc)
+    r = int(hc['rank'])
+    o, lse = orc.history_attention_kv(hc['q'], hc['cache'], hc['cache'][..., :r], hc['block_table'], hc['ctx'],
+                                      float(g['scale']))
+    assert np.isfinite(o).all()
+    np.testing.assert_allclose(o, g['o'], rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(lse, g['lse'], rtol=1e-5, atol=2e-6)
+
+
 def test_window_decode_oracle_matches_reference():
     w = cases.window_case()
     g = load('window_decode', w)
