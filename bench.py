@@ -1,6 +1,7 @@
 """Benchmark of the B200 S6 hybrid decode path (BASELINE config 2 by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5|contig|export]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 2|3|4|5|contig|export|heads]
 
 One step = one decode step of an Ouro-1.4B-shaped S6 model's attention path: 24 layers x 4 loops
 of (writer projection, latent query, exact RoPE + window append, paged latent-history read,
@@ -17,7 +18,8 @@ cpu_baseline / --impl reference: the CPU oracle (numpy fp32 restatement of the r
 torch path) on a bounded sample of the same workload, extrapolated to a step.
 
 --config contig measures the HF engines' contiguous-layout reader (fused_history.history_attention) at
-config-2 scale; --config export the rollout cache export of one 8192-token request (24 layers).
+config-2 scale; --config export the rollout cache export of one 8192-token request (24 layers);
+--config heads the per-head (LLA MLA-style) history reader at B = 64, ctx 8192.
 
 --config 3 measures the latent writer of a prompt step instead (8 prompts x 4096 tokens, 24 layers x
 4 loops of writer GEMM + bf16 register add + committed-row RoPE and scatter, tcgen05): rows/s, with
@@ -46,6 +48,7 @@ METRIC = 'S6 decode tokens/s and latent-history HBM GB/s (% roofline), B=64 ctx 
 METRIC3 = 'S6 latent writer (prefill) committed rows/s and tensor TFLOP/s (% roofline), 8 x 4096 prompt tokens'
 METRIC_CONTIG = 'contiguous-layout latent history reader tokens/s and HBM GB/s (% roofline), B=64, 8160 keys'
 METRIC_EXPORT = 'rollout cache export rows/s and HBM GB/s (% roofline), one 8192-token request, 24 layers'
+METRIC_HEADS = 'per-head (LLA MLA-style) latent history reader tokens/s and HBM GB/s (% roofline), B=64 ctx 8K'
 FALLBACK_TFLOPS = 1400.0
 
 
@@ -732,6 +735,73 @@ def run_contig(args):
     return line
 
 
+def run_heads(args):
+    """--config heads: the per-head history reader of the LLA serving path (history_attention_kv,
+    mla=True) at config-2 scale - 64 sequences at ctx 8192, 16 KV heads, rows [c (rank) | k_rope
+    (d_rope)] - for the 4 loops of 6 layers (each layer's cache is read at every loop), one GPU."""
+    import numpy as np
+    import torch
+    rank_, world, local = dist_env()
+    if world > 1 and rank_ != 0:
+        return None
+    torch.cuda.set_device(local)
+    importlib.import_module(f'{PKG}._lib').load()
+    ops = importlib.import_module(f'{PKG}.s6_ops')
+    B, H, page, ctx, layers, loops = 64, 16, 16, 8192, 6, 4
+    r, dr = args.heads_rank, args.heads_rope
+    Lk = r + dr
+    pages = ctx // page
+    nb = B * pages + 1
+    g = torch.Generator(device='cuda').manual_seed(args.seed)
+    caches = [torch.randn(nb, H, page, Lk, generator=g, device='cuda').to(torch.bfloat16) for _ in range(layers)]
+    perm = torch.randperm(nb - 1, generator=torch.Generator().manual_seed(args.seed)).to(torch.int32) + 1
+    table = perm.view(B, pages).cuda()
+    ctx_t = torch.full((B,), ctx, dtype=torch.int32, device='cuda')
+    q = torch.randn(B, H, Lk, generator=g, device='cuda').to(torch.bfloat16)
+    props = torch.cuda.get_device_properties(local)
+    splits = ops.num_kv_splits(ctx, B, 512, props.multi_processor_count)
+    ws = ops.S6Workspace(H, r, B * splits)
+    ws.ensure('cuda')
+    scale = 128 ** -0.5
+
+    def step():
+        for _ in range(loops):
+            for c in caches:
+                ops.history_attention_kv(q, c, c[..., :r], table, ctx_t, scale, splits, ws, None, None, 'b200',
+                                         mla=True)
+    step()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    with ClockSampler(local) as clk:
+        ms = time_graph(torch, graph, args.steps, None) / args.steps
+    reads = layers * loops
+    bytes_step = reads * B * H * ctx * Lk * 2
+    peak, peak_kind = peaks()
+    achieved = bytes_step / (ms / 1e3) / 1e9
+    line = {'metric': METRIC_HEADS, 'value': B / (ms / 1e3), 'unit': 'tokens/s', 'n_gpus': 1, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
+            'config': {'workload': f'per-head paged history read MLA-style (LLA serving path): {reads} reads '
+                                   f'({layers} layers x {loops} loops), B={B}, ctx {ctx}, {H} KV heads, rows '
+                                   f'[{r} | {dr}]', 'global_batch': B, 'ctx': ctx, 'rank': r, 'd_rope': dr,
+                       'splits': splits, 'l2': 'inputs larger than L2 (per-head caches ~%d GB), no flush' %
+                       round(layers * nb * H * page * Lk * 2 / 1e9)},
+            'roofline': {'bound': 'hbm', 'kernel': 'history_heads_split_kernel + reduce, the whole step',
+                         'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
+                         'peak_source': peak_kind, 'bytes_per_step': bytes_step, 'traffic': None},
+            'cpu_baseline': None, 'e2e': None, 'gpu_launches': 2 * reads * args.steps, 'clocks': clk.summary()}
+    print(json.dumps(line), flush=True)
+    return line
+
+
 def run_export(args):
     """--config export: the rollout cache export of one finished 8192-token request over 24 layers
     (cache_export.export_rows: one gather launch, one pinned copy out), one GPU."""
@@ -814,7 +884,9 @@ def main():
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5', 'contig', 'export'])
+    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5', 'contig', 'export', 'heads'])
+    ap.add_argument('--heads-rank', type=int, default=128, help='--config heads: latent rank r of the LLA rows')
+    ap.add_argument('--heads-rope', type=int, default=32, help='--config heads: RoPE tail d_rope of the LLA rows')
     ap.add_argument('--seed', type=int, default=0)
     ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
     ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')
@@ -825,12 +897,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
-    if args.config in ('contig', 'export'):
+    if args.config in ('contig', 'export', 'heads'):
         if args.impl == 'reference':
             print(json.dumps({'impl': 'reference', 'unavailable': f'--config {args.config} has no reference arm; '
                               'its line carries the oracle as cpu_baseline'}), flush=True)
             return
-        (run_contig if args.config == 'contig' else run_export)(args)
+        {'contig': run_contig, 'export': run_export, 'heads': run_heads}[args.config](args)
         return
     args.config = int(args.config)
     if args.impl == 'reference':

@@ -8,19 +8,27 @@
 // oracle is _history_reference (s6_ops.py:204-222).  Empty rows give o = 0, lse = -inf.
 //
 // B200 design.  With a KV head per query head (LLA: kvH = H = 16) each (token, head) pair is a GEMV
-// at ~1 flop per byte, an HBM stream that CUDA cores sustain; the heads-as-M tensor-core tiling of the
-// MQA reader does not apply.  One CTA per (token, head, split): a cp.async ring stages the head's
-// pages (16 rows x Lk) in shared memory, rows past ctx zero-filled; warps score 4 keys each (lanes
-// over columns, warp-sum), the CTA keeps the online softmax, and every thread accumulates its Lv
-// columns of P.V from the same tile.  The normalised partial and its lse go to the workspace
-// [T, H, splits, Lv + 1] (the reference's attn_logits layout); a second kernel merges the splits.
+// at ~1 flop per byte, an HBM stream; the heads-as-M tiling of the MQA reader does not apply.  Each
+// (token, head, split) is one independent warp (a 32-thread CTA, many resident per SM): a ring of
+// shared-memory stages holds its pages (16 rows x Lk, rows padded by 16 bytes so ldmatrix is
+// conflict-free), each row fetched by one bulk copy (cp.async.bulk, completion counted on the
+// stage's mbarrier) - 16 requests per page, where 16-byte cp.async would need Lk / 8 per row and
+// exhaust the SM's outstanding-request capacity long before HBM does; rows past ctx are zeroed.  The arithmetic runs on mma.sync m16n8k16 with the vector
+// as the N = 8 operand's first column, so a 16-key page costs Lk/16 + Lv/16 tensor instructions and
+// no per-element conversions:
+//   scores   S[16 keys]  = K_tile (A: 16 keys x 16 columns) . q (B column 0)
+//   values   O^T[Lv]    += V_tile^T (A: ldmatrix.trans, 16 value columns x 16 keys) . p (B column 0)
+// The online softmax runs on the 16 scores (lanes with c4 = 0 hold two each).  The normalised partial
+// and its lse go to the workspace [T, H, splits, Lv + 1] (the reference's attn_logits layout); a second
+// kernel merges the splits.
 #include "../../include/hla_s6.h"
 #include "common.cuh"
 #include "hla_s6_internal.h"
 
 namespace hla {
 
-constexpr int kHdThreads = 128, kHdStages = 4, kHdPage = 16, kHdMaxCols = 4;  // Lv <= 512
+constexpr int kHdPage = 16, kHdThreads = 128;   // kHdThreads: the reduce kernel's block
+constexpr int kHdMaxLv = 512, kHdMaxCols = kHdMaxLv / kHdThreads;
 
 struct HeadsParams {
   const __nv_bfloat16* q;  // [T, H, Lk]
@@ -37,18 +45,44 @@ struct HeadsParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(kHdThreads) history_heads_split_kernel(const HeadsParams p) {
+// Stages of the per-warp ring for a row width (shared memory per warp-CTA stays under ~40 KB).
+__host__ __device__ inline int heads_stages(int Lk) { return Lk <= 256 ? 4 : (Lk <= 512 ? 3 : 2); }
+__host__ __device__ inline int heads_row_elems(int Lk) { return Lk + 8; }   // +16 B per row
+inline int heads_smem_bytes(int Lk) { return 64 + (heads_stages(Lk) * kHdPage * heads_row_elems(Lk) + Lk) * 2; }
+
+// One contiguous global -> shared copy by the bulk-copy engine (no multicast), completion counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// D = A . B with only D's column 0 kept (rows g8 and g8 + 8 in the c4 = 0 lanes): the other two
+// accumulators start at zero and are dropped.
+__device__ __forceinline__ void mma_col0(float& c0, float& c2, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "{\n"
+      ".reg .f32 d1, d3;\n"
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,d1,%1,d3}, {%2,%3,%4,%5}, {%6,%7}, {%0,%8,%1,%8};\n"
+      "}\n"
+      : "+f"(c0), "+f"(c2)
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// VT = Lv / 16 value tiles.
+template <int VT>
+__global__ void __launch_bounds__(32, 1) history_heads_split_kernel(const HeadsParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lane = threadIdx.x, g8 = lane >> 2, c4 = lane & 3;
   const int split = blockIdx.x % p.splits;
   const int row = blockIdx.x / p.splits;  // t * H + h
   const int t = row / p.H, h = row % p.H;
   const int kvh = h / (p.H / p.kvH);
-  const int Lk = p.Lk, Lv = p.Lv, lk8 = Lk / 8;
-  const int tile_bytes = kHdPage * Lk * 2;
-  uint8_t* tiles = smem_raw;
-  float* qs = reinterpret_cast<float*>(smem_raw + kHdStages * tile_bytes);  // [Lk]
-  float* sc = qs + Lk;                                                      // [16] scores (log2 domain)
+  const int Lk = p.Lk, Lv = p.Lv, lk8 = Lk / 8, RE = heads_row_elems(Lk), S = heads_stages(Lk);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);                       // [S] page landed
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw + 64);          // [Lk]
+  __nv_bfloat16* tiles = qs + Lk;                                               // [S][16][RE]
   float* out = p.ws + (static_cast<int64_t>(row) * p.splits + split) * (Lv + 1);
 
   const int n = max(p.ctx[t], 0);
@@ -56,100 +90,137 @@ __global__ void __launch_bounds__(kHdThreads) history_heads_split_kernel(const H
   const int per = (pages + p.splits - 1) / p.splits;
   const int pg0 = split * per, pg1 = min(pages, pg0 + per);
   if (pg0 >= pg1) {  // nothing to read in this split
-    for (int c = tid; c < Lv; c += kHdThreads) out[c] = 0.f;
-    if (tid == 0) out[Lv] = -INFINITY;
+    for (int c = lane; c < Lv; c += 32) out[c] = 0.f;
+    if (lane == 0) out[Lv] = -INFINITY;
     return;
   }
-  const __nv_bfloat16* qr = p.q + static_cast<int64_t>(t) * p.q_st + static_cast<int64_t>(h) * p.q_sh;
-  for (int c = tid; c < Lk; c += kHdThreads) qs[c] = __bfloat162float(qr[c]) * p.scale_log2;
+  {
+    const uint4* qr = reinterpret_cast<const uint4*>(p.q + static_cast<int64_t>(t) * p.q_st +
+                                                     static_cast<int64_t>(h) * p.q_sh);
+    for (int c = lane; c < lk8; c += 32) reinterpret_cast<uint4*>(qs)[c] = qr[c];
+  }
 
+  // the split's block ids, 32 at a time (one coalesced load per 32 pages; pages are requested in
+  // increasing order), broadcast by shuffle so no page waits on its own table read
+  int ids_chunk = -1, ids = -1;
+  auto block_of = [&](int lp) -> int {
+    const int idx = lp - pg0, chunk = idx >> 5;
+    if (chunk != ids_chunk) {
+      ids_chunk = chunk;
+      const int j = pg0 + (chunk << 5) + lane;
+      ids = (j < pg1 && j < p.max_blocks) ? p.bt[static_cast<int64_t>(t) * p.bt_st + j] : -1;
+    }
+    return __shfl_sync(0xffffffffu, ids, idx & 31);
+  };
+  const uint32_t row_bytes = static_cast<uint32_t>(Lk) * 2;
   auto load_page = [&](int lp, int stage) {
-    int blk = lp < p.max_blocks ? p.bt[static_cast<int64_t>(t) * p.bt_st + lp] : -1;
+    int blk = block_of(lp);
     if (blk < 0 || blk >= p.nb) {
-      if (tid == 0) record_error(p.err, kErrSlots);
+      if (lane == 0) record_error(p.err, kErrSlots);
       blk = -1;
     }
-    const int valid = min(kHdPage, n - lp * kHdPage);
-    uint8_t* dst = tiles + stage * tile_bytes;
-    const __nv_bfloat16* base = p.cache + static_cast<int64_t>(blk < 0 ? 0 : blk) * p.c_sb +
-                                static_cast<int64_t>(kvh) * p.c_sh;
-    for (int i = tid; i < kHdPage * lk8; i += kHdThreads) {
-      const int r = i / lk8, ch = i % lk8;
-      const bool live = blk >= 0 && r < valid;  // rows past ctx (and unreadable blocks) read as zeros
-      cp_async16(dst + (r * Lk + ch * 8) * 2, base + static_cast<int64_t>(live ? r : 0) * p.c_sr + ch * 8,
-                 live ? 16 : 0);
+    const int valid = blk < 0 ? 0 : min(kHdPage, n - lp * kHdPage);
+    __nv_bfloat16* dst = tiles + stage * kHdPage * RE;
+    // generic-proxy accesses of this stage (the previous page's reads, zero fills) precede the copies
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(valid) * row_bytes);
+    __syncwarp();
+    if (lane < valid) {
+      const __nv_bfloat16* src = p.cache + static_cast<int64_t>(blk) * p.c_sb + static_cast<int64_t>(kvh) * p.c_sh +
+                                 static_cast<int64_t>(lane) * p.c_sr;
+      bulk_g2s(dst + lane * RE, src, row_bytes, &full[stage]);
+    } else if (lane < kHdPage) {
+      uint4* z = reinterpret_cast<uint4*>(dst + lane * RE);  // rows past ctx read as zeros
+      for (int c = 0; c < lk8; ++c) z[c] = make_uint4(0u, 0u, 0u, 0u);
     }
   };
 
-  // prologue: STAGES - 1 pages in flight
-#pragma unroll
-  for (int s = 0; s < kHdStages - 1; ++s) {
-    if (pg0 + s < pg1) load_page(pg0 + s, s);
-    cp_async_commit();
+  if (lane == 0) {
+    for (int s2 = 0; s2 < S; ++s2) mbar_init(&full[s2], 1);
+    fence_barrier_init();
   }
-  __syncthreads();  // q staged
+  __syncwarp();
+  for (int s2 = 0; s2 < S - 1; ++s2)
+    if (pg0 + s2 < pg1) load_page(pg0 + s2, s2);
+  __syncwarp();
 
   float m = -INFINITY, l = 0.f;
-  float o[kHdMaxCols];
+  float oc0[VT], oc2[VT];  // O^T rows g8 and g8 + 8 of value tile vt (meaningful in c4 = 0 lanes)
 #pragma unroll
-  for (int i = 0; i < kHdMaxCols; ++i) o[i] = 0.f;
+  for (int i = 0; i < VT; ++i) oc0[i] = oc2[i] = 0.f;
+  const uint32_t qbase = smem_u32(qs);
 
   for (int lp = pg0, it = 0; lp < pg1; ++lp, ++it) {
-    const int nxt = lp + kHdStages - 1;
-    if (nxt < pg1) load_page(nxt, (it + kHdStages - 1) % kHdStages);
-    cp_async_commit();
-    cp_async_wait<kHdStages - 1>();
-    __syncthreads();
-    const __nv_bfloat16* tile = reinterpret_cast<const __nv_bfloat16*>(tiles + (it % kHdStages) * tile_bytes);
+    const int nxt = lp + S - 1;
+    if (nxt < pg1) load_page(nxt, (it + S - 1) % S);
+    const bool landed = __all_sync(0xffffffffu, mbar_wait(&full[it % S], (it / S) & 1));
+    if (!landed) {
+      // give up on this split, but not before the copies already issued into this CTA's shared
+      // memory have completed (bounded waits)
+      if (lane == 0) record_error(p.err, kErrWaitFull);
+      for (int q = it + 1, lq = lp + 1; lq < pg1 && q <= it + S - 1; ++q, ++lq) mbar_wait(&full[q % S], (q / S) & 1);
+      break;
+    }
+    __syncwarp();
+    const uint32_t tb = smem_u32(tiles + (it % S) * kHdPage * RE);
     const int valid = min(kHdPage, n - lp * kHdPage);
-    // scores: warp w owns keys 4w .. 4w + 3
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const int key = warp * 4 + kk;
-      const __nv_bfloat162* kr = reinterpret_cast<const __nv_bfloat162*>(tile + key * Lk);
-      float acc = 0.f;
-      for (int c = lane; c < Lk / 2; c += 32) {
-        const float2 kv = __bfloat1622float2(kr[c]);
-        acc = fmaf(qs[2 * c], kv.x, fmaf(qs[2 * c + 1], kv.y, acc));
+    // ---- scores of the 16 keys
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < Lk; k0 += 16) {
+      uint32_t a[4];
+      ldsm_x4(tb + (((lane & 15) * RE + k0 + ((lane >> 4) << 3)) << 1), a[0], a[1], a[2], a[3]);
+      uint32_t b0 = 0u, b1 = 0u;
+      if (g8 == 0) {
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(qbase + ((k0 + 2 * c4) << 1)));
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(qbase + ((k0 + 8 + 2 * c4) << 1)));
       }
-      acc = warp_sum(acc);
-      if (lane == 0) sc[key] = key < valid ? acc : -INFINITY;
+      mma_bf16_16816(sacc, a, b0, b1);
     }
-    __syncthreads();
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < kHdPage; ++k) tmax = fmaxf(tmax, sc[k]);
-    const float mn = fmaxf(m, tmax);  // finite: every visited page has a key below ctx
+    const float s0 = (c4 == 0 && g8 < valid) ? sacc[0] * p.scale_log2 : -INFINITY;
+    const float s1 = (c4 == 0 && g8 + 8 < valid) ? sacc[2] * p.scale_log2 : -INFINITY;
+    // ---- online softmax over the tile
+    float tm = fmaxf(s0, s1);
+    tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+    tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
+    tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+    tm = __shfl_sync(0xffffffffu, tm, 0);
+    const float mn = fmaxf(m, tm);  // finite: every visited page has a key below ctx
     const float alpha = exp2f(m - mn);
-    float pk[kHdPage];
-    float ps = 0.f;
-#pragma unroll
-    for (int k = 0; k < kHdPage; ++k) {
-      pk[k] = exp2f(sc[k] - mn);
-      ps += pk[k];
-    }
+    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);  // 0 for masked keys and c4 != 0 lanes
+    float ps = p0 + p1;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    ps = __shfl_sync(0xffffffffu, ps, 0);
     l = l * alpha + ps;
     m = mn;
+    // ---- P as the B operand's column 0: lane c4 of g8 = 0 takes keys 2c4, 2c4 + 1, 2c4 + 8, 2c4 + 9
+    //      (key j < 8 lives in lane 4j as p0, key j + 8 there as p1)
+    const float pa = __shfl_sync(0xffffffffu, p0, 8 * c4), pb = __shfl_sync(0xffffffffu, p0, 8 * c4 + 4);
+    const float pc = __shfl_sync(0xffffffffu, p1, 8 * c4), pd = __shfl_sync(0xffffffffu, p1, 8 * c4 + 4);
+    const uint32_t b0 = g8 == 0 ? pack_bf16(pa, pb) : 0u, b1 = g8 == 0 ? pack_bf16(pc, pd) : 0u;
+    // ---- O^T += V^T . P
+    const int vkey = (lane & 7) + ((lane >> 4) << 3), vcol = ((lane >> 3) & 1) << 3;
 #pragma unroll
-    for (int i = 0; i < kHdMaxCols; ++i) {
-      const int c = tid + i * kHdThreads;
-      if (c < Lv) {
-        float acc = o[i] * alpha;
-#pragma unroll
-        for (int k = 0; k < kHdPage; ++k) acc = fmaf(pk[k], __bfloat162float(tile[k * Lk + c]), acc);
-        o[i] = acc;
-      }
+    for (int vt = 0; vt < VT; ++vt) {
+      oc0[vt] *= alpha;
+      oc2[vt] *= alpha;
+      uint32_t a[4];
+      ldsm_x4_t(tb + ((vkey * RE + vt * 16 + vcol) << 1), a[0], a[1], a[2], a[3]);
+      mma_col0(oc0[vt], oc2[vt], a, b0, b1);
     }
-    __syncthreads();  // the tile and the scores are consumed
+    __syncwarp();  // the stage is consumed before the next load overwrites it
   }
-  cp_async_wait<0>();
   const float inv = l > 0.f ? 1.f / l : 0.f;
+  if (c4 == 0) {
 #pragma unroll
-  for (int i = 0; i < kHdMaxCols; ++i) {
-    const int c = tid + i * kHdThreads;
-    if (c < Lv) out[c] = o[i] * inv;
+    for (int vt = 0; vt < VT; ++vt) {
+      out[vt * 16 + g8] = oc0[vt] * inv;
+      out[vt * 16 + g8 + 8] = oc2[vt] * inv;
+    }
   }
-  if (tid == 0) out[Lv] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+  if (lane == 0) out[Lv] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
 }
 
 // Merge of a (token, head)'s splits -> o (bf16, [T, H, Lv] strided) and lse [H, T].
@@ -211,10 +282,10 @@ extern "C" int hla_s6_history_attention_heads(const void* q, int64_t q_stride_t,
     set_error("per-head history: H must be a multiple of kvH, splits >= 1, ctx / table / out / lse set");
     return kStatusInvalid;
   }
-  if (key_width % 8 || value_width % 8 || value_width < 8 || value_width > key_width ||
-      value_width > kHdMaxCols * kHdThreads || key_width > 1024) {
-    set_error("per-head history: widths must be multiples of 8 with value <= key, value <= %d, key <= 1024",
-              kHdMaxCols * kHdThreads);
+  if (key_width % 16 || value_width % 16 || value_width < 16 || value_width > key_width || value_width > kHdMaxLv ||
+      key_width > 1024) {
+    set_error("per-head history: widths must be multiples of 16 with value <= key, value <= %d, key <= 1024",
+              kHdMaxLv);
     return kStatusInvalid;
   }
   if ((reinterpret_cast<uintptr_t>(cache) % 16) || (cache_stride_block % 8) || (cache_stride_head % 8) ||
@@ -251,16 +322,28 @@ extern "C" int hla_s6_history_attention_heads(const void* q, int64_t q_stride_t,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.ws = workspace;
   p.err = error_flag;
-  const int smem = kHdStages * kHdPage * key_width * 2 + (key_width + kHdPage) * 4;
-  static unsigned attr_mask = 0;
-  ensure_smem_limit(history_heads_split_kernel, kHdStages * kHdPage * 1024 * 2 + (1024 + kHdPage) * 4, attr_mask);
+  const int smem = heads_smem_bytes(key_width);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t ctas = static_cast<int64_t>(num_tokens) * num_heads * num_kv_splits;
   if (ctas > 0x7fffffff) {
     set_error("per-head history: too many (token, head, split) programs");
     return kStatusInvalid;
   }
-  history_heads_split_kernel<<<static_cast<unsigned>(ctas), kHdThreads, smem, s>>>(p);
+#define HLA_HEADS(VT)                                                                                   \
+  {                                                                                                    \
+    static unsigned attr_mask = 0;                                                                     \
+    ensure_smem_limit(history_heads_split_kernel<VT>, heads_smem_bytes(1024), attr_mask);              \
+    history_heads_split_kernel<VT><<<static_cast<unsigned>(ctas), 32, smem, s>>>(p);                   \
+  }
+  switch (value_width / 16) {
+    case 4: HLA_HEADS(4); break;
+    case 8: HLA_HEADS(8); break;
+    case 16: HLA_HEADS(16); break;
+    case 32: HLA_HEADS(32); break;
+    default: set_error("per-head history: value width %d unsupported (64, 128, 256, 512)", value_width);
+      return kStatusInvalid;
+  }
+#undef HLA_HEADS
   int rc = cuda_status(cudaGetLastError(), "history_heads_split_kernel launch");
   if (rc) return rc;
   history_heads_reduce_kernel<<<num_tokens * num_heads, kHdThreads, 0, s>>>(

@@ -111,7 +111,8 @@ int hla_s6_history_attention_contig(const void* q, int64_t q_stride_b, int64_t q
  * first ctx[t] rows of KV head h / (H / kv_heads) of cache [num_blocks, kv_heads, page, >= key_width]
  * (bf16, strides per block / head / row, unit last stride, multiples of 8 elements), scoring the
  * whole key_width row against q [T, H, key_width] and averaging its first value_width columns (the
- * row [c | rotated k_rope] read once; value_width <= 512, key_width <= 1024, page 16).
+ * row [c | rotated k_rope] read once; widths multiples of 16, value_width in {64, 128, 256, 512},
+ * key_width <= 1024, page 16).
  * out bf16 [T, H, value_width] (strided), lse fp32 [H, T]; empty rows (ctx 0 or empty[t]) give
  * o = 0, lse = -inf.  Workspace: T * H * num_kv_splits * (value_width + 1) floats, the reference's
  * attn_logits layout.  A block id outside the cache sets error_flag (3) and reads as zeros.
