@@ -101,6 +101,32 @@ int latent_cache_tmap(CUtensorMap* map, const void* cache, int64_t num_blocks, i
   return kStatusOk;
 }
 
+int combine_b_tmap(CUtensorMap* map, const void* B, int H, int W, int64_t b_sh, int64_t b_sk) {
+  if (reinterpret_cast<uintptr_t>(B) % 16 || (b_sh * 2) % 16 || (b_sk * 2) % 16 || b_sk < 128 || H < 1) {
+    set_error("decode combine: B [H, W, 128] needs a 16-byte aligned base and strides that are multiples of 8 "
+              "elements (head %lld, row %lld)", static_cast<long long>(b_sh), static_cast<long long>(b_sk));
+    return kStatusInvalid;
+  }
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return kStatusCuda;
+  }
+  // (64 columns, W rows, 2 column slabs, H heads): a box of 64 rows lands as [slab][row][64]
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(W), 2, static_cast<cuuint64_t>(H)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(b_sk * 2), 128, static_cast<cuuint64_t>(b_sh * 2)};
+  cuuint32_t box[4] = {64, 64, 2, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(B), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for the combine's B", static_cast<int>(r));
+    return kStatusCuda;
+  }
+  return kStatusOk;
+}
+
 int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, int W, int64_t st_b, int64_t st_n,
                      int tile) {
   if (reinterpret_cast<uintptr_t>(base) % 16 || (st_n * 2) % 16 || (st_b * 2) % 16 || st_n < W || B < 1 || N < 1) {

@@ -30,13 +30,17 @@ struct CombineSmem {
   static constexpr int Q_OFF = OW_OFF + kCTok * 128 * 4;          // float [8 warps][128]
   static constexpr int L_OFF = Q_OFF + 8 * 128 * 4;               // float lse_h[16], lse_w[16]
   static constexpr int QSL_OFF = L_OFF + 2 * kCTok * 4;         // int32 query_start_loc copy
-  static constexpr int BYTES = QSL_OFF + kQslCap * 4;
+  static constexpr int BAR_OFF = QSL_OFF + kQslCap * 4;          // mbarrier: all of B[h] landed
+  static constexpr int BYTES = BAR_OFF + 16 + 1024;              // + slack to align the base to 1024 B
 };
 
 template <int W>
-__global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams p) {
+__global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_constant__ CUtensorMap tmap_b,
+                                                             const CombineParams p) {
   using S = CombineSmem<W>;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // B[h] arrives by TMA with SWIZZLE_128B, whose pattern follows address bits: 1024-byte aligned base
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* ow_s = reinterpret_cast<float*>(smem + S::OW_OFF);
   float* q_s = reinterpret_cast<float*>(smem + S::Q_OFF);
   float* lh_s = reinterpret_cast<float*>(smem + S::L_OFF);
@@ -45,17 +49,18 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
   const int h = blockIdx.x, t0 = blockIdx.y * kCTok, T = p.T, H = p.H;
   constexpr int NK = W / kCKC;
 
-  // ---- all of B[h] in flight now; it lands while steps 1-2 run
-  const __nv_bfloat16* Bh = p.B + static_cast<int64_t>(h) * p.b_sh;
-  for (int kc = 0; kc < NK; ++kc) {
-    uint8_t* dst = smem + S::B_OFF + kc * kCChunkBytes;
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {  // 64 rows x 16 chunks = 1024 chunks
-      const int idx = tid + it * 256, row = idx >> 4, ch = idx & 15;
-      cp_async16(dst + swz(row, ch, 256), Bh + static_cast<int64_t>(kc * kCKC + row) * p.b_sk + ch * 8);
-    }
+  // ---- all of B[h] in flight now (W/64 TMA boxes of 64 rows x 2 slabs of 64 columns, one mbarrier);
+  //      it lands while steps 1-2 run.  Chunk kc holds [slab][row][64] with 128-byte rows swizzled
+  //      by row % 8.
+  uint64_t* bbar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  if (tid == 0) {
+    mbar_init(bbar, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmap_b);
+    mbar_arrive_expect_tx(bbar, W * 128 * 2);
+    for (int kc = 0; kc < NK; ++kc) tma_load_4d(smem + S::B_OFF + kc * kCChunkBytes, &tmap_b, bbar, 0, kc * kCKC, 0, h);
   }
-  cp_async_commit();
+  __syncthreads();  // the barrier is initialised before any thread waits on it
   WindowArgs win = p.win;
   win.qsl = stage_qsl(p.win.qsl, p.win.R, reinterpret_cast<int32_t*>(smem + S::QSL_OFF));
 
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
   // ---- 3: o_hist[16 x 128] = z[16 x W] . B[h][W x 128]; warp w owns columns 16w .. 16w+15
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   const uint32_t zb = smem_u32(smem + S::Z_OFF);
-  cp_async_wait<0>();
+  if (!mbar_wait(bbar, 0)) record_error(p.err, kErrWaitFull);
   __syncthreads();
   for (int kc = 0; kc < NK; ++kc) {
     const uint32_t bb = smem_u32(smem + S::B_OFF + kc * kCChunkBytes);
@@ -203,7 +208,8 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
       const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
       ldsm_x4(zb + swz(arow, (kc * kCKC + ks * 16) / 8 + (lane >> 4), W * 2), a[0], a[1], a[2], a[3]);
       const int krow = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      ldsm_x4_t(bb + swz(krow, 2 * warp + (lane >> 4), 256), b0, b1, b2, b3);
+      const int bch = 2 * warp + (lane >> 4);  // 16-byte chunk of the 128 columns: slab bch / 8
+      ldsm_x4_t(bb + (bch >> 3) * (kCKC * 128) + krow * 128 + ((((bch & 7) ^ (krow & 7))) << 4), b0, b1, b2, b3);
       mma_bf16_16816(acc[0], a, b0, b1);
       mma_bf16_16816(acc[1], a, b2, b3);
     }
@@ -234,6 +240,9 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams
 
 template <int W>
 static int launch_combine(const CombineParams& p, bool pdl, cudaStream_t s) {
+  CUtensorMap tb;
+  int rc = combine_b_tmap(&tb, p.B, p.H, W, p.b_sh, p.b_sk);
+  if (rc) return rc;
   static unsigned attr_mask = 0;
   const int smem = CombineSmem<W>::BYTES;
   ensure_smem_limit(decode_combine_kernel<W>, smem, attr_mask);
@@ -247,7 +256,7 @@ static int launch_combine(const CombineParams& p, bool pdl, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_combine_kernel<W>, p), "decode_combine_kernel launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_combine_kernel<W>, tb, p), "decode_combine_kernel launch");
 }
 
 int decode_combine(const CombineParams& p, int W, bool pdl, cudaStream_t s) {

@@ -95,6 +95,8 @@ struct ContigArgs {
   int* err;
 };
 int history_attention_contig(const ContigArgs& c, cudaStream_t stream);
+// 4-D TMA map over the combine's up-projection B [H, W, 128] bf16 (capi.cu).
+int combine_b_tmap(CUtensorMap* map, const void* B, int H, int W, int64_t b_sh, int64_t b_sk);
 // 4-D TMA map over a [B, N, W] bf16 tensor: (64, N, W/64, B) with boxes of `tile` rows (capi.cu).
 int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, int W, int64_t st_b, int64_t st_n,
                      int tile);
