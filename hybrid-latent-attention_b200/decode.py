@@ -84,8 +84,9 @@ class S6DecodeModel:
     """
 
     def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
-                 latent_rows=None, exchange=None, exchange_mode='peer'):
+                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=False):
         self.s, self.device = shape, torch.device(device)
+        self.window_overlap = window_overlap
         s = shape
         B = len(batch.ctx)
         self.B = B
@@ -178,6 +179,11 @@ class S6DecodeModel:
         self.scale = s.head_dim ** -0.5
         self.graph = None
         self.history_graph = None
+        # exact-window part computed beside the history kernel (window_overlap): one buffer, reused by
+        # every (layer, loop) - window i + 1 is ordered after prepare i + 1, which follows combine i
+        self.win_o = torch.empty(B, s.heads, s.head_dim, dtype=BF16, device=self.device)
+        self.win_lse = torch.empty(s.heads, B, dtype=torch.float32, device=self.device)
+        self._win_stream = None
 
     # ------------------------------------------------------------------ peer exchange
     def _init_peer_exchange(self, rank, world, group):
@@ -301,6 +307,25 @@ class S6DecodeModel:
                   v.stride(1), _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(ex),
                   ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
                   self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, None, stream)
+        # 2b. (window_overlap) exact window on a side stream, beside the history kernel (it needs prepare's
+        #     q_rope and appended row only); the combine then takes it as its external exact part.  Measured
+        #     slower than the window inside the combine (config 2: 18.3 vs 17.2 ms per step), so off by default
+        win_done = None
+        if self.window_overlap:
+            main = torch.cuda.current_stream(self.device)
+            if self._win_stream is None:
+                self._win_stream = torch.cuda.Stream(self.device)
+            fork = torch.cuda.Event()
+            fork.record(main)
+            self._win_stream.wait_event(fork)
+            _lib.call('hla_s6_window_attention', _lib.ptr(qr), qr.stride(0), qr.stride(1), _lib.ptr(ex), ex.shape[0],
+                      ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
+                      self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B,
+                      _lib.ptr(self.seq_lens), s.window, float(self.scale), B, s.heads, s.head_dim,
+                      _lib.ptr(self.win_o), self.win_o.stride(0), self.win_o.stride(1), _lib.ptr(self.win_lse),
+                      _lib.ctypes.c_void_p(self._win_stream.cuda_stream))
+            win_done = torch.cuda.Event()
+            win_done.record(self._win_stream)
         # 3. history split
         self._history(layer, loop, stream)
         # 3b. sequence split: reduce this GPU's slice to (z, lse) and all-gather the parts
@@ -333,21 +358,27 @@ class S6DecodeModel:
             recv = self.xrecv[:world * part_stride]
             torch.distributed.all_gather_into_tensor(recv, send, group=group)
             z_in, lse_in, parts, flags = recv, recv[zf:], world, 0
-        # 4. fused combine -> out
+        # 4. fused combine -> out (with the side stream's window part when window_overlap)
         out = self.out[layer, loop]
+        if win_done is not None:
+            torch.cuda.current_stream(self.device).wait_event(win_done)
+            chunk = (_lib.ptr(self.win_o), self.win_o.stride(0), self.win_o.stride(1), _lib.ptr(self.win_lse))
+        else:
+            chunk = (None, 0, 0, None)
         _lib.call('hla_s6_decode_combine', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws), self.ws_floats,
                   _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, part_flags, part_seen, None, _lib.ptr(Bm),
                   Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
                   _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
                   _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
-                  _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), None, 0, 0, None,
+                  _lib.ptr(self.qsl), B, _lib.ptr(self.seq_lens), s.window, float(self.scale), *chunk,
                   _lib.ptr(out),
                   out.stride(0), out.stride(1), None, flags, None, stream)
 
     def launches_per_step(self):
-        """Launches of this library per step (the sequence split adds one reduce per (layer, loop))."""
+        """Launches of this library per step (the sequence split adds one reduce per (layer, loop), the
+        side-stream window one window kernel)."""
         s = self.s
-        return s.layers * s.loops * (5 if self.exchange is not None else 4)
+        return s.layers * s.loops * (4 + (self.exchange is not None) + bool(self.window_overlap))
 
     def step(self, overlap_writer=True):
         """One decode step.  With ``overlap_writer`` the writer launches run on a side stream forked from

@@ -1,0 +1,33 @@
+"""The whole decode step of S6DecodeModel (4-5 launches per (layer, loop), graph-captured) in its two
+arrangements of the exact window - inside the fused combine, or as its own kernel on a side stream
+beside the history kernel (window_overlap) - agree, eagerly and under graph replay.  GPU."""
+import pytest
+import torch
+
+from conftest import pkg
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(overlap):
+    dec = pkg('decode')
+    shape = dec.OuroShape(layers=2)
+    return dec.S6DecodeModel(shape, dec.DecodeBatch([4096, 1000, 40, 2000, 1, 33, 31, 0][:8]), device='cuda', seed=11,
+                             window_overlap=overlap)
+
+
+def test_side_stream_window_matches_fused_window():
+    fused, side = _model(False), _model(True)
+    assert torch.equal(fused.acts, side.acts)
+    fused.step()
+    side.step()
+    torch.cuda.synchronize()
+    assert torch.isfinite(side.out.float()).all()
+    # the side-stream window is rounded to bf16 before the merge (as the reference's FA2 output is)
+    torch.testing.assert_close(side.out.float(), fused.out.float(), atol=2e-2, rtol=1e-2)
+    eager = side.out.clone()
+    g = side.capture()
+    side.out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(side.out, eager)
