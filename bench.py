@@ -786,6 +786,41 @@ def run_heads(args):
     bytes_step = reads * B * H * ctx * Lk * 2
     peak, peak_kind = peaks()
     achieved = bytes_step / (ms / 1e3) / 1e9
+    # e2e: q in from pinned memory per loop, o and lse out per read
+    hq = q.cpu().pin_memory()
+    outs = []
+
+    def e2e_step():
+        outs.clear()
+        for _ in range(loops):
+            qq = hq.to('cuda', non_blocking=True)
+            for c in caches:
+                o, lse = ops.history_attention_kv(qq, c, c[..., :r], table, ctx_t, scale, splits, ws, None, None,
+                                                  'b200', mla=True)
+                outs.append((o.to('cpu', non_blocking=True), lse.to('cpu', non_blocking=True)))
+    e2e_step()
+    ms_e2e = _events_ms(torch, e2e_step, max(3, args.steps // 4))
+    h2d = loops * B * H * Lk * 2
+    d2h = reads * B * H * (r * 2 + 4)
+    cpu = None
+    if not args.no_cpu:
+        from oracle import s6_oracle as orc
+        use_all_host_threads()
+        rows = 1   # sequences (each with its 16 heads) in the sample
+        ids = table[:rows].cpu().numpy()
+        kc = caches[0][torch.from_numpy(ids.reshape(-1)).long().cuda()].float().cpu().numpy()
+        tab = np.arange(rows * pages, dtype=np.int32).reshape(rows, pages)
+        qq = q[:rows].float().cpu().numpy()
+        cc = np.full(rows, ctx, dtype=np.int32)
+        orc.history_attention_kv(qq, kc, kc[..., :r], tab, cc, scale, dt=np.float32)
+        reps = 10
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            orc.history_attention_kv(qq, kc, kc[..., :r], tab, cc, scale, dt=np.float32)
+        sec = (time.perf_counter() - t0) / reps / rows * B * reads
+        cpu = {'value': B / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
+               'sample': f'oracle numpy fp32 per-head reader, {rows} of {B} sequences (16 heads, ctx {ctx}), '
+                         f'extrapolated to the {reads} reads of a step'}
     line = {'metric': METRIC_HEADS, 'value': B / (ms / 1e3), 'unit': 'tokens/s', 'n_gpus': 1, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
@@ -797,7 +832,12 @@ def run_heads(args):
             'roofline': {'bound': 'hbm', 'kernel': 'history_heads_split_kernel + reduce, the whole step',
                          'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
                          'peak_source': peak_kind, 'bytes_per_step': bytes_step, 'traffic': None},
-            'cpu_baseline': None, 'e2e': None, 'gpu_launches': 2 * reads * args.steps, 'clocks': clk.summary()}
+            'cpu_baseline': cpu,
+            'e2e': {'value': B / (ms_e2e / 1e3), 'unit': 'tokens/s', 'h2d_bytes_per_step': h2d,
+                    'd2h_bytes_per_step': d2h,
+                    'path': 's6_ops.history_attention_kv(mla=True) per read, q copied in from pinned memory per '
+                            'loop, o and lse copied out per read'},
+            'gpu_launches': 2 * reads * args.steps, 'clocks': clk.summary()}
     print(json.dumps(line), flush=True)
     return line
 

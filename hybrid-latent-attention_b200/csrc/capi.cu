@@ -154,6 +154,68 @@ int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, i
   return kStatusOk;
 }
 
+// 5-D map over a per-head cache [num_blocks, kv_heads, 16, >= Lk] (LLA) starting at column 0 of `base`:
+// dims (cols, 16 rows, slabs, kv head, block), slab s covering columns [s * cols, (s + 1) * cols), with
+// the (2 * cols)-byte swizzle (cols = 64, 32 or 16), so a box of (cols, 16, slabs, 1, 1) lands one page
+// of one KV head as [slab][row][2 * cols bytes].
+struct HeadsTmapKey {
+  const void* ptr;
+  int64_t nb, kvh, sb_, sh, sr;
+  int cols, slabs, dev;
+  bool operator==(const HeadsTmapKey& o) const {
+    return ptr == o.ptr && nb == o.nb && kvh == o.kvh && sb_ == o.sb_ && sh == o.sh && sr == o.sr &&
+           cols == o.cols && slabs == o.slabs && dev == o.dev;
+  }
+};
+static HeadsTmapKey g_htmap_keys[16];
+static CUtensorMap g_htmap_vals[16];
+static int g_htmap_used = 0, g_htmap_next = 0;
+
+int heads_cache_tmap(CUtensorMap* map, const void* base, int64_t num_blocks, int64_t kv_heads, int64_t st_block,
+                     int64_t st_head, int64_t st_row, int cols, int slabs) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (st_row * 2) % 16 || (st_head * 2) % 16 || (st_block * 2) % 16 ||
+      (cols != 64 && cols != 32 && cols != 16) || slabs < 1 || slabs > 256 || num_blocks < 1 || kv_heads < 1) {
+    set_error("per-head cache: needs a 16-byte aligned base and strides that are multiples of 8 elements");
+    return kStatusInvalid;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const HeadsTmapKey key{base, num_blocks, kv_heads, st_block, st_head, st_row, cols, slabs, dev};
+  {
+    std::lock_guard<std::mutex> lock(g_tmap_mu);
+    for (int i = 0; i < g_htmap_used; ++i)
+      if (g_htmap_keys[i] == key) {
+        *map = g_htmap_vals[i];
+        return kStatusOk;
+      }
+  }
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return kStatusCuda;
+  }
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(cols), 16, static_cast<cuuint64_t>(slabs),
+                        static_cast<cuuint64_t>(kv_heads), static_cast<cuuint64_t>(num_blocks)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(st_row * 2), static_cast<cuuint64_t>(cols * 2),
+                           static_cast<cuuint64_t>(st_head * 2), static_cast<cuuint64_t>(st_block * 2)};
+  cuuint32_t box[5] = {static_cast<cuuint32_t>(cols), 16, static_cast<cuuint32_t>(slabs), 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                           : (cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for the per-head cache", static_cast<int>(r));
+    return kStatusCuda;
+  }
+  std::lock_guard<std::mutex> lock(g_tmap_mu);
+  const int slot = g_htmap_used < 16 ? g_htmap_used++ : (g_htmap_next++ % 16);
+  g_htmap_keys[slot] = key;
+  g_htmap_vals[slot] = *map;
+  return kStatusOk;
+}
+
 static int check_history_args(const HistoryArgs& a) {
   if (a.T < 0 || a.H < 1 || a.H > 16) {
     set_error("history attention needs 1..16 query heads per KV head (got H=%d, T=%d)", a.H, a.T);

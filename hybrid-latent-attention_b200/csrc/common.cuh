@@ -126,6 +126,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
+// 5-D form of tma_load_4d (no multicast).
+__device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- cp.async (16-byte, L2-cached)
 // src_bytes < 16 zero-fills the rest of the 16-byte destination (0 = pure zero fill, no read).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes = 16) {
@@ -144,6 +154,15 @@ __device__ __forceinline__ void cp_async_wait() {
 // the same logical chunk touches 8 distinct bank groups.
 __device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
   return static_cast<uint32_t>(row * row_bytes + ((chunk ^ (row & 7)) << 4));
+}
+
+// ---------------------------------------------------------------- stream-K partition
+// G CTAs split P work units (pages) evenly: CTA c takes [stream_start(c), stream_start(c + 1)).
+__host__ __device__ inline int64_t stream_start(int64_t c, int64_t P, int64_t G) { return c * P / G; }
+
+// Largest CTA index c with stream_start(c) <= p.
+__host__ __device__ inline int64_t stream_owner(int64_t p, int64_t P, int64_t G) {
+  return ((p + 1) * G - 1) / P;
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch

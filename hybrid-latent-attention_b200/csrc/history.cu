@@ -63,13 +63,6 @@ struct HistoryCfg {
   static constexpr int MIN_CTAS = PAGE_BYTES <= 16384 ? 4 : ((STAGES * PAGE_BYTES <= 100 * 1024) ? 2 : 1);
 };
 
-__host__ __device__ inline int64_t stream_start(int64_t c, int64_t P, int64_t G) { return c * P / G; }
-
-// Largest CTA index c with stream_start(c) <= p.
-__host__ __device__ inline int64_t stream_owner(int64_t p, int64_t P, int64_t G) {
-  return ((p + 1) * G - 1) / P;
-}
-
 __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int key_lo, int valid) {
   if (key_lo >= valid) return 0u;
   if (key_lo + 1 >= valid) return v & 0xffffu;

@@ -97,6 +97,11 @@ struct ContigArgs {
 int history_attention_contig(const ContigArgs& c, cudaStream_t stream);
 // 4-D TMA map over the combine's up-projection B [H, W, 128] bf16 (capi.cu).
 int combine_b_tmap(CUtensorMap* map, const void* B, int H, int W, int64_t b_sh, int64_t b_sk);
+// 5-D TMA map over a per-head cache [num_blocks, kv_heads, 16, >= Lk] from column 0 of `base` (capi.cu):
+// a box is `slabs` slabs of `cols` columns (64, 32 or 16) of one page of one KV head, laid out
+// [slab][row][2 * cols bytes] with the (2 * cols)-byte swizzle.
+int heads_cache_tmap(CUtensorMap* map, const void* base, int64_t num_blocks, int64_t kv_heads, int64_t st_block,
+                     int64_t st_head, int64_t st_row, int cols, int slabs);
 // 4-D TMA map over a [B, N, W] bf16 tensor: (64, N, W/64, B) with boxes of `tile` rows (capi.cu).
 int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, int W, int64_t st_b, int64_t st_n,
                      int tile);
