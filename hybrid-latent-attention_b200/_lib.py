@@ -17,6 +17,7 @@ ABI_VERSION = 1
 
 OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
 COMBINE_AFTER_PARTIALS = 1   # hla_s6_decode_combine flag (include/hla_s6.h)
+PARTIALS_AFTER_QUERY = 1     # hla_s6_history_partials flag
 REDUCE_AFTER_PARTIALS = 1    # hla_s6_history_reduce_exchange flag
 PEER_HANDLE_BYTES = 64       # HLA_S6_PEER_HANDLE_BYTES
 
@@ -28,7 +29,7 @@ SIGNATURES = {
     'hla_s6_history_attention': [P, _i64, _i64, P, _i64, _i64, _i64, P, _i64, _i32, P, P, _i32, _i32, _i32, _i32,
                                  _f32, _i32, P, _i64, P, _i64, _i64, P, P, P],
     'hla_s6_history_partials': [P, _i64, _i64, P, _i64, _i64, _i64, P, _i64, _i32, P, _i32, _i32, _i32, _i32, _f32,
-                                _i32, P, _i64, P, P],
+                                _i32, P, _i64, P, _i32, P],
     'hla_s6_history_reduce': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, _i64, _i64, P, P, P],
     'hla_s6_history_plan': [_i32, _i32, _i32, _i32, _i32, _i64, P, P, P],
     'hla_s6_window_attention': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, P, _i32, _f32,

@@ -300,10 +300,15 @@ int hla_s6_history_partials(const void* q_lat, int64_t q_stride_t, int64_t q_str
                             const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
                             const int32_t* ctx, int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, float scale,
                             int32_t num_kv_splits, float* workspace, int64_t workspace_floats, int* error_flag,
-                            void* stream) {
+                            int32_t flags, void* stream) {
   HistoryArgs a = make_history_args(q_lat, q_stride_t, q_stride_h, cache, num_blocks, cache_stride_block,
                                     cache_stride_row, block_table, block_table_stride, max_blocks, ctx, num_tokens, num_heads,
                                     width, page, scale, num_kv_splits, workspace, workspace_floats, error_flag);
+  if (flags & ~HLA_S6_PARTIALS_AFTER_QUERY) {
+    set_error("history partials: unknown flags 0x%x", flags);
+    return kStatusInvalid;
+  }
+  a.pdl = (flags & HLA_S6_PARTIALS_AFTER_QUERY) != 0;
   int rc = check_history_args(a);
   if (rc) return rc;
   HistoryPlan plan;

@@ -150,6 +150,9 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int x = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * 64;
   constexpr int HALF = W / 2;
+  // a history split launched as this grid's programmatic dependent may start streaming pages now;
+  // it reads q_lat only after this grid has completed
+  if (tid == 0) griddep_launch_dependents();
   if (x >= W / 64) {
     const int32_t* qsl = stage_qsl(p.qsl, p.R, reinterpret_cast<int32_t*>(qs));  // q tile unused here
     // ---------------- exact part: 16 tokens of head h per CTA; thread = (token, 8 rotation pairs)

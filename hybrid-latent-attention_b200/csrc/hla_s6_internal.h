@@ -54,6 +54,7 @@ struct HistoryArgs {
   int64_t ws_floats;
   int32_t waves;            // CTAs per SM slot multiplier for the stream-K grid (>= 1)
   int* err;
+  int32_t pdl = 0;          // launch the split as a programmatic dependent of the preceding launch
 };
 
 struct HistoryPlan {

@@ -81,12 +81,18 @@ class S6DecodeModel:
       holding ``world`` parts, plus a flag word per part) and raises the flags; the combine waits
       for them.  No collective library call is on the step.
     * ``'nccl'``: the reduce writes a local part and an NCCL ``all_gather_into_tensor`` moves it.
+
+    ``pdl`` (default on): the history split is launched as a programmatic dependent of the prepare
+    (it streams pages while the prepare runs and reads q_lat after it), and the combine (or the
+    sequence split's reduce) as one of the history split.  ``pdl=False`` serialises every launch;
+    the results are bit-identical.
     """
 
     def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
-                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=False):
+                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=False, pdl=True):
         self.s, self.device = shape, torch.device(device)
         self.window_overlap = window_overlap
+        self.pdl = pdl
         s = shape
         B = len(batch.ctx)
         self.B = B
@@ -259,7 +265,9 @@ class S6DecodeModel:
         h = a[:, 3 * D:]
         return q, k, v, h
 
-    def _history(self, layer, loop, stream):
+    def _history(self, layer, loop, stream, flags=0):
+        """The history split of one (layer, loop); ``flags=PARTIALS_AFTER_QUERY`` when the preceding launch
+        on ``stream`` is this (layer, loop)'s prepare, which writes q_lat."""
         s, B = self.s, self.B
         A, _, width = self.layers[layer].readers(loop)
         cache = self.l1[layer] if loop == 0 else self.main[layer]
@@ -267,7 +275,7 @@ class S6DecodeModel:
         _lib.call('hla_s6_history_partials', _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), _lib.ptr(cache),
                   cache.shape[0], cache.stride(0), cache.stride(2), _lib.ptr(self.latent_table),
                   self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.ctx_latent), B, s.heads,
-                  width, s.page, float(self.scale), self.splits, _lib.ptr(self.ws), self.ws_floats, None, stream)
+                  width, s.page, float(self.scale), self.splits, _lib.ptr(self.ws), self.ws_floats, None, flags, stream)
 
     def layer_loop(self, layer, loop, stream, wstream=None):
         """The four launches of one (layer, loop); the writer goes to ``wstream`` when given (it reads only
@@ -326,11 +334,14 @@ class S6DecodeModel:
                       _lib.ctypes.c_void_p(self._win_stream.cuda_stream))
             win_done = torch.cuda.Event()
             win_done.record(self._win_stream)
-        # 3. history split
-        self._history(layer, loop, stream)
+        # 3. history split, a programmatic dependent of the prepare just launched (pages stream meanwhile;
+        #    q_lat is read once the prepare has completed).  The side-stream window, when on, sits between
+        #    them in host order only, on another stream.
+        self._history(layer, loop, stream, _lib.PARTIALS_AFTER_QUERY if self.pdl else 0)
         # 3b. sequence split: reduce this GPU's slice to (z, lse) and all-gather the parts
         z_in = lse_in = None
-        parts, part_stride, flags = 0, 0, _lib.COMBINE_AFTER_PARTIALS
+        after = _lib.COMBINE_AFTER_PARTIALS if self.pdl else 0
+        parts, part_stride, flags = 0, 0, after
         part_flags = part_seen = None
         if self.exchange is not None and self.exchange_mode == 'peer':
             import ctypes
@@ -341,13 +352,14 @@ class S6DecodeModel:
             flags_out = [b + self.x_region + (i * world + rank) * 4 for b in self.x_bases]
             _lib.call('hla_s6_history_reduce_exchange', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws),
                       self.ws_floats, None, _lib.pointer_array(parts), _lib.pointer_array(flags_out),
-                      _lib.ptr(self.x_counters[2 * i]), world, _lib.REDUCE_AFTER_PARTIALS, stream)
+                      _lib.ptr(self.x_counters[2 * i]), world, _lib.REDUCE_AFTER_PARTIALS if self.pdl else 0,
+                      stream)
             own = self.x_bases[rank] + i * world * part_stride * 4
             z_in = ctypes.c_void_p(own)
             lse_in = ctypes.c_void_p(own + B * s.heads * width * 4)
             part_flags = ctypes.c_void_p(self.x_bases[rank] + self.x_region + i * world * 4)
             part_seen = _lib.ptr(self.x_counters[2 * i + 1])
-            parts, flags = world, _lib.COMBINE_AFTER_PARTIALS   # its producer is the reduce just launched
+            parts, flags = world, after   # its producer is the reduce just launched
         elif self.exchange is not None:
             rank, world, group = self.exchange
             zf = B * s.heads * width

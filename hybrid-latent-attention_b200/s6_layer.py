@@ -128,7 +128,7 @@ def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_sc
         bt = ctx.block_table(block_table)
         _lib.call('hla_s6_history_partials', _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), _lib.ptr(cache), nb,
                   sb, sr, _lib.ptr(bt), bt.stride(0), bt.shape[1], _lib.ptr(ctx.ctx_latent), T, H, width, lpage,
-                  float(ctx.scale), int(splits), _lib.ptr(ws_ptr), ws_floats, None, stream)
+                  float(ctx.scale), int(splits), _lib.ptr(ws_ptr), ws_floats, None, 0, stream)
         z_in = lse_in = None
         empty = ctx.empty_latent
     else:

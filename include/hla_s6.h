@@ -73,13 +73,18 @@ int hla_s6_history_attention_static(const void* q_lat, int64_t q_stride_t, int64
 
 /* Split stage only: leaves fp32 partials (o, lse per row segment) in the workspace for
  * hla_s6_history_reduce or hla_s6_decode_combine with the same (T, H, W, page, splits,
- * workspace).  Replaces the stage-1 half of s6_ops.py:156-159 (vLLM _fwd_grouped_kernel_stage1). */
+ * workspace).  Replaces the stage-1 half of s6_ops.py:156-159 (vLLM _fwd_grouped_kernel_stage1).
+ * flags: HLA_S6_PARTIALS_AFTER_QUERY launches the split as a programmatic dependent of the
+ * immediately preceding launch on the stream, which must be the one that writes q_lat (for example
+ * hla_s6_decode_prepare) and must write nothing else this call reads: the split then streams cache
+ * pages while that launch runs and reads q_lat only after it has completed. */
+#define HLA_S6_PARTIALS_AFTER_QUERY 1
 int hla_s6_history_partials(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
                             int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,
                             const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
                             const int32_t* ctx, int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, float scale,
                             int32_t num_kv_splits, float* workspace, int64_t workspace_floats, int* error_flag,
-                            void* stream);
+                            int32_t flags, void* stream);
 
 /* Reduce stage: partials -> out (bf16, optional), out_f32 (fp32 [T, H, W] contiguous, optional)
  * and lse [H, T].  Replaces vLLM _decode_softmax_reducev_fwd called at s6_ops.py:158-159. */

@@ -31,3 +31,27 @@ def test_side_stream_window_matches_fused_window():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(side.out, eager)
+
+
+def test_programmatic_launches_match_serial_launches():
+    """The step's programmatic dependent launches (history split beside the prepare that writes q_lat,
+    combine beside the history split) give bit-identical outputs to fully serialised launches, for
+    every (layer, loop) - each writes the shared q_lat buffer anew, so a stale read would show -
+    eagerly and under graph replay."""
+    dec = pkg('decode')
+    shape = dec.OuroShape(layers=3)
+    batch = dec.DecodeBatch([4096, 1000, 40, 2000, 1, 33, 31, 0, 8192, 300])
+    chained = dec.S6DecodeModel(shape, batch, device='cuda', seed=5, pdl=True)
+    serial = dec.S6DecodeModel(shape, batch, device='cuda', seed=5, pdl=False)
+    chained.step()
+    serial.step()
+    torch.cuda.synchronize()
+    assert torch.isfinite(serial.out.float()).all()
+    assert torch.equal(chained.out, serial.out)
+    g = chained.capture()
+    expect = chained.out.clone()
+    for _ in range(3):
+        chained.out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(chained.out, expect)
