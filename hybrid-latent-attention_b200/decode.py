@@ -412,6 +412,48 @@ class S6DecodeModel:
                 self.layer_loop(layer, loop, stream, wstream)
         main.wait_stream(side)
 
+    def step_io(self, host_in, host_out):
+        """One decode step fed from and drained to pinned host memory: ``host_in`` is ``acts``' shape
+        ([layers, loops, B, q | k | v | h]), ``host_out`` is ``out``'s.  The copies are pipelined
+        with the compute per (layer, loop), in the step's order: a copy stream brings each (layer,
+        loop)'s activations in ahead of its launches, which wait only for their own slice (the
+        writer branch included), and each output goes back to the host as soon as its combine has
+        finished.  Only the first slice's copy-in and the last output's copy-out stay exposed.  The
+        results equal ``acts.copy_(host_in); step(); host_out.copy_(out)``."""
+        s = self.s
+        main = torch.cuda.current_stream(self.device)
+        if getattr(self, '_io', None) is None:
+            self._io = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+        h2d, d2h, side = self._io
+        for st in (h2d, d2h, side):
+            st.wait_stream(main)
+        order = [(layer, loop) for loop in range(s.loops) for layer in range(s.layers)]
+        ready = []
+        with torch.cuda.stream(h2d):
+            for layer, loop in order:
+                self.acts[layer, loop].copy_(host_in[layer, loop], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                ready.append(ev)
+        stream = _lib.stream_of(self.out)
+        wstream = _lib.ctypes.c_void_p(side.cuda_stream)
+        for (layer, loop), ev in zip(order, ready):
+            main.wait_event(ev)
+            side.wait_event(ev)
+            self.layer_loop(layer, loop, stream, wstream)
+            done = torch.cuda.Event()
+            done.record(main)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                host_out[layer, loop].copy_(self.out[layer, loop], non_blocking=True)
+        for st in (h2d, d2h, side):
+            main.wait_stream(st)
+
+    def capture_io(self, host_in, host_out):
+        """``step_io`` captured as one CUDA graph (copies and kernels)."""
+        self.io_graph = self._capture(lambda: self.step_io(host_in, host_out))
+        return self.io_graph
+
     def history_only(self):
         """The 96 history-split launches of a step alone (roofline timing of the dominant kernel)."""
         stream = _lib.stream_of(self.out)

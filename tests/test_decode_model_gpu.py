@@ -55,3 +55,35 @@ def test_programmatic_launches_match_serial_launches():
         g.replay()
         torch.cuda.synchronize()
         assert torch.equal(chained.out, expect)
+
+
+def test_pipelined_host_io_step_matches_copy_step_copy():
+    """step_io (per-(layer, loop) copy-in ahead of the launches, copy-out after each combine, on their own
+    streams) gives exactly acts <- host_in; step(); host_out <- out - eagerly and as a replayed graph,
+    with new host inputs between replays."""
+    dec = pkg('decode')
+    shape = dec.OuroShape(layers=2)
+    batch = dec.DecodeBatch([3000, 17, 0, 500, 64, 1])
+    piped = dec.S6DecodeModel(shape, batch, device='cuda', seed=9)
+    plain = dec.S6DecodeModel(shape, batch, device='cuda', seed=9)
+    g = torch.Generator().manual_seed(3)
+    host_in = torch.empty(piped.acts.shape, dtype=piped.acts.dtype, pin_memory=True)
+    host_out = torch.empty(piped.out.shape, dtype=piped.out.dtype, pin_memory=True)
+
+    def check():
+        plain.acts.copy_(host_in)
+        plain.step()
+        torch.cuda.synchronize()
+        assert torch.equal(host_out, plain.out.cpu())
+
+    host_in.copy_(torch.randn(host_in.shape, generator=g).to(host_in.dtype))
+    piped.step_io(host_in, host_out)
+    torch.cuda.synchronize()
+    check()
+    graph = piped.capture_io(host_in, host_out)
+    for _ in range(2):
+        host_in.copy_(torch.randn(host_in.shape, generator=g).to(host_in.dtype))
+        host_out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        check()
