@@ -79,7 +79,8 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
       o[3] = __bfloat162float(b[1].y);
       lse_w = p.chunk_lse[static_cast<int64_t>(h) * T + t];
     } else if (t < T) {
-      window_warp(win, t, h, q_s + warp * 128, o, lse_w);
+      if (!win.ctx_tok && win.window <= 32) window_warp_short(win, t, h, q_s + warp * 128, o, lse_w);
+      else window_warp(win, t, h, q_s + warp * 128, o, lse_w);
     } else {
       o[0] = o[1] = o[2] = o[3] = 0.f;
       lse_w = -INFINITY;
@@ -139,32 +140,44 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
           lo = m.x;
           hi = m.y;
         }
-        // up to 4 partial slots per pass, all loads of a pass issued together
-        float mx = -INFINITY;
-        for (int s = lo; s < hi; ++s) mx = fmaxf(mx, p.ws_lse[static_cast<int64_t>(s) * H + h]);
-        if (mx != -INFINITY) {
-          float wsum = 0.f;
-          for (int s0 = lo; s0 < hi; s0 += 4) {
-            float wgt[4];
-            float4 v[4][NV];
+        // up to 4 partial slots per pass, their lse and rows loaded together (one memory round for a row
+        // with <= 4 partials); the running max rescales the sums when a later pass raises it
+        float mx = -INFINITY, wsum = 0.f;
+        for (int s0 = lo; s0 < hi; s0 += 4) {
+          float ls[4];
+          float4 v[4][NV];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int s = s0 + u;
-              wgt[u] = s < hi ? expf(p.ws_lse[static_cast<int64_t>(s) * H + h] - mx) : 0.f;
-              const float4* src = reinterpret_cast<const float4*>(p.ws_o + (static_cast<int64_t>(s < hi ? s : lo) * H + h) * W);
+          for (int u = 0; u < 4; ++u) {
+            const int s = s0 + u;
+            ls[u] = s < hi ? p.ws_lse[static_cast<int64_t>(s) * H + h] : -INFINITY;
+            const float4* src = reinterpret_cast<const float4*>(p.ws_o + (static_cast<int64_t>(s < hi ? s : lo) * H + h) * W);
 #pragma unroll
-              for (int i = 0; i < NV; ++i) v[u][i] = s < hi ? src[i * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < NV; ++i) v[u][i] = s < hi ? src[i * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          const float m2 = fmaxf(fmaxf(mx, fmaxf(ls[0], ls[1])), fmaxf(ls[2], ls[3]));
+          if (m2 == -INFINITY) continue;
+          if (m2 != mx) {
+            const float sc = expf(mx - m2);  // 0 while nothing has been summed (mx = -inf)
+            wsum *= sc;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+              acc[i].x *= sc; acc[i].y *= sc; acc[i].z *= sc; acc[i].w *= sc;
             }
+            mx = m2;
+          }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              wsum += wgt[u];
+          for (int u = 0; u < 4; ++u) {
+            if (ls[u] == -INFINITY) continue;  // past hi, or a slot without keys
+            const float wgt = expf(ls[u] - mx);
+            wsum += wgt;
 #pragma unroll
-              for (int i = 0; i < NV; ++i) {
-                acc[i].x += wgt[u] * v[u][i].x; acc[i].y += wgt[u] * v[u][i].y;
-                acc[i].z += wgt[u] * v[u][i].z; acc[i].w += wgt[u] * v[u][i].w;
-              }
+            for (int i = 0; i < NV; ++i) {
+              acc[i].x += wgt * v[u][i].x; acc[i].y += wgt * v[u][i].y;
+              acc[i].z += wgt * v[u][i].z; acc[i].w += wgt * v[u][i].w;
             }
           }
+        }
+        if (mx != -INFINITY) {
           const float inv = 1.f / wsum;
 #pragma unroll
           for (int i = 0; i < NV; ++i) {

@@ -27,7 +27,8 @@ __global__ void __launch_bounds__(128) window_kernel(const WindowArgs a, __nv_bf
   if (!a.ctx_tok) w.qsl = stage_qsl(a.qsl, a.R, qsl_s);
   if (h >= H) return;
   float o[4], lse;
-  window_warp(w, t, h, q_s[warp], o, lse);
+  if (!w.ctx_tok && w.window <= 32) window_warp_short(w, t, h, q_s[warp], o, lse);
+  else window_warp(w, t, h, q_s[warp], o, lse);
   __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + lane * 4;
   reinterpret_cast<__nv_bfloat162*>(dst)[0] = __floats2bfloat162_rn(o[0], o[1]);
   reinterpret_cast<__nv_bfloat162*>(dst)[1] = __floats2bfloat162_rn(o[2], o[3]);

@@ -218,6 +218,118 @@ __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, f
   lse = mx + logf(l);
 }
 
+// window_warp for a window of at most 32 history keys (the decode window, W = 32) in two dependent
+// memory rounds instead of one per 16 keys: round 1 fetches q and the block-table entries of every
+// key, round 2 issues all K and V loads at once - lane l's K row (history key first + l) and, for
+// the value accumulation, its 4 dims of every key's V row.  A 33rd key (the current token when the
+// window is full) is scored by the whole warp (4 dims per lane, warp sum).  Same math and key order
+// as window_warp; the current token's dot product is summed across lanes.  Only for the decode
+// mode (ctx_tok unset) with window <= 32.
+__device__ __forceinline__ void window_warp_short(const WindowArgs& a, int t, int h, float* q_s, float (&o)[4],
+                                                  float& lse) {
+  const int lane = threadIdx.x & 31;
+  o[0] = o[1] = o[2] = o[3] = 0.f;
+  lse = -INFINITY;
+  int r;
+  if (!token_request(a.qsl, a.R, t, r)) return;
+  const int qlen = a.qsl[r + 1] - a.qsl[r];
+  const int64_t pos = static_cast<int64_t>(a.seq_lens[r]) - qlen + (t - a.qsl[r]);
+  if (pos < 0) return;
+  const int64_t first = pos - a.window > 0 ? pos - a.window : 0;
+  const int n = static_cast<int>(pos - first + 1);          // <= 33
+  const int nl = n < 32 ? n : 32;                           // keys owned by lanes; key 32 (if any) is shared
+  auto row_of = [&](int64_t j) -> int64_t {                 // element offset of key j's row, or -1
+    const int64_t col = j / a.page;
+    if (col >= a.max_blocks) return -1;
+    const int blk = a.bt[static_cast<int64_t>(r) * a.bt_st + col];
+    if (blk < 0 || blk >= a.num_blocks) return -1;
+    return static_cast<int64_t>(blk) * a.c_sb + static_cast<int64_t>(h) * a.c_sh + (j % a.page) * a.c_sr;
+  };
+  // ---- round 1: q and the rows' block ids
+  const uint2 qu = *reinterpret_cast<const uint2*>(a.q + static_cast<int64_t>(t) * a.q_st +
+                                                   static_cast<int64_t>(h) * a.q_sh + lane * 4);
+  const int64_t off = lane < nl ? row_of(first + lane) : -1;
+  const int64_t offx = n > 32 ? row_of(first + 32) : -1;   // same address in every lane
+  {
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&qu);
+    __syncwarp();
+    q_s[lane * 4 + 0] = __bfloat162float(b[0].x);
+    q_s[lane * 4 + 1] = __bfloat162float(b[0].y);
+    q_s[lane * 4 + 2] = __bfloat162float(b[1].x);
+    q_s[lane * 4 + 3] = __bfloat162float(b[1].y);
+  }
+  __syncwarp();
+  // ---- round 2: every K and V load of the window
+  uint4 kr[16];
+  if (off >= 0) {
+    const uint4* kp = reinterpret_cast<const uint4*>(a.cache + off);
+#pragma unroll
+    for (int v = 0; v < 16; ++v) kr[v] = __ldg(kp + v);
+  }
+  uint2 vv[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const int64_t ro = __shfl_sync(0xffffffffu, off, e);
+    vv[e] = ro >= 0 ? __ldg(reinterpret_cast<const uint2*>(a.cache + ro + 128 + lane * 4)) : make_uint2(0u, 0u);
+  }
+  uint2 kx = make_uint2(0u, 0u), vx = make_uint2(0u, 0u);
+  if (offx >= 0) {
+    kx = __ldg(reinterpret_cast<const uint2*>(a.cache + offx + lane * 4));
+    vx = __ldg(reinterpret_cast<const uint2*>(a.cache + offx + 128 + lane * 4));
+  }
+  // ---- scores
+  float sc = -INFINITY;
+  if (off >= 0) {
+    float dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < 16; ++v) {
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&kr[v]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dot = fmaf(q_s[v * 8 + 2 * e], __bfloat162float(b[e].x), dot);
+        dot = fmaf(q_s[v * 8 + 2 * e + 1], __bfloat162float(b[e].y), dot);
+      }
+    }
+    sc = dot * a.scale;
+  }
+  float scx = -INFINITY;
+  if (offx >= 0) {
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&kx);
+    float part = q_s[lane * 4 + 0] * __bfloat162float(b[0].x);
+    part = fmaf(q_s[lane * 4 + 1], __bfloat162float(b[0].y), part);
+    part = fmaf(q_s[lane * 4 + 2], __bfloat162float(b[1].x), part);
+    part = fmaf(q_s[lane * 4 + 3], __bfloat162float(b[1].y), part);
+    scx = warp_sum(part) * a.scale;
+  }
+  const float mx = fmaxf(warp_max(sc), scx);
+  if (mx == -INFINITY) return;
+  const float p = sc == -INFINITY ? 0.f : expf(sc - mx);
+  const float px = scx == -INFINITY ? 0.f : expf(scx - mx);
+  const float l = warp_sum(p) + px;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const float pw = __shfl_sync(0xffffffffu, p, e);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&vv[e]);
+    o[0] = fmaf(pw, __bfloat162float(b[0].x), o[0]);
+    o[1] = fmaf(pw, __bfloat162float(b[0].y), o[1]);
+    o[2] = fmaf(pw, __bfloat162float(b[1].x), o[2]);
+    o[3] = fmaf(pw, __bfloat162float(b[1].y), o[3]);
+  }
+  {
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&vx);
+    o[0] = fmaf(px, __bfloat162float(b[0].x), o[0]);
+    o[1] = fmaf(px, __bfloat162float(b[0].y), o[1]);
+    o[2] = fmaf(px, __bfloat162float(b[1].x), o[2]);
+    o[3] = fmaf(px, __bfloat162float(b[1].y), o[3]);
+  }
+  const float inv = 1.f / l;
+  o[0] *= inv;
+  o[1] *= inv;
+  o[2] *= inv;
+  o[3] *= inv;
+  lse = mx + logf(l);
+}
+
 // ------------------------------------------------------------------ exact append (A10)
 struct ExactArgs {
   __nv_bfloat16* q;  // [T, H, 128] roped in place (may be NULL)

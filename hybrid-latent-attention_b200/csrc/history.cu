@@ -565,8 +565,10 @@ __global__ void __launch_bounds__(kReduceThreads)
       *reinterpret_cast<float4*>(x.part[d] + zoff) = acc;
       if (lse_here) x.part[d][loff] = lse;
     }
+    // each writer makes its own peer stores visible system-wide before the CTA barrier; the other
+    // threads stored nothing (a fence in every thread stalled the kernel on membar)
+    __threadfence_system();
   }
-  __threadfence_system();
   __syncthreads();
   if (tid == 0) {
     const unsigned total = gridDim.x * gridDim.y * gridDim.z;
