@@ -10,8 +10,8 @@ Every step issues the four launches per (layer, loop) of ``decode.S6DecodeModel.
 one), so ``ncu -k regex:history_split -s 1 -c 2`` selects one launch of each width.  With the
 defaults the device holds about 3 GB.
 
-``--seq-split N`` runs rank 0's share of an N-way sequence split (config 5: B = 4 at ctx 128K) as a
-one-rank job: the latent rows of the first of N page slices, the reduce with its peer-store exchange
+``--seq-split N`` runs rank 0's share of an N-way sequence split (config 5: ``--batch 4 --ctx 131072``) as a
+one-rank job (``--time`` also times it as a graph): the latent rows of the first of N page slices, the reduce with its peer-store exchange
 (to this GPU only) and the N = 1 flag wait in the combine; the kernel sequence and sizes per GPU are
 those of the N-GPU step, without the other ranks.
 
@@ -32,6 +32,20 @@ from pathlib import Path
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
 
+def _graph_ms(torch, graph, reps):
+    """Device time per replay of a captured graph (CUDA events, after three warm-up replays)."""
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--layers', type=int, default=2)
@@ -42,6 +56,9 @@ def main():
     ap.add_argument('--prompts', type=int, default=8)
     ap.add_argument('--seq-split', type=int, default=0)
     ap.add_argument('--reader', choices=['contig', 'heads', 'export'])
+    ap.add_argument('--time', action='store_true',
+                    help='with --seq-split: capture the step as a CUDA graph and report its device time and that of '
+                         'its history launches alone (CUDA events)')
     args = ap.parse_args()
     import torch
     dec = importlib.import_module('hybrid-latent-attention_b200.decode')
@@ -59,6 +76,12 @@ def main():
         for _ in range(args.steps):
             model.step(overlap_writer=False)
         torch.cuda.synchronize()
+        if args.time:
+            ms, ms_hist = _graph_ms(torch, model.capture(), 20), _graph_ms(torch, model.capture_history(), 20)
+            loops = shape.layers * shape.loops
+            print(f'1/{args.seq_split} slice: step {ms:.3f} ms, history launches alone {ms_hist:.3f} ms, the rest '
+                  f'{(ms - ms_hist) / loops * 1e3:.1f} us per (layer, loop)')
+            model.graph = model.history_graph = None
         model.close_exchange()
         dist.destroy_process_group()
         print(f'ok: {args.steps} steps of a 1/{args.seq_split} sequence-split slice, '
