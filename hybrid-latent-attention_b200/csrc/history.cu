@@ -538,6 +538,89 @@ __global__ void __launch_bounds__(kReduceThreads, 1) history_reduce_kernel(const
   if (tid == 0 && blockIdx.z == 0 && lse_out) lse_out[static_cast<int64_t>(h) * lse_sh + t * lse_st] = lse;
 }
 
+// Stage-2 merge for rows with few partials (the usual decode and contiguous-reader case: about
+// grid / T + 1 slots per row): one warp per (row t, head h), all W columns - lane l holds float4
+// columns l, l + 32, ... - and the slots' lse and rows loaded together, up to 4 (W = 1024: 2) slots
+// per memory round, with an online rescale when a later round raises the max.  Launched as a
+// programmatic dependent of the split (reduce_pdl): it waits for the split grid before its first
+// read.  Same outputs as history_reduce_kernel.
+constexpr int kReduceWarpHeads = 4;  // warps (rows x heads) per CTA
+template <int W>
+__global__ void __launch_bounds__(32 * kReduceWarpHeads)
+    history_reduce_warp_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
+                               const int2* __restrict__ meta, int stream_mode, int T, int H,
+                               const uint8_t* __restrict__ empty, __nv_bfloat16* __restrict__ out, int64_t o_st,
+                               int64_t o_sh, float* __restrict__ out_f32, float* __restrict__ lse_out, int64_t lse_st,
+                               int64_t lse_sh) {
+  griddep_wait();
+  constexpr int NV = W / 128, U = NV > 4 ? 2 : 4;
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.x * kReduceWarpHeads + (threadIdx.x >> 5);
+  if (pair >= T * H) return;
+  const int t = pair / H, h = pair % H;
+  int lo = t, hi = t + 1;
+  if (stream_mode) {
+    const int2 m = meta[t];
+    lo = m.x;
+    hi = m.y;
+  }
+  float4 acc[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float mx = -INFINITY, wsum = 0.f;
+  if (!(empty && empty[t])) {
+    for (int s0 = lo; s0 < hi; s0 += U) {
+      float ls[U];
+      float4 v[U][NV];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int s = s0 + u;
+        ls[u] = s < hi ? ws_lse[static_cast<int64_t>(s) * H + h] : -INFINITY;
+        const float4* src = reinterpret_cast<const float4*>(ws_o + (static_cast<int64_t>(s < hi ? s : lo) * H + h) * W);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) v[u][i] = s < hi ? src[i * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float m2 = mx;
+#pragma unroll
+      for (int u = 0; u < U; ++u) m2 = fmaxf(m2, ls[u]);
+      if (m2 == -INFINITY) continue;
+      if (m2 != mx) {
+        const float sc = expf(mx - m2);  // 0 while nothing has been summed
+        wsum *= sc;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          acc[i].x *= sc; acc[i].y *= sc; acc[i].z *= sc; acc[i].w *= sc;
+        }
+        mx = m2;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (ls[u] == -INFINITY) continue;
+        const float w = expf(ls[u] - mx);
+        wsum += w;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          acc[i].x += w * v[u][i].x; acc[i].y += w * v[u][i].y; acc[i].z += w * v[u][i].z; acc[i].w += w * v[u][i].w;
+        }
+      }
+    }
+  }
+  const bool is_empty = mx == -INFINITY;
+  const float inv = is_empty ? 0.f : 1.f / wsum;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 r = make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
+    const int c = (i * 32 + lane) * 4;
+    if (out) {
+      __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + c;
+      reinterpret_cast<__nv_bfloat162*>(dst)[0] = __floats2bfloat162_rn(r.x, r.y);
+      reinterpret_cast<__nv_bfloat162*>(dst)[1] = __floats2bfloat162_rn(r.z, r.w);
+    }
+    if (out_f32) *reinterpret_cast<float4*>(out_f32 + (static_cast<int64_t>(t) * H + h) * W + c) = r;
+  }
+  if (lane == 0 && lse_out) lse_out[static_cast<int64_t>(h) * lse_sh + t * lse_st] = is_empty ? -INFINITY : mx + logf(wsum);
+}
+
 // The sequence-split exchange fused into the reduce: this GPU's part - z fp32 [T, H, W] followed by
 // lse [H, T] - is stored straight into every rank's receive slot (peer memory over NVLink, this
 // GPU's own slot included).  Once every CTA's stores are visible system-wide, the last CTA to
@@ -801,6 +884,33 @@ int history_reduce_strided(const HistoryArgs& a, const HistoryPlan& plan, const 
   if (a.W != 256 && a.W != 512 && a.W != 1024) {
     set_error("unsupported latent width %d", a.W);
     return kStatusInvalid;
+  }
+  if (plan.stream_mode && plan.grid <= 8 * static_cast<int64_t>(a.T)) {
+    // few partials per row (about grid / T + 1): warp per (row, head), launched as a programmatic
+    // dependent of the split
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((static_cast<int64_t>(a.T) * a.H + kReduceWarpHeads - 1) / kReduceWarpHeads));
+    cfg.blockDim = dim3(32 * kReduceWarpHeads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+    cudaError_t e;
+    switch (a.W) {
+      case 256: e = cudaLaunchKernelEx(&cfg, history_reduce_warp_kernel<256>, plan.ws_o, plan.ws_lse, plan.meta,
+                                       plan.stream_mode, a.T, a.H, empty, o, o_st, o_sh, out_f32, lse, lse_st, lse_sh);
+        break;
+      case 512: e = cudaLaunchKernelEx(&cfg, history_reduce_warp_kernel<512>, plan.ws_o, plan.ws_lse, plan.meta,
+                                       plan.stream_mode, a.T, a.H, empty, o, o_st, o_sh, out_f32, lse, lse_st, lse_sh);
+        break;
+      default: e = cudaLaunchKernelEx(&cfg, history_reduce_warp_kernel<1024>, plan.ws_o, plan.ws_lse, plan.meta,
+                                      plan.stream_mode, a.T, a.H, empty, o, o_st, o_sh, out_f32, lse, lse_st, lse_sh);
+        break;
+    }
+    return cuda_status(e, "history_reduce_warp_kernel launch");
   }
   dim3 grid(a.T, a.H, a.W / (4 * kReduceCols));
 #define HLA_REDUCE(WW)                                                                                          \
