@@ -219,3 +219,46 @@ def meta_cases():
                        (100, 8, 512, 108), (8448, 513, 512, 108), (1 << 20, 1, 512, 4), (8192, 64, 512, 148),
                        (8192, 1, 512, 148), (32768, 256, 512, 148), (131072, 4, 512, 148)],
     )
+
+
+def _neox_rope(x, positions, base=10000.0):
+    """Rotate-half RoPE over the last dim (head_dim 128) at integer positions, float64."""
+    d = x.shape[-1]
+    inv = base ** (-np.arange(0, d, 2, dtype=np.float64) / d)
+    ang = np.asarray(positions, dtype=np.float64)[..., None] * inv
+    c, s = np.cos(ang), np.sin(ang)
+    x1, x2 = x[..., :d // 2].astype(np.float64), x[..., d // 2:].astype(np.float64)
+    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
+
+
+def config1_case(seed=2048, heads=16, head_dim=128, ctx=2048, window=32, page=16, rank=512, rank1=256, loops=4,
+                 latent_theta=10000.0, max_pos=4096):
+    """one layer of the S6 hybrid decode op (4 loops; loop 0 reads the loop-1 latent of
+    width rank1, loops 1-3 the main latent of width rank) for batch 1 at context 2048 - 2016 latent rows
+    and a W = 32 exact window plus the current token (position 2048).  Values N(0, 1); absorb A_t
+    [H, d, w] ~ N(0, 1/sqrt(d)) and up-projection B_t [H, w, d] ~ N(0, 1/sqrt(w)); window K and the
+    query rotated with RoPE base 10000; page 16 with identity page tables (block j holds page j).
+    Every value is bf16-representable."""
+    rng = np.random.default_rng(seed)
+    H, d = heads, head_dim
+    ctx_lat = ctx - window
+    pages = -(-(ctx + 1) // page)                        # pages of positions 0 .. ctx
+    table = np.arange(pages, dtype=np.int32)[None, :]    # identity: block j = page j
+    out = dict(table=table, ctx=np.array([ctx], dtype=np.int32), ctx_lat=np.array([ctx_lat], dtype=np.int32),
+               positions=np.array([ctx], dtype=np.int64), seq_lens=np.array([ctx + 1], dtype=np.int32),
+               query_start_loc=np.array([0, 1], dtype=np.int32), window=np.int32(window),
+               latent_theta=np.float64(latent_theta), max_pos=np.int32(max_pos))
+    out['lat_main'] = _bf16(rng.standard_normal((pages, 1, page, 2 * rank), dtype=np.float32))
+    out['lat_l1'] = _bf16(rng.standard_normal((pages, 1, page, 2 * rank1), dtype=np.float32))
+    pos_rows = (np.arange(pages)[:, None] * page + np.arange(page)[None, :])          # [pages, page]
+    for t in range(loops):
+        w = rank1 if t == 0 else rank
+        out[f'q_pre{t}'] = _bf16(rng.standard_normal((1, H, d), dtype=np.float32))
+        out[f'A{t}'] = _bf16(rng.standard_normal((H, d, w), dtype=np.float32) / np.sqrt(d))
+        out[f'B{t}'] = _bf16(rng.standard_normal((H, w, d), dtype=np.float32) / np.sqrt(w))
+        out[f'q_rope{t}'] = _bf16(_neox_rope(rng.standard_normal((1, H, d)), [[ctx]]))
+        k = rng.standard_normal((pages, page, H, d))
+        k = _neox_rope(k, pos_rows[:, :, None])
+        v = rng.standard_normal((pages, page, H, d))
+        out[f'exact{t}'] = _bf16(np.concatenate([k, v], axis=-1))                       # physical [nb, page, H, 2d]
+    return out

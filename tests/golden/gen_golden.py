@@ -76,6 +76,38 @@ def main():
     lse = lse.masked_fill(invalid[None, :], -float('inf'))
     save('window_decode', w, o=o.numpy(), lse=lse.numpy(), scale=np.float64(scale))
 
+    # ---- one layer x 4 loops of the decode op in fp32 (latent query with the bf16 table
+    #      as serving computes it, then history + B + exact window + merge with fp32 arithmetic)
+    c1 = cases.config1_case()
+    inv = s6_layer.latent_inv_freq(128, float(c1['latent_theta']))
+    tabs = {w: s6_layer.latent_rope_table(int(c1['max_pos']), inv, w, torch.bfloat16) for w in (256, 512)}
+    pos = T_(c1['positions'])
+    qsl, seq_lens, table = T_(c1['query_start_loc']), T_(c1['seq_lens']), T_(c1['table'])
+    ctx1, ctx_lat1, window = T_(c1['ctx']), T_(c1['ctx_lat']), int(c1['window'])
+    scale = 1 / math.sqrt(128)
+    invalid = torch.zeros(1, dtype=torch.bool)
+    outs = {}
+    for t in range(4):
+        w = 256 if t == 0 else 512
+        q_lat = s6_layer.latent_query(T_(c1[f'q_pre{t}']).bfloat16(), T_(c1[f'A{t}']).bfloat16(), pos, tabs[w], 'torch')
+        q_lat = q_lat.float()
+        cache = T_(c1['lat_l1'] if t == 0 else c1['lat_main'])
+        o_h, lse_h = s6_ops.history_attention(q_lat, cache, table, ctx_lat1, scale, 1, None, None, None, 'torch')
+        o_h = torch.einsum('thr,hrd->thd', o_h, T_(c1[f'B{t}']))
+        phys = T_(c1[f'exact{t}'])
+        last = int(c1['ctx'][0])
+        cur = phys[int(c1['table'][0, last // 16]), last % 16][None]          # [1, H, 2d]
+        q_rope = T_(c1[f'q_rope{t}'])
+        o_c, lse_c = s6_ops.chunk_attention(q_rope, cur[..., :128].contiguous(), cur[..., 128:].contiguous(), qsl, 1,
+                                            invalid, scale, 'torch')
+        o_w, lse_w = s6_ops.window_attention(q_rope, phys.transpose(1, 2), table, ctx1, window, scale)
+        o_x, lse_x = s6_ops.merge_lse(o_w, lse_w, o_c, lse_c)
+        out = s6_ops.merge_states(o_h, lse_h, o_x, lse_x, invalid, 'torch')
+        outs[f'q_lat{t}'] = q_lat.numpy()
+        outs[f'lse_hist{t}'] = lse_h.numpy()
+        outs[f'out{t}'] = out.numpy()
+    save('config1', c1, scale=np.float64(scale), **outs)
+
     # ---- A5 prefill pieces: causal chunk attention and the per-token window history
     c = cases.chunk_case()
     qsl = T_(c['query_start_loc'])

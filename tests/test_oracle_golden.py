@@ -198,3 +198,32 @@ def test_slot_mapping_and_scatter_skip_padding():
     written = {int(s) for s in slots if s >= 0}
     for s in range(flat.shape[0]):
         assert np.isnan(flat[s]).all() != (s in written)
+
+
+def test_config1_decode_op_matches_reference():
+    """BASELINE config 1 - one layer x 4 loops of the S6 decode op at context 2048 (2016 latent rows, W = 32
+    window + the current token, identity page tables), the reference computing in fp32: the oracle's
+    latent query (from q_pre and the absorb A, bf16 RoPE table) and its history + B + window + merge
+    composition against the reference's outputs, loop by loop (loop 0 on the 256-wide loop-1 latent)."""
+    c = cases.config1_case()
+    g = load('config1', c)
+    scale = float(g['scale'])
+    inv = orc.latent_inv_freq(128, float(c['latent_theta']))
+    ex_bt = c['table']
+    for t in range(4):
+        w = 256 if t == 0 else 512
+        table = orc.bf16(orc.latent_rope_table(int(c['max_pos']), inv, w))
+        # the reference runs the latent query in bf16: the einsum rounded once, then the torch bf16 RoPE order
+        x = orc.bf16(np.einsum('thd,hdr->thr', c[f'q_pre{t}'].astype(np.float64), c[f'A{t}'].astype(np.float64)))
+        q_lat = orc.latent_rope(x, c['positions'], table, emulate_bf16=True)
+        same = q_lat == g[f'q_lat{t}']
+        assert same.mean() > 0.99, f'loop {t}: {same.mean():.4f} of q_lat bit-exact'
+        np.testing.assert_allclose(q_lat, g[f'q_lat{t}'], rtol=0, atol=1.6e-2)   # the rest: one bf16 ulp apart
+        cache = c['lat_l1'] if t == 0 else c['lat_main']
+        o, lse = orc.history_attention(g[f'q_lat{t}'], cache, c['table'], c['ctx_lat'], scale)
+        np.testing.assert_allclose(lse, g[f'lse_hist{t}'], atol=1e-5, rtol=0)
+        out = orc.attend_decode(g[f'q_lat{t}'], c[f'q_rope{t}'], cache, c['table'], c['ctx_lat'],
+                                c[f'exact{t}'].transpose(0, 2, 1, 3), ex_bt, c['query_start_loc'], c['seq_lens'],
+                                int(c['window']), c[f'B{t}'], scale, np.zeros(1, dtype=bool))
+        np.testing.assert_allclose(out, g[f'out{t}'], rtol=1e-4, atol=1e-5)
+        assert np.isfinite(out).all() and np.abs(out).max() > 1e-3
