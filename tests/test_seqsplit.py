@@ -98,10 +98,11 @@ def _cpu_rank(rank, world, init, out):
         dist.destroy_process_group()
 
 
-def test_two_gloo_ranks_merge_to_the_full_history():
+@pytest.mark.parametrize('world', [2, 4])
+def test_gloo_ranks_merge_to_the_full_history(world):
     with tempfile.TemporaryDirectory() as d:
         init, out = f'file://{os.path.join(d, "rdv")}', os.path.join(d, 'result')
-        _run_ranks(_cpu_rank, 2, init, out, 120)
+        _run_ranks(_cpu_rank, world, init, out, 180)
         assert open(out).read() == 'ok'
 
 
