@@ -675,21 +675,40 @@ def run_contig(args):
     bytes_step = s.layers * B * N * 2 * 2 * ((s.loops - 1) * s.rank + s.rank1)
     peak, peak_kind = peaks()
     achieved = bytes_step / (ms / 1e3) / 1e9
-    # e2e: q and mask in from pinned memory, z and lse out, each read of the step
+    # e2e: q and mask in from pinned memory per loop, z and lse out to pinned memory per read; the copies run
+    # on their own streams (copy-in one loop ahead, copy-out behind each read), pipelined with the reads
     hq = {w: q[w].cpu().pin_memory() for w in q}
     hm = mask.cpu().pin_memory()
-    outs = []
+    reads = [(s.rank1 if loop == 0 else s.rank, layer) for loop in range(s.loops) for layer in range(s.layers)]
+    hz = [torch.empty(B, H, w, dtype=torch.bfloat16, pin_memory=True) for w, _ in reads]
+    hl = [torch.empty(B, H, dtype=torch.float32, pin_memory=True) for _ in reads]
+    dq = {w: torch.empty_like(q[w]) for w in q}
+    dm = torch.empty_like(mask)
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    keep = []
 
     def e2e_step():
-        outs.clear()
+        main = torch.cuda.current_stream()
+        keep.clear()
+        h2d.wait_stream(main)
+        d2h.wait_stream(main)
         for loop in range(s.loops):
             w = s.rank1 if loop == 0 else s.rank
-            qq = hq[w].to('cuda', non_blocking=True)
-            mm = hm.to('cuda', non_blocking=True)
+            with torch.cuda.stream(h2d):
+                dq[w].copy_(hq[w], non_blocking=True)
+                dm.copy_(hm, non_blocking=True)
+            main.wait_stream(h2d)
             for layer in range(s.layers):
+                i = loop * s.layers + layer
                 k, v = kv[w][layer]
-                z, lse = fh.history_attention(qq, k, v, mm, scale)
-                outs.append((z.to('cpu', non_blocking=True), lse.to('cpu', non_blocking=True)))
+                z, lse = fh.history_attention(dq[w], k, v, dm, scale)
+                d2h.wait_stream(main)
+                with torch.cuda.stream(d2h):
+                    hz[i].copy_(z, non_blocking=True)
+                    hl[i].copy_(lse, non_blocking=True)
+                keep.append((z, lse))     # outputs stay alive until their copy-out has run
+            h2d.wait_stream(main)         # the next loop's copy-in waits for this loop's reads of dq / dm
+        main.wait_stream(d2h)
     e2e_step()
     ms_e2e = _events_ms(torch, e2e_step, max(3, args.steps // 4))
     h2d = s.loops * (B * H * s.rank * 2 + B * N)
@@ -727,7 +746,7 @@ def run_contig(args):
             'e2e': {'value': B / (ms_e2e / 1e3), 'unit': 'tokens/s', 'h2d_bytes_per_step': h2d,
                     'd2h_bytes_per_step': d2h,
                     'path': 'fused_history.history_attention per read, q and mask copied in from pinned memory per '
-                            'loop, z and lse copied out per read'},
+                            'loop and z and lse copied out per read, on copy streams pipelined with the reads'},
             'gpu_launches': 2 * s.layers * s.loops * args.steps, 'clocks': clk.summary()}
     print(json.dumps(line), flush=True)
     return line
@@ -784,18 +803,35 @@ def run_heads(args):
     bytes_step = reads * B * H * ctx * Lk * 2
     peak, peak_kind = peaks()
     achieved = bytes_step / (ms / 1e3) / 1e9
-    # e2e: q in from pinned memory per loop, o and lse out per read
+    # e2e: q in from pinned memory per loop, o and lse out to pinned memory per read, on copy streams pipelined
+    # with the reads (as in the contiguous reader's bench)
     hq = q.cpu().pin_memory()
-    outs = []
+    dq = torch.empty_like(q)
+    ho = [torch.empty(B, H, r, dtype=torch.bfloat16, pin_memory=True) for _ in range(layers * loops)]
+    hl = [torch.empty(H, B, dtype=torch.float32, pin_memory=True) for _ in range(layers * loops)]
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    keep = []
 
     def e2e_step():
-        outs.clear()
-        for _ in range(loops):
-            qq = hq.to('cuda', non_blocking=True)
-            for c in caches:
-                o, lse = ops.history_attention_kv(qq, c, c[..., :r], table, ctx_t, scale, splits, ws, None, None,
+        main = torch.cuda.current_stream()
+        keep.clear()
+        h2d.wait_stream(main)
+        d2h.wait_stream(main)
+        for loop in range(loops):
+            with torch.cuda.stream(h2d):
+                dq.copy_(hq, non_blocking=True)
+            main.wait_stream(h2d)
+            for j, c in enumerate(caches):
+                i = loop * layers + j
+                o, lse = ops.history_attention_kv(dq, c, c[..., :r], table, ctx_t, scale, splits, ws, None, None,
                                                   'b200', mla=True)
-                outs.append((o.to('cpu', non_blocking=True), lse.to('cpu', non_blocking=True)))
+                d2h.wait_stream(main)
+                with torch.cuda.stream(d2h):
+                    ho[i].copy_(o, non_blocking=True)
+                    hl[i].copy_(lse, non_blocking=True)
+                keep.append((o, lse))
+            h2d.wait_stream(main)
+        main.wait_stream(d2h)
     e2e_step()
     ms_e2e = _events_ms(torch, e2e_step, max(3, args.steps // 4))
     h2d = loops * B * H * Lk * 2
@@ -834,7 +870,7 @@ def run_heads(args):
             'e2e': {'value': B / (ms_e2e / 1e3), 'unit': 'tokens/s', 'h2d_bytes_per_step': h2d,
                     'd2h_bytes_per_step': d2h,
                     'path': 's6_ops.history_attention_kv(mla=True) per read, q copied in from pinned memory per '
-                            'loop, o and lse copied out per read'},
+                            'loop and o and lse copied out per read, on copy streams pipelined with the reads'},
             'gpu_launches': 2 * reads * args.steps, 'clocks': clk.summary()}
     print(json.dumps(line), flush=True)
     return line
