@@ -123,6 +123,49 @@ class PrefillWriter:
             for layer in range(self.s.layers):
                 self.layer_loop(layer, loop, stream)
 
+    def step_io(self, host_in, host_out, out_src):
+        """One prompt step fed from pinned host memory (``host_in``: ``h``'s shape, the four loops' hidden
+        states) with ``out_src`` (a device tensor the step writes, e.g. a layer's latent cache) read back
+        into ``host_out``.  Each loop's hidden states arrive on a copy stream and that loop's launches
+        wait only for them, so loops 1-3 are copied in during the previous loop's writers; the read-back
+        follows the last launch.  The results equal ``h.copy_(host_in); step(); host_out.copy_(out_src)``."""
+        main = torch.cuda.current_stream(self.device)
+        if getattr(self, '_io', None) is None:
+            self._io = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+        h2d, d2h = self._io
+        h2d.wait_stream(main)
+        d2h.wait_stream(main)
+        ready = []
+        with torch.cuda.stream(h2d):
+            for loop in range(self.s.loops):
+                self.h[loop].copy_(host_in[loop], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                ready.append(ev)
+        stream = _lib.stream_of(self.h)
+        for loop in range(self.s.loops):
+            main.wait_event(ready[loop])
+            for layer in range(self.s.layers):
+                self.layer_loop(layer, loop, stream)
+        d2h.wait_stream(main)
+        with torch.cuda.stream(d2h):
+            host_out.copy_(out_src, non_blocking=True)
+        main.wait_stream(h2d)
+        main.wait_stream(d2h)
+
+    def capture_io(self, host_in, host_out, out_src):
+        """``step_io`` captured as one CUDA graph (copies and kernels)."""
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.step_io(host_in, host_out, out_src)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        self.io_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.io_graph):
+            self.step_io(host_in, host_out, out_src)
+        return self.io_graph
+
     def capture(self):
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))

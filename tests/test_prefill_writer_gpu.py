@@ -52,3 +52,35 @@ def test_prefill_writer_graph_replay_is_deterministic():
     torch.cuda.synchronize()
     for a, b in zip(before, (*m.main, *m.l1)):
         assert torch.equal(a, b)
+
+
+def test_pipelined_host_io_step_matches_copy_step_copy():
+    """PrefillWriter.step_io (each loop's hidden states copied in on a copy stream, the launches of a loop
+    waiting only for their own copy, one cache read back at the end) gives exactly h <- host_in; step();
+    host_out <- cache - eagerly and as a replayed graph with new host inputs."""
+    dec, pre = pkg('decode'), pkg('prefill')
+    shape = dec.OuroShape(layers=2, max_position=4096)
+    piped = pre.PrefillWriter(shape, 2, 300, device='cuda', seed=4)
+    plain = pre.PrefillWriter(shape, 2, 300, device='cuda', seed=4)
+    g = torch.Generator().manual_seed(5)
+    host_in = torch.empty(piped.h.shape, dtype=piped.h.dtype, pin_memory=True)
+    host_out = torch.empty(piped.main[-1].shape, dtype=piped.main[-1].dtype, pin_memory=True)
+
+    def check():
+        plain.h.copy_(host_in)
+        plain.step()
+        torch.cuda.synchronize()
+        assert torch.equal(host_out, plain.main[-1].cpu())
+        assert torch.equal(piped.l1[0], plain.l1[0])
+
+    host_in.copy_(torch.randn(host_in.shape, generator=g).to(host_in.dtype))
+    piped.step_io(host_in, host_out, piped.main[-1])
+    torch.cuda.synchronize()
+    check()
+    graph = piped.capture_io(host_in, host_out, piped.main[-1])
+    for _ in range(2):
+        host_in.copy_(torch.randn(host_in.shape, generator=g).to(host_in.dtype))
+        host_out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        check()
