@@ -119,8 +119,10 @@ int hla_s6_history_attention_contig(const void* q, int64_t q_stride_b, int64_t q
  * row [c | rotated k_rope] read once; widths multiples of 16, value_width in {64, 128, 256, 512},
  * key_width <= 1024, page 16).
  * out bf16 [T, H, value_width] (strided), lse fp32 [H, T]; empty rows (ctx 0 or empty[t]) give
- * o = 0, lse = -inf.  Workspace: T * H * num_kv_splits * (value_width + 1) floats, the reference's
- * attn_logits layout.  A block id outside the cache sets error_flag (3) and reads as zeros.
+ * o = 0, lse = -inf.  Workspace: T * H * num_kv_splits * (value_width + 1) floats, the size of the
+ * reference's attn_logits; within it the kernel keeps stream-K partial slots and a slot range per
+ * (token, head) (num_kv_splits == 1: one slot per (token, head)).  The cache rows must be 16-byte
+ * aligned; pages are read by TMA.  A block id outside the cache sets error_flag (3) and reads as zeros.
  * Replaces hla/vllm_latent/s6_ops.py:128-161 history_attention_kv(..., mla=True) (vLLM
  * decode_attention_fwd_grouped with IS_MLA), as lla_layer.attend calls it (lla_layer.py:67-74). */
 int hla_s6_history_attention_heads(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
