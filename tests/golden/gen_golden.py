@@ -15,6 +15,9 @@ The reference functions called (file:line in the reference project):
   hla/latent/fused_history.py:11 reference (the contiguous-layout reader's torch definition)
   hla/vllm_latent/cache_export.py:13 RolloutCacheExporter (begin / observe / export / finish), driven
   through a stand-in runner that exposes the attributes the exporter reads
+  BASELINE config 1 (config1.npz): s6_layer.latent_query('torch', bf16 table) per loop, then in fp32
+  s6_ops.history_attention('torch'), the B einsum (s6_layer.py:114), chunk_attention('torch') over the
+  current token + window_attention + merge_lse (the exact window), and merge_states('torch')
 """
 from __future__ import annotations
 
