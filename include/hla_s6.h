@@ -1,10 +1,12 @@
 /* libhla_s6 - C ABI of the B200 (sm_100a) S6 hybrid latent-attention decode path.
  *
- * Every entry point takes plain device pointers, element strides and sizes, launches on the
- * given cudaStream_t (passed as void*), never synchronises the host and never allocates
- * device memory: outputs and the fp32 workspace are owned by the caller.  All calls are
- * safe to capture in a CUDA graph (shapes and pointers are baked in at capture; contents
- * such as ctx, block tables, q and the caches may change between replays).
+ * Every compute entry point takes plain device pointers, element strides and sizes, launches on
+ * the given cudaStream_t (passed as void*), never synchronises the host and never allocates
+ * device memory: outputs and the fp32 workspace are owned by the caller.  (The one allocating
+ * call is the sequence split's set-up, hla_s6_peer_alloc.)  The compute entry points are safe to
+ * capture in a CUDA graph: shapes and pointers are baked in at capture, and contents such as ctx,
+ * block tables, q and the caches may change between replays.  This note does not cover
+ * hla_s6_history_attention_static, whose own comment states what it needs.
  *
  * Return value: 0 on success, HLA_S6_EINVAL for a bad shape/stride/size (Python: ValueError),
  * HLA_S6_EOVERFLOW when the workspace is too small (Python: RuntimeError, the message of
