@@ -49,7 +49,9 @@ def test_matches_reference_fixture(name, kw, splits):
 
 
 @pytest.mark.parametrize('rank,d_rope,kvh,ctx', [(512, 64, 16, [8191, 1, 4000, 16, 17, 0, 2500, 8192]),
-                                                 (256, 32, 16, [3000] * 12), (64, 32, 2, [100, 7, 1000])])
+                                                 (256, 32, 16, [3000] * 12), (64, 32, 2, [100, 7, 1000]),
+                                                 # key width 80, not a multiple of 32: 16-column slabs, 32-byte swizzle
+                                                 (64, 16, 16, [300, 0, 17, 5000, 33])])
 def test_matches_oracle(rank, d_rope, kvh, ctx):
     rng = np.random.default_rng(rank + len(ctx))
     T, H, page, Lk = len(ctx), 16, 16, rank + d_rope
