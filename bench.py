@@ -15,11 +15,14 @@ L2 (the latent caches are ~40 GB per GPU).  e2e: the same step with its per-step
 copied host->device from pinned memory and its outputs read back, inside the timed region.
 roofline: the dominant kernel (history split) timed alone in a graph of its 96 launches.
 cpu_baseline / --impl reference: the CPU oracle (numpy fp32 restatement of the reference's
-torch path) on a bounded sample of the same workload, extrapolated to a step.
+torch path) on bounded, measured samples of the same workload: one decode token of one sequence
+through all 24 layers x 4 loops per sample (config 5: one layer of 24, scaled and flagged).
 
 --config contig measures the HF engines' contiguous-layout reader (fused_history.history_attention) at
 config-2 scale; --config export the rollout cache export of one 8192-token request (24 layers);
 --config heads the per-head (LLA MLA-style) history reader at B = 64, ctx 8192.
+
+--profile CASE runs a few eager steps of one workload for profilers (see run_profile).
 
 --config 3 measures the latent writer of a prompt step instead (8 prompts x 4096 tokens, 24 layers x
 4 loops of writer GEMM + bf16 register add + committed-row RoPE and scatter, tcgen05): rows/s, with
@@ -164,51 +167,46 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- CPU oracle baseline
 class CpuSample:
-    """The oracle's per-(layer, loop) decode composition (writer GEMM, latent query, exact window, paged
-    history, B, merge) at widths 512 and 256 on ``rows_sample`` sequences of the workload (the longest:
-    an upper bound on the work per row).  Inputs are built and the path run once untimed (BLAS thread
-    start, page faults) in the constructor; ``run()`` times one pass and extrapolates it to a full step:
-    24 x (3 t_512 + t_256) x (B / rows_sample) seconds."""
+    """The oracle's decode work for ONE token of one sequence at history ``ctx``: one (layer, loop) pass
+    is the writer GEMM, latent query (absorb + RoPE), exact window + current token, paged history over
+    ``ctx - W`` latent rows, B up-projection and merge - loop 0 at width rank1, loops 1-3 at rank.
+    ``run()`` times ``layers`` x loops passes (every layer reads the same caches, each pass more bytes than
+    the host's caches hold) and returns the measured seconds.  With ``layers == shape.layers`` a pass set
+    is a whole decode token, so tokens/s needs no extrapolation; the CPU's time per token does not depend
+    on how many sequences share a step (each has its own caches)."""
 
-    def __init__(self, ctx_list, shape, rows_sample, seed=0):
+    def __init__(self, shape, ctx, layers, seed=0):
         import numpy as np
         from oracle import s6_oracle as orc
-        self.orc, self.np, self.shape = orc, np, shape
+        self.orc, self.np, self.shape, self.ctx, self.layers = orc, np, shape, int(ctx), layers
         rng = np.random.default_rng(seed)
-        self.B = len(ctx_list)
-        sample = sorted(ctx_list, reverse=True)[:rows_sample]
         H, d, page, W_ = shape.heads, shape.head_dim, shape.page, shape.window
+        c = self.ctx
         self.scale = 1 / math.sqrt(d)
         self.data = {}
-        n = len(sample)
         for width in (shape.rank, shape.rank1):
-            pages = [-(-(c + 1) // page) for c in sample]
-            lat = rng.standard_normal((sum(pages) + 1, 1, page, 2 * width), dtype=np.float32)
-            ltab = np.zeros((n, max(pages)), dtype=np.int32)
+            pages = -(-(c + 1) // page)
+            lat = rng.standard_normal((pages + 1, 1, page, 2 * width), dtype=np.float32)
+            ltab = np.arange(1, pages + 1, dtype=np.int32)[None]
+            etab = np.zeros_like(ltab)            # exact cache: only the window's pages exist
             k = 1
-            for r, p in enumerate(pages):
-                ltab[r, :p] = np.arange(k, k + p)
-                k += p
-            etab = np.zeros_like(ltab)           # exact cache: only each row's window pages exist
-            k = 1
-            for r, c in enumerate(sample):
-                for col in range(max(0, c - W_) // page, c // page + 1):
-                    etab[r, col] = k
-                    k += 1
+            for col in range(max(0, c - W_) // page, c // page + 1):
+                etab[0, col] = k
+                k += 1
             self.data[width] = dict(
                 lat=lat, ltab=ltab, etab=etab, ex=rng.standard_normal((k, H, page, 2 * d), dtype=np.float32),
-                q_pre=rng.standard_normal((n, H, d), dtype=np.float32),
-                h=rng.standard_normal((n, shape.hidden), dtype=np.float32),
+                q_pre=rng.standard_normal((1, H, d), dtype=np.float32),
+                h=rng.standard_normal((1, shape.hidden), dtype=np.float32),
                 E=rng.standard_normal((2 * width, shape.hidden), dtype=np.float32),
                 A=rng.standard_normal((H, d, width), dtype=np.float32),
                 Bm=rng.standard_normal((H, width, d), dtype=np.float32),
-                tab=np.zeros((max(sample) + 1, width), dtype=np.float32), pos=np.asarray(sample),
-                qsl=np.arange(n + 1, dtype=np.int32), seq=np.asarray(sample, dtype=np.int32) + 1,
-                ctx_lat=np.maximum(np.asarray(sample) - W_, 0), invalid=np.zeros(n, dtype=bool))
-        self.n, self.ctx_max = n, max(sample)
-        self.run()
+                tab=np.zeros((c + 1, width), dtype=np.float32), pos=np.asarray([c]),
+                qsl=np.arange(2, dtype=np.int32), seq=np.asarray([c + 1], dtype=np.int32),
+                ctx_lat=np.maximum(np.asarray([c]) - W_, 0), invalid=np.zeros(1, dtype=bool))
+        self._pass(shape.rank)                    # untimed: BLAS thread start, page faults
+        self._pass(shape.rank1)
 
-    def _one(self, width):
+    def _pass(self, width):
         D, orc, np = self.data[width], self.orc, self.np
         _ = D['h'] @ D['E'].T                                                     # writer projection
         q_lat = orc.latent_query(D['q_pre'], D['A'], D['pos'], D['tab'], dt=np.float32)  # absorb + RoPE
@@ -217,18 +215,36 @@ class CpuSample:
 
     def run(self):
         s = self.shape
-        t = {}
-        for width in (s.rank, s.rank1):
-            t0 = time.perf_counter()
-            self._one(width)
-            t[width] = time.perf_counter() - t0
-        return s.layers * ((s.loops - 1) * t[s.rank] + t[s.rank1]) * (self.B / self.n)
+        t0 = time.perf_counter()
+        for _ in range(self.layers):
+            for loop in range(s.loops):
+                self._pass(s.rank1 if loop == 0 else s.rank)
+        return time.perf_counter() - t0
 
     def describe(self):
         s = self.shape
-        return (f'oracle numpy fp32 per-(layer, loop) decode op (writer GEMM, latent query, window, paged history, '
-                f'B, merge) at widths {s.rank}/{s.rank1} on {self.n} of {self.B} sequences (ctx {self.ctx_max}), '
-                f'extrapolated x{s.layers} layers x (3+1) loops x {self.B}/{self.n}')
+        return (f'oracle numpy fp32 decode of one token at ctx {self.ctx}: {self.layers} layers x {s.loops} loops '
+                f'of (writer GEMM, latent query, window, paged history, B, merge) at widths {s.rank1}/{s.rank}')
+
+
+def cpu_decode_steps(shape, ctx_list, steps, warmup, seed, layers=None):
+    """Time ``warmup + steps`` CPU steps of the decode work; step i decodes one token of one sequence,
+    taken in a fixed stratified order over the batch's contexts (sorted, then spread) so that a few steps
+    cover the length distribution.  Returns (seconds per timed step, contexts timed, layers per step)."""
+    L = shape.layers if layers is None else layers
+    srt = sorted(int(c) for c in ctx_list)
+    n = steps + warmup
+    order = [srt[min(len(srt) - 1, (i * len(srt)) // max(n, 1) + len(srt) // (2 * max(n, 1)))] for i in range(n)]
+    samples, secs, timed = {}, [], []
+    for i, c in enumerate(order):
+        if c not in samples:
+            samples.clear()                      # one sample's caches resident at a time
+            samples[c] = CpuSample(shape, c, L, seed=seed + i)
+        t = samples[c].run()
+        if i >= warmup:
+            secs.append(t)
+            timed.append(c)
+    return secs, timed, L, samples[order[-1]]
 
 
 class PrefillCpuSample:
@@ -251,7 +267,7 @@ class PrefillCpuSample:
         for w in (s.rank, s.rank1):
             ang = self.pos[:, None] * inv[np.arange(w // 2) % inv.shape[0]][None]
             self.tab[w] = orc.bf16(np.concatenate((np.cos(ang), np.sin(ang)), -1).astype(np.float32))
-        self.run()
+        self._layer()                             # untimed: BLAS thread start, page faults
 
     def _layer(self):
         orc, s = self.orc, self.shape
@@ -262,16 +278,16 @@ class PrefillCpuSample:
             reg = orc.write_step(reg, orc.bf16(self.h[t] @ self.E[t].T))
         orc.committed_row(reg, s.rank, self.pos, self.tab[s.rank])
 
-    def run(self):
+    def pass_seconds(self):
+        """Measured seconds of one layer's writer on ``rows`` tokens (it commits ``rows`` rows)."""
         t0 = time.perf_counter()
         self._layer()
-        return (time.perf_counter() - t0) * self.shape.layers * (self.T / self.rows)
+        return time.perf_counter() - t0
 
     def describe(self):
-        s = self.shape
         return (f'oracle numpy fp32 writer of one layer (4 loops: GEMM -> bf16, bf16 register add, latent RoPE of '
-                f'the committed rows) on {self.rows} of {self.T} tokens, extrapolated x{s.layers} layers x '
-                f'{self.T}/{self.rows}')
+                f'the committed rows) on {self.rows} of a prompt step\'s {self.T} tokens; rows/s = rows committed '
+                f'per measured second')
 
 
 def cpu_threads():
@@ -294,34 +310,40 @@ def use_all_host_threads():
 
 
 def run_reference(args):
-    """--impl reference: the CPU oracle port of the reference path on this host, rank 0 only."""
+    """--impl reference: the CPU oracle port of the reference path on this host, rank 0 only.  Each step is
+    one bounded, measured sample: one decode token of one sequence through every (layer, loop) - configs
+    2 and 4 - or through one layer's 4 loops at config 5's 131072-token context (then scaled to 24 layers,
+    flagged in the line).  ms_per_step is the measured time of that sample."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     dec = importlib.import_module(f'{PKG}.decode')
     shape = dec.OuroShape()
-    use_all_host_threads()
+    cores = use_all_host_threads()
     if args.config == 3:
         return run_reference_prefill(args, shape, world)
     ctx, scaling, _, _ = config_batch(args.config, 0, 1, args.seed)
-    if scaling == 'weak':
-        ctx = ctx * world          # the whole job's requests; tokens/s of the CPU path does not depend on B
-    cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
-    samples = []
-    for i in range(args.warmup + args.steps):
-        sec = cs.run()
-        if i >= args.warmup:
-            samples.append(sec)
-    desc = cs.describe()
-    sec = statistics.mean(samples)
-    tok = len(ctx) / sec
+    if args.config == 4:
+        ctx = config_batch(4, 0, 1, args.seed)[0]
+    layers = 1 if args.config == 5 else shape.layers
+    secs, timed, L, last = cpu_decode_steps(shape, ctx, args.steps, args.warmup, args.seed, layers)
+    scale = shape.layers / L                    # 1 except at config 5
+    tok = len(secs) / (sum(secs) * scale)
+    batch = len(ctx) * (world if scaling == 'weak' else 1)
+    sample = (f'{last.describe()}; step i decodes one token of one of the batch\'s sequences (contexts timed: '
+              f'{sorted(set(timed))[:8]}{"..." if len(set(timed)) > 8 else ""})' +
+              (f'; one layer of 24 timed per step, tokens/s scaled by 24' if scale != 1 else ''))
     line = {'metric': METRIC, 'value': tok, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
-            'warmup': args.warmup, 'ms_per_step': sec * 1e3, 'higher_is_better': True, 'scaling': scaling,
-            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded)', 'impl': 'reference',
-            'config': {'workload': f'BASELINE config {args.config}: S6 decode step attention path',
-                       'global_batch': len(ctx), 'ctx': max(ctx), 'parallelism': 'host cores'},
-            'cpu_baseline': {'value': tok, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
-                             'sample': desc},
+            'warmup': args.warmup, 'ms_per_step': statistics.mean(secs) * 1e3, 'higher_is_better': True,
+            'scaling': scaling, 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded)', 'impl': 'reference',
+            'step': 'one bounded sample: one decode token of one sequence (all 24 layers x 4 loops' +
+                    (', of which one layer is timed' if scale != 1 else '') + ')',
+            'sample_ms': [round(x * 1e3, 3) for x in secs], 'extrapolated': scale != 1,
+            'extrapolation': {'layers_timed': L, 'layers': shape.layers} if scale != 1 else None,
+            'config': {'workload': f'BASELINE config {args.config}: S6 decode step attention path, one token of one '
+                                   f'sequence per step', 'global_batch': batch, 'ctx': max(ctx),
+                       'parallelism': 'host cores'},
+            'cpu_baseline': {'value': tok, 'unit': 'tokens/s', 'cores': cores, 'kind': 'port', 'sample': sample},
             'e2e': {'value': tok, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
 
@@ -335,18 +357,21 @@ def prefill_config(world):
 
 
 def run_reference_prefill(args, shape, world):
+    """Config 3's reference arm: each step is one layer's writer (4 loops) on --cpu-tokens tokens of one
+    prompt, measured; rows/s = the rows that step committed per second (no extrapolation)."""
     T = 8 * 4096
     cs = PrefillCpuSample(shape, T, args.cpu_tokens, seed=args.seed)
-    samples = []
+    secs = []
     for i in range(args.warmup + args.steps):
-        sec = cs.run()
+        sec = cs.pass_seconds()
         if i >= args.warmup:
-            samples.append(sec)
-    sec = statistics.mean(samples)
-    rows = T * shape.layers / sec          # the CPU path's throughput does not depend on the job's size
+            secs.append(sec)
+    rows = len(secs) * args.cpu_tokens / sum(secs)
     line = {'metric': METRIC3, 'value': rows, 'unit': 'rows/s', 'n_gpus': world, 'steps': args.steps,
-            'warmup': args.warmup, 'ms_per_step': sec * 1e3 * world, 'higher_is_better': True, 'scaling': 'weak',
-            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded)', 'impl': 'reference',
+            'warmup': args.warmup, 'ms_per_step': statistics.mean(secs) * 1e3, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded)', 'impl': 'reference',
+            'step': f'one bounded sample: one layer\'s writer (4 loops) on {args.cpu_tokens} prompt tokens',
+            'sample_ms': [round(x * 1e3, 3) for x in secs], 'extrapolated': False,
             'config': prefill_config(world),
             'cpu_baseline': {'value': rows, 'unit': 'rows/s', 'cores': cpu_threads(), 'kind': 'port',
                              'sample': cs.describe()},
@@ -457,12 +482,15 @@ def run_ours(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            use_all_host_threads()
-            cs = CpuSample(ctx, shape, args.cpu_rows, seed=args.seed)
-            secs = [cs.run() for _ in range(args.cpu_reps)]
-            sec, desc = statistics.median(secs), cs.describe() + f'; median of {args.cpu_reps} timed passes'
-            cpu = {'value': len(ctx) / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
-                   'sample': desc}
+            cores = use_all_host_threads()
+            layers = 1 if args.config == 5 else shape.layers
+            secs, timed, L, last = cpu_decode_steps(shape, ctx, args.cpu_reps, 1, args.seed, layers)
+            scale = shape.layers / L
+            cpu = {'value': len(secs) / (sum(secs) * scale), 'unit': 'tokens/s', 'cores': cores, 'kind': 'port',
+                   'sample': f'{last.describe()}; {len(secs)} timed tokens, one sequence each (contexts '
+                             f'{sorted(set(timed))[:6]}{"..." if len(set(timed)) > 6 else ""})' +
+                             ('; one layer of 24 timed, scaled by 24' if scale != 1 else ''),
+                   'sample_ms': [round(x * 1e3, 3) for x in secs], 'extrapolated': scale != 1}
         attn_bytes = model.latent_bytes_per_step() + model.window_bytes_per_step()
         line = {
             'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
@@ -580,12 +608,12 @@ def run_prefill(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            use_all_host_threads()
+            cores = use_all_host_threads()
             cs = PrefillCpuSample(shape, model.T, args.cpu_tokens, seed=args.seed)
-            secs = [cs.run() for _ in range(max(1, args.cpu_reps // 20))]
-            sec = statistics.median(secs)
-            cpu = {'value': model.rows_per_step() / sec, 'unit': 'rows/s', 'cores': cpu_threads(), 'kind': 'port',
-                   'sample': cs.describe() + f'; median of {len(secs)} timed passes'}
+            secs = [cs.pass_seconds() for _ in range(3)]
+            cpu = {'value': len(secs) * args.cpu_tokens / sum(secs), 'unit': 'rows/s', 'cores': cores,
+                   'kind': 'port', 'sample': cs.describe() + f'; {len(secs)} timed passes',
+                   'sample_ms': [round(x * 1e3, 3) for x in secs], 'extrapolated': False}
         line = {
             'metric': METRIC3, 'value': value, 'unit': 'rows/s', 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'weak',
@@ -726,7 +754,7 @@ def run_contig(args):
             orc.contiguous_history(qq, kk, vv, mm, scale, dt=np.float32)
         sec_row = (time.perf_counter() - t0) / 3 / rows
         sec = sec_row * B * s.layers * ((s.loops - 1) + s.rank1 / s.rank)
-        cpu = {'value': B / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
+        cpu = {'value': B / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port', 'extrapolated': True,
                'sample': f'oracle numpy fp32 contiguous reader, {rows} of {B} rows at width {s.rank} x {N} keys, '
                          f'extrapolated to 96 reads of a step (the width-256 read scaled by width)'}
     line = {'metric': METRIC_CONTIG, 'value': B / (ms / 1e3), 'unit': 'tokens/s', 'n_gpus': 1, 'steps': args.steps,
@@ -850,7 +878,7 @@ def run_heads(args):
         for _ in range(reps):
             orc.history_attention_kv(qq, kc, kc[..., :r], tab, cc, scale, dt=np.float32)
         sec = (time.perf_counter() - t0) / reps / rows * B * reads
-        cpu = {'value': B / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port',
+        cpu = {'value': B / sec, 'unit': 'tokens/s', 'cores': cpu_threads(), 'kind': 'port', 'extrapolated': True,
                'sample': f'oracle numpy fp32 per-head reader, {rows} of {B} sequences (16 heads, ctx {ctx}), '
                          f'extrapolated to the {reads} reads of a step'}
     line = {'metric': METRIC_HEADS, 'value': B / (ms / 1e3), 'unit': 'tokens/s', 'n_gpus': 1, 'steps': args.steps,
@@ -929,7 +957,7 @@ def run_export(args):
         for _ in range(3):
             orc.export_rows(mh, lh, mbh, lbh, bs, length)
         sec = (time.perf_counter() - t0) / 3 * (L / layers)
-        cpu = {'value': L * length / sec, 'unit': 'rows/s', 'cores': 1, 'kind': 'port',
+        cpu = {'value': L * length / sec, 'unit': 'rows/s', 'cores': 1, 'kind': 'port', 'extrapolated': True,
                'sample': f'oracle numpy gather (the reference exporter\'s indexing) of {layers} of {L} layers, '
                          f'host-resident caches, extrapolated'}
     line = {'metric': METRIC_EXPORT, 'value': L * length / (ms / 1e3), 'unit': 'rows/s', 'n_gpus': 1,
@@ -950,6 +978,118 @@ def run_export(args):
     return line
 
 
+# ----------------------------------------------------------------------------- profiler workloads
+def _graph_ms(torch, graph, reps):
+    """Device time per replay of a captured graph (CUDA events, after three warm-up replays)."""
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_profile(args):
+    """--profile CASE: a few eager steps of one workload, small enough for ncu (a few GB on the device).
+
+    decode     the four launches per (layer, loop) of S6DecodeModel.step in order (writer, prepare, history
+               split, combine; loop 0 reads the 256-wide latent, loops 1-3 the 512-wide one), so
+               ``ncu -k regex:history_split -s 1 -c 2`` selects one launch of each width (2 layers: ~3 GB)
+    prefill    the config-3 prompt-step writer (prefill.PrefillWriter: four writer launches per layer,
+               N = 512 at loop 0 and 1024 at loops 1-3, 4096 tokens per prompt; 1 layer x 8 prompts: ~1 GB)
+    seq-split  rank 0's share of an --split N-way sequence split (config 5: --batch 4 --ctx 131072) as a
+               one-rank job: the latent rows of the first of N page slices, the reduce with its peer-store
+               exchange (to this GPU only) and the one-part flag wait in the combine; with --time it also
+               times the step and its history launches alone as CUDA graphs
+    contig / heads / export   two calls of the other readers at the config-2 shape
+    """
+    import torch
+    dec = importlib.import_module(f'{PKG}.decode')
+    importlib.import_module(f'{PKG}._lib').load()
+    case = args.profile
+    if case in ('contig', 'heads', 'export'):
+        return _profile_reader(args, torch)
+    if case == 'seq-split':
+        import torch.distributed as dist
+        dist.init_process_group('gloo', init_method='tcp://127.0.0.1:29531', rank=0, world_size=1)
+        shape = dec.OuroShape(layers=args.layers, max_position=args.ctx + 128)
+        ctx = [args.ctx] * args.batch
+        split = dec.seq_split_rows([c - shape.window for c in ctx], shape.page, 0, args.split)
+        model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=0,
+                                  latent_rows=[n for _, n in split], exchange=(0, 1, dist.group.WORLD))
+        for _ in range(args.profile_steps):
+            model.step(overlap_writer=False)
+        torch.cuda.synchronize()
+        if args.time:
+            ms, ms_hist = _graph_ms(torch, model.capture(), 20), _graph_ms(torch, model.capture_history(), 20)
+            loops = shape.layers * shape.loops
+            print(f'1/{args.split} slice: step {ms:.3f} ms, history launches alone {ms_hist:.3f} ms, the rest '
+                  f'{(ms - ms_hist) / loops * 1e3:.1f} us per (layer, loop)')
+            model.graph = model.history_graph = None
+        model.close_exchange()
+        dist.destroy_process_group()
+        print(f'ok: {args.profile_steps} steps of a 1/{args.split} sequence-split slice, '
+              f'{model.launches_per_step()} launches each')
+        return
+    if case == 'prefill':
+        pre = importlib.import_module(f'{PKG}.prefill')
+        model = pre.PrefillWriter(dec.OuroShape(layers=args.layers), args.prompts, 4096, device='cuda', seed=0)
+        for _ in range(args.profile_steps):
+            model.step()
+        torch.cuda.synchronize()
+        print(f'ok: {args.profile_steps} prefill steps, {model.launches_per_step()} launches each')
+        return
+    model = dec.S6DecodeModel(dec.OuroShape(layers=args.layers), dec.DecodeBatch([args.ctx] * args.batch),
+                              device='cuda', seed=0)
+    for _ in range(args.profile_steps):
+        model.step(overlap_writer=False)
+    torch.cuda.synchronize()
+    print(f'ok: {args.profile_steps} steps, {model.launches_per_step()} launches each')
+
+
+def _profile_reader(args, torch):
+    B, ctx = args.batch, args.ctx
+    g = torch.Generator(device='cuda').manual_seed(0)
+    if args.profile == 'contig':
+        fh = importlib.import_module(f'{PKG}.fused_history')
+        N = ctx - 32
+        k = torch.randn(B, N, 512, generator=g, device='cuda').to(torch.bfloat16)
+        v = torch.randn(B, N, 512, generator=g, device='cuda').to(torch.bfloat16)
+        q = torch.randn(B, 16, 512, generator=g, device='cuda').to(torch.bfloat16)
+        mask = torch.ones(B, N, dtype=torch.bool, device='cuda')
+        for _ in range(2):
+            fh.history_attention(q, k, v, mask, 128 ** -0.5)
+    elif args.profile == 'heads':
+        ops = importlib.import_module(f'{PKG}.s6_ops')
+        pages = ctx // 16
+        nb = B * pages + 1
+        cache = torch.randn(nb, 16, 16, 160, generator=g, device='cuda').to(torch.bfloat16)
+        table = (torch.randperm(nb - 1, device='cuda').to(torch.int32) + 1).view(B, pages)
+        ctx_t = torch.full((B,), ctx, dtype=torch.int32, device='cuda')
+        q = torch.randn(B, 16, 160, generator=g, device='cuda').to(torch.bfloat16)
+        splits = ops.num_kv_splits(ctx, B, 512, torch.cuda.get_device_properties(0).multi_processor_count)
+        ws = ops.S6Workspace(16, 128, B * splits)
+        for _ in range(2):
+            ops.history_attention_kv(q, cache, cache[..., :128], table, ctx_t, 128 ** -0.5, splits, ws, None, None,
+                                     'b200', mla=True)
+    else:
+        ce = importlib.import_module(f'{PKG}.cache_export')
+        need = ctx // 16
+        nb = 4 * need
+        main = [torch.randn(nb, 1, 16, 1024, generator=g, device='cuda').to(torch.bfloat16) for _ in range(24)]
+        l1 = [torch.randn(nb, 1, 16, 512, generator=g, device='cuda').to(torch.bfloat16) for _ in range(24)]
+        mb = torch.randperm(nb, device='cuda')[:need].to(torch.int32)
+        lb = torch.randperm(nb, device='cuda')[:need].to(torch.int32)
+        for _ in range(2):
+            ce.export_rows(main, l1, mb, lb, ctx, 16)
+    torch.cuda.synchronize()
+    print(f'ok: 2 calls of the {args.profile} reader')
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -960,13 +1100,25 @@ def main():
     ap.add_argument('--heads-rank', type=int, default=128, help='--config heads: latent rank r of the LLA rows')
     ap.add_argument('--heads-rope', type=int, default=32, help='--config heads: RoPE tail d_rope of the LLA rows')
     ap.add_argument('--seed', type=int, default=0)
-    ap.add_argument('--cpu-rows', type=int, default=4, help='sequences timed by the CPU oracle sample')
-    ap.add_argument('--cpu-reps', type=int, default=100, help='timed passes of the CPU baseline leg')
+    ap.add_argument('--cpu-reps', type=int, default=8,
+                    help='tokens (one sequence each, every layer and loop) timed by the CPU baseline leg')
     ap.add_argument('--cpu-tokens', type=int, default=4096, help='tokens of the config-3 CPU oracle sample')
     ap.add_argument('--exchange', default='peer', choices=['peer', 'nccl'],
                     help='config 5 on several GPUs: how the (z, lse) parts move')
     ap.add_argument('--no-cpu', action='store_true', help='skip the CPU baseline leg')
+    prof = ap.add_argument_group('profiler workloads (--profile CASE; no JSON line, for ncu)')
+    prof.add_argument('--profile', choices=['decode', 'prefill', 'seq-split', 'contig', 'heads', 'export'])
+    prof.add_argument('--profile-steps', type=int, default=2, help='eager steps of the profiled workload')
+    prof.add_argument('--layers', type=int, default=2)
+    prof.add_argument('--batch', type=int, default=64)
+    prof.add_argument('--ctx', type=int, default=8192)
+    prof.add_argument('--prompts', type=int, default=8)
+    prof.add_argument('--split', type=int, default=2, help='--profile seq-split: ways of the sequence split')
+    prof.add_argument('--time', action='store_true', help='--profile seq-split: also time the step as CUDA graphs')
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
     if args.config in ('contig', 'export', 'heads'):

@@ -16,6 +16,8 @@ LIB_PATH = Path(os.environ.get('HLA_S6_LIB', _PKG / 'libhla_s6.so'))
 ABI_VERSION = 1
 
 OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
+# codes a kernel writes to its optional device error word (HLA_S6_ERR_*)
+ERR_WAIT_COPY, ERR_WAIT_STAGE, ERR_RANGE, ERR_WAIT_PEER, ERR_BLOCK = 1, 2, 3, 4, 5
 COMBINE_AFTER_PARTIALS = 1   # hla_s6_decode_combine flag (include/hla_s6.h)
 PARTIALS_AFTER_QUERY = 1     # hla_s6_history_partials flag
 REDUCE_AFTER_PARTIALS = 1    # hla_s6_history_reduce_exchange flag
@@ -65,6 +67,8 @@ SIGNATURES = {
     'hla_s6_history_reduce_exchange': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, P, _i32, _i32, P],
     'hla_s6_window_history': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _f32, _i32,
                               _i32, _i32, P, _i64, _i64, P, P],
+    'hla_s6_step_metadata': [P, _i32, P, _i32, _i32, P, P, P, P, P, P, P, P, P],
+    'hla_s6_gather_block_table': [P, _i64, _i32, _i32, P, _i32, P, _i64, P],
     'hla_s6_chunk_attention': [P, _i64, _i64, P, _i64, _i64, P, _i64, _i64, P, _i32, _i32, _i32, _i32, _f32, P, _i64,
                                _i64, P, P],
 }
@@ -89,8 +93,16 @@ def load():
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int32
+    lib.hla_s6_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+    lib.hla_s6_set_wait_limit_ns.restype = ctypes.c_uint64
     _lib = lib
     return lib
+
+
+def set_wait_limit_ns(ns: int) -> int:
+    """Limit (device ns) of the kernels' bounded waits for launches issued from now on; 0 restores the
+    2 s default.  Returns the previous limit (``hla_s6_set_wait_limit_ns``)."""
+    return int(load().hla_s6_set_wait_limit_ns(int(ns)))
 
 
 def check(rc: int, what: str):

@@ -2,7 +2,7 @@
 
 The library is a plain C-ABI shared object (include/hla_s6.h); Python binds it with ctypes.
 Incremental: sources are recompiled only when a .cu/.cuh/.h under csrc/ or include/ is newer
-than the library.  ``python build.py [--force] [--debug]``.
+than the library; the translation units compile in parallel.  ``python build.py [--force] [-v]``.
 """
 from __future__ import annotations
 
@@ -10,6 +10,7 @@ import argparse
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -32,7 +33,7 @@ def _stale(target: Path) -> bool:
     return any(p.stat().st_mtime > mtime for p in deps)
 
 
-def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Path:
+def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile csrc/*.cu into libhla_s6.so next to this file; returns its path."""
     if not force and not _stale(LIB):
         return LIB
@@ -40,21 +41,22 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Pa
     objdir.mkdir(exist_ok=True)
     flags = ARCH + ['-O3', '-lineinfo', '-std=c++17', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr',
                     '-I', str(CSRC), '-I', str(ROOT / 'include')]
-    if debug:
-        flags += ['-DHLA_DEBUG=1']
     if verbose:
         flags += ['-Xptxas', '-v']
-    objs = []
-    for src in sources():
+    def compile_one(src):
         obj = objdir / (src.stem + '.o')
-        cmd = [NVCC, *flags, '-c', str(src), '-o', str(obj)]
-        proc = subprocess.run(cmd, capture_output=True, text=True)
-        if proc.returncode != 0:
-            sys.stderr.write(proc.stdout + proc.stderr)
-            raise RuntimeError(f'nvcc failed on {src.name}')
-        if verbose:
-            sys.stderr.write(proc.stderr)
-        objs.append(str(obj))
+        proc = subprocess.run([NVCC, *flags, '-c', str(src), '-o', str(obj)], capture_output=True, text=True)
+        return src, obj, proc
+
+    objs = []
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
+        for src, obj, proc in pool.map(compile_one, sources()):
+            if proc.returncode != 0:
+                sys.stderr.write(proc.stdout + proc.stderr)
+                raise RuntimeError(f'nvcc failed on {src.name}')
+            if verbose:
+                sys.stderr.write(proc.stderr)
+            objs.append(str(obj))
     tmp = LIB.with_suffix('.so.tmp')
     cmd = [NVCC, *ARCH, '-shared', '-o', str(tmp), *objs, '-lcudart']
     proc = subprocess.run(cmd, capture_output=True, text=True)
@@ -68,7 +70,6 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Pa
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()
     ap.add_argument('--force', action='store_true')
-    ap.add_argument('--debug', action='store_true')
     ap.add_argument('-v', '--verbose', action='store_true')
     args = ap.parse_args()
-    print(build(args.force, args.debug, args.verbose))
+    print(build(args.force, args.verbose))

@@ -5,6 +5,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/hla_s6.h"
@@ -20,6 +21,10 @@ void set_error(const char* fmt, ...) {
   vsnprintf(g_error, sizeof(g_error), fmt, ap);
   va_end(ap);
 }
+
+static std::atomic<uint64_t> g_wait_ns{2000000000ull};
+
+uint64_t wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
 
 int cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return kStatusOk;
@@ -275,6 +280,11 @@ extern "C" {
 int hla_s6_version(void) { return HLA_S6_ABI_VERSION; }
 
 const char* hla_s6_last_error(void) { return g_error; }
+
+uint64_t hla_s6_set_wait_limit_ns(uint64_t ns) {
+  if (ns == 0) ns = 2000000000ull;
+  return g_wait_ns.exchange(ns, std::memory_order_relaxed);
+}
 
 int hla_s6_history_attention(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
                              int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,

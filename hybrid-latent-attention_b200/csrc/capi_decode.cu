@@ -435,6 +435,7 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
   p.part_flags = z_in ? part_flags : nullptr;
   p.part_seen = part_seen;
   p.err = error_flag;
+  p.wait_ns = wait_limit_ns();
   p.empty = empty;
   p.T = num_tokens;
   p.H = num_heads;

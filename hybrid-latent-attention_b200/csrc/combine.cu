@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
       // every rank's part of this exchange slot has landed (bounded wait); the last CTA through
       // clears the flags for the slot's next use
       if (threadIdx.x == 0) {
-        if (!wait_flags_sys(p.part_flags, p.num_parts)) record_error(p.err, kErrWaitPeer);
+        if (!wait_flags_sys(p.part_flags, p.num_parts, p.wait_ns)) record_error(p.err, kErrWaitPeer);
         const unsigned total = gridDim.x * gridDim.y * gridDim.z;
         if (atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(p.part_seen), 1u) == total - 1) {
           for (int q = 0; q < p.num_parts; ++q) p.part_flags[q] = 0;
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
   // ---- 3: o_hist[16 x 128] = z[16 x W] . B[h][W x 128]; warp w owns columns 16w .. 16w+15
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   const uint32_t zb = smem_u32(smem + S::Z_OFF);
-  if (!mbar_wait(bbar, 0)) record_error(p.err, kErrWaitFull);
+  if (!mbar_wait(bbar, 0, p.wait_ns)) record_error(p.err, kErrWaitFull);
   __syncthreads();
   for (int kc = 0; kc < NK; ++kc) {
     const uint32_t bb = smem_u32(smem + S::B_OFF + kc * kCChunkBytes);

@@ -21,6 +21,7 @@ struct CombineParams {
   int* part_flags;
   int* part_seen;
   int* err;  // optional device error word (a peer that never delivers)
+  uint64_t wait_ns;  // bound of the flag wait and of the B-load wait (device ns)
   const uint8_t* empty;  // optional [T]: rows whose latent history is empty
   int T, H;
   const __nv_bfloat16* B;  // [H, W, 128] up-projection

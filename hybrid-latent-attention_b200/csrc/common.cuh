@@ -1,19 +1,18 @@
 // Shared device helpers for the S6 sm_100a kernels: mbarriers, TMA bulk-tensor loads,
 // ldmatrix / mma.sync fragments, bf16 packing and bounded waits.
 //
-// Every wait on an mbarrier is bounded (HLA_WAIT_NS of wall time read from %globaltimer);
-// when it runs out the kernel records an error code in the caller's error word and the
-// caller's loops unwind, so a lost copy turns into a status, never into a hung GPU.
+// Every wait on an mbarrier or a peer flag is bounded by a limit in nanoseconds of device time
+// (%globaltimer) that the launch passes in its parameters (hla_s6_set_wait_limit_ns, default
+// kDefaultWaitNs); when it runs out the kernel records an error code in the caller's error word
+// and the caller's loops unwind, so a lost copy turns into a status, never into a hung GPU.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#ifndef HLA_WAIT_NS
-#define HLA_WAIT_NS 2000000000ull   // 2 s of device time before a wait gives up
-#endif
-
 namespace hla {
+
+constexpr uint64_t kDefaultWaitNs = 2000000000ull;  // 2 s of device time before a wait gives up
 
 // Error codes written to the optional device error word (first writer wins).
 enum : int {
@@ -22,6 +21,7 @@ enum : int {
   kErrWaitEmpty = 2,   // producer gave up waiting for a free stage
   kErrSlots = 3,       // a partial would land outside the workspace
   kErrWaitPeer = 4,    // gave up waiting for another GPU's part of a sequence-split exchange
+  kErrBlock = 5,       // a block-table entry outside the cache (the page reads as zeros)
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -89,22 +89,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: true when the phase completed, false when HLA_WAIT_NS elapsed first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait: true when the phase completed, false when `limit_ns` elapsed first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > HLA_WAIT_NS) return false;
+    if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
   }
 }
 
-// Bounded wait until flags[0 .. n) are all nonzero (HLA_WAIT_NS of device time in total).
-__device__ __forceinline__ bool wait_flags_sys(const int* flags, int n) {
+// Bounded wait until flags[0 .. n) are all nonzero (`limit_ns` of device time in total).
+__device__ __forceinline__ bool wait_flags_sys(const int* flags, int n, uint64_t limit_ns) {
   const uint64_t t0 = global_ns();
   for (int q = 0; q < n; ++q) {
     for (uint32_t it = 0; ld_acquire_sys(flags + q) == 0; ++it) {
-      if ((it & 63u) == 63u && global_ns() - t0 > HLA_WAIT_NS) return false;
+      if ((it & 63u) == 63u && global_ns() - t0 > limit_ns) return false;
     }
   }
   return true;

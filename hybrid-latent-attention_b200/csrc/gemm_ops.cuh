@@ -28,6 +28,7 @@ struct WriterParams {
   const int32_t* qsl;
   int R;
   int* err;  // optional device error word (bounded waits of the tcgen05 path)
+  uint64_t wait_ns;  // bound of every mbarrier wait of the tcgen05 path (device ns)
 };
 
 struct PrepareParams {

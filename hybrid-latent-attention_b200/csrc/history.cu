@@ -1,4 +1,4 @@
-// Paged latent-history reader of the S6 decode path (SURVEY A1 + A2).
+// Paged latent-history reader of the S6 decode path (split-K attention + split count / workspace).
 //
 // Reference behaviour: hla/vllm_latent/s6_ops.py:117-161 (history_attention /
 // history_attention_kv) and its torch oracle s6_ops.py:204-222 (_history_reference):
@@ -41,6 +41,8 @@ struct HistoryParams {
   int32_t grid;                // CTAs launched (stream mode)
   int32_t stream_mode;         // 1: stream-K over pages, 0: one CTA per row
   int* err;
+  uint64_t wait_ns;            // bound of every mbarrier wait (device ns)
+  int64_t num_blocks;          // cache blocks: a table entry outside [0, num_blocks) sets kErrBlock
   // contiguous layout (the HF engines' reader): every row has contig_n keys in K/V [rows, N, W]
   // (tile = PG consecutive keys of the row; two tensor maps, K and V) and a per-key mask
   int32_t contig_n;
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
         const int lp = static_cast<int>(g - base);
         const int s = it % STAGES;
         if (it >= STAGES) {
-          if (!mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) {
+          if (!mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, p.wait_ns)) {
             record_error(p.err, kErrWaitEmpty);
             atomicExch(&misc[0], 1);
             break;
@@ -200,6 +202,9 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
           tma_load_4d(stages + s * C::PAGE_BYTES + (W / 64) * C::SLAB_BYTES, &tmap_v, &full[s], 0, lp * PG, 0, r);
         } else {
           const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
+          // a page outside the table or the cache loads as zeros (TMA out-of-range fill): never a read
+          // outside the buffers, but the caller learns of it through the error word
+          if (blk < 0 || blk >= p.num_blocks) record_error(p.err, kErrBlock);
           tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk);
         }
       }
@@ -271,7 +276,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
           if (k < nk && mrow[k]) vis |= 1u << (2 * j + e);
         }
     }
-    const bool ok = mbar_wait(&full[s], (it / STAGES) & 1);
+    const bool ok = mbar_wait(&full[s], (it / STAGES) & 1, p.wait_ns);
     if (!ok) {
       record_error(p.err, kErrWaitFull);
       misc[1] = 1;
@@ -722,6 +727,8 @@ static int launch_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStrea
   p.grid = plan.grid;
   p.stream_mode = plan.stream_mode;
   p.err = a.err;
+  p.wait_ns = wait_limit_ns();
+  p.num_blocks = a.num_blocks;
   const size_t smem = history_smem_bytes<W, PG>(plan.stream_mode ? a.T : 0);
   occupancy_for<W, PG>();
   p.contig_n = 0;
@@ -835,6 +842,8 @@ static int launch_contig(const ContigArgs& c, const HistoryPlan& plan, cudaStrea
   p.grid = plan.grid;
   p.stream_mode = plan.stream_mode;
   p.err = c.err;
+  p.wait_ns = wait_limit_ns();
+  p.num_blocks = 0;
   p.contig_n = c.N;
   p.mask = c.mask;
   p.mask_st = c.m_sb;

@@ -62,6 +62,7 @@ struct HeadsParams {
   float* ws;      // [slots_cap][Lv + 1]
   int2* meta;     // [T * H] slot range of each row (stream mode)
   int* err;
+  uint64_t wait_ns;  // bound of every mbarrier wait (device ns)
 };
 
 // Stages of the per-warp ring: one page being read while the next lands.  A deeper ring holds more
@@ -287,13 +288,13 @@ __global__ void __launch_bounds__(32) history_heads_split_kernel(const __grid_co
       ++issued;
     }
     const int stage = static_cast<int>(it % S);
-    const bool landed = __all_sync(0xffffffffu, mbar_wait(&full[stage], static_cast<uint32_t>((it / S) & 1)));
+    const bool landed = __all_sync(0xffffffffu, mbar_wait(&full[stage], static_cast<uint32_t>((it / S) & 1), p.wait_ns));
     if (!landed) {
       // give up, but not before the copies already issued into this CTA's shared memory have
       // completed (bounded waits)
       if (lane == 0) record_error(p.err, kErrWaitFull);
       for (int64_t q2 = it + 1; q2 < issued; ++q2)
-        mbar_wait(&full[q2 % S], static_cast<uint32_t>((q2 / S) & 1));
+        mbar_wait(&full[q2 % S], static_cast<uint32_t>((q2 / S) & 1), p.wait_ns);
       return;
     }
     const uint32_t tb = tiles + stage * stage_bytes;
@@ -567,6 +568,7 @@ extern "C" int hla_s6_history_attention_heads(const void* q, int64_t q_stride_t,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.ws = workspace;
   p.err = error_flag;
+  p.wait_ns = wait_limit_ns();
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define HLA_HEADS(VT)                                                                               \
   rc = mode == 64 ? launch_heads<VT, 64>(tmap, p, workspace_floats, s) : launch_heads<VT, 32>(tmap, p, workspace_floats, s)

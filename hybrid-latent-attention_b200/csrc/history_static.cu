@@ -24,27 +24,60 @@ constexpr int64_t kStaticScratchFloats = int64_t(2) << 20;  // 2 Mi floats = 8 M
 
 static __device__ __align__(256) float g_history_scratch[kStaticScratchFloats];
 
-// Device address of g_history_scratch for the current device.  In host code the symbol's name is a
-// host-side stand-in, not a device address, so it is resolved once per device with
-// cudaGetSymbolAddress (with that device current) and cached.
+// Device address of g_history_scratch in the current context.  In host code the symbol's name is a
+// host-side stand-in, not a device address, so it is resolved with cudaGetSymbolAddress while that
+// context is current, once per context, and kept.  The key is the CUDA context, not the device
+// ordinal: after cudaDeviceReset, or with another context current on the same device, the array lives
+// at another address and is looked up again.  The look-up may load this library's device code into
+// the context, so the first call in each context must come before any stream capture.
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+static CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrent>(p);
+  });
+  return fn;
+}
+
 static int static_scratch(float** out) {
+  constexpr int kSlots = 64;
   static std::mutex mu;
-  static float* addr[64] = {nullptr};
+  static CUcontext ctxs[kSlots] = {nullptr};
+  static float* addrs[kSlots] = {nullptr};
+  static int used = 0, next = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "history_attention_static: cudaGetDevice");
-  if (dev < 0 || dev >= 64) {
-    set_error("history_attention_static: device ordinal %d out of range", dev);
-    return kStatusInvalid;
+  CtxGetCurrent get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get && get(&ctx) == CUDA_SUCCESS && !ctx) {
+    // no context is current yet (the runtime makes the primary one current lazily): make it so now
+    if ((e = cudaSetDevice(dev)) != cudaSuccess) return cuda_status(e, "history_attention_static: cudaSetDevice");
+    get(&ctx);
+  }
+  if (!get || !ctx) {
+    set_error("history_attention_static: no current CUDA context");
+    return kStatusCuda;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_history_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "history_attention_static: cudaGetSymbolAddress");
-    addr[dev] = static_cast<float*>(p);
-  }
-  *out = addr[dev];
+  for (int i = 0; i < used; ++i)
+    if (ctxs[i] == ctx) {
+      *out = addrs[i];
+      return kStatusOk;
+    }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_history_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "history_attention_static: cudaGetSymbolAddress");
+  const int slot = used < kSlots ? used++ : (next++ % kSlots);
+  ctxs[slot] = ctx;
+  addrs[slot] = static_cast<float*>(p);
+  *out = addrs[slot];
   return kStatusOk;
 }
 

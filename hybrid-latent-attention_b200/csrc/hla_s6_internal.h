@@ -19,6 +19,9 @@ enum Status : int {
 constexpr int kHistoryMaxStreamRows = 1024;
 
 void set_error(const char* fmt, ...);
+// Bound (device ns) that launches give their kernels' mbarrier and peer-flag waits
+// (hla_s6_set_wait_limit_ns; kDefaultWaitNs until set).
+uint64_t wait_limit_ns();
 
 // Raise `func`'s dynamic shared-memory limit to `bytes`, once per device (bit `dev` of `mask`).
 template <typename F>

@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_tile_rows(p, j, n_lo, n_hi);
         for (int kb = 0; kb < NK; ++kb, ++g) {
           const int s = g % kTcStages;
-          if (g >= kTcStages && !mbar_wait(&empty[s], ((g / kTcStages) - 1) & 1)) {
+          if (g >= kTcStages && !mbar_wait(&empty[s], ((g / kTcStages) - 1) & 1, p.wait_ns)) {
             record_error(p.err, kErrWaitEmpty);
             ok = false;
             break;
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
         const int b = it & 1;
-        if (it >= 2 && !mbar_wait(&tempty[b], ((it >> 1) - 1) & 1)) {
+        if (it >= 2 && !mbar_wait(&tempty[b], ((it >> 1) - 1) & 1, p.wait_ns)) {
           record_error(p.err, kErrWaitEmpty);
           break;
         }
@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t d = tmem + b * kTcN;
         for (int kb = 0; kb < NK; ++kb, ++g) {
           const int s = g % kTcStages;
-          if (!mbar_wait(&full[s], (g / kTcStages) & 1)) {
+          if (!mbar_wait(&full[s], (g / kTcStages) & 1, p.wait_ns)) {
             record_error(p.err, kErrWaitFull);
             ok = false;
             break;
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       // nothing may still write TMEM when it is released
       tc_commit(drained);
-      if (!mbar_wait(drained, 0)) record_error(p.err, kErrWaitFull);
+      if (!mbar_wait(drained, 0, p.wait_ns)) record_error(p.err, kErrWaitFull);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2-5)
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in);
       // tcgen05.ld / wait::ld are warp-collective (.sync.aligned): the wait result is made warp-uniform
       // and every lane runs the loads; rows past T only skip their global accesses
-      const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1));
+      const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1, p.wait_ns));
       tc_fence_after();
       if (!done) {
         record_error(p.err, kErrWaitFull);
@@ -428,12 +428,12 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 // Bounded wait with cluster-scope acquire (arrivals come from the peer CTA too).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > HLA_WAIT_NS) return false;
+    if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
   }
 }
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t bar_cluster, int c0, int c1) {
@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int n_mine = leader ? n_lo : n_hi;
         for (int kb = 0; kb < NK; ++kb, ++g) {
           const int s = g % kT2Stages;
-          if (g >= kT2Stages && !mbar_wait(&empty[s], ((g / kT2Stages) - 1) & 1)) {
+          if (g >= kT2Stages && !mbar_wait(&empty[s], ((g / kT2Stages) - 1) & 1, p.wait_ns)) {
             record_error(p.err, kErrWaitEmpty);
             ok = false;
             break;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int it = 0;
       for (int tile = first; tile < num_tiles && ok; tile += stride, ++it) {
         const int b = it & 1;
-        if (it >= 2 && !mbar_wait_cluster(&tempty[b], ((it >> 1) - 1) & 1)) {
+        if (it >= 2 && !mbar_wait_cluster(&tempty[b], ((it >> 1) - 1) & 1, p.wait_ns)) {
           record_error(p.err, kErrWaitEmpty);
           break;
         }
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t d = tmem + b * kTcN;
         for (int kb = 0; kb < NK; ++kb, ++g) {
           const int s = g % kT2Stages;
-          if (!mbar_wait(&full[s], (g / kT2Stages) & 1)) {
+          if (!mbar_wait(&full[s], (g / kT2Stages) & 1, p.wait_ns)) {
             record_error(p.err, kErrWaitFull);
             ok = false;
             break;
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc2_commit_both(&tfull[b]);
       }
       tc2_commit_both(drained);  // the peer's copy is not waited on
-      if (!mbar_wait(drained, 0)) record_error(p.err, kErrWaitFull);
+      if (!mbar_wait(drained, 0, p.wait_ns)) record_error(p.err, kErrWaitFull);
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2-5, both CTAs)
@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool pair_tile = p.commit && j < p.w / 256;
       TileIn in;
       tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in);
-      const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1));
+      const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1, p.wait_ns));
       tc_fence_after();
       if (!done) {
         record_error(p.err, kErrWaitFull);
@@ -651,6 +651,7 @@ int writer_tc(const WriterParams& p, cudaStream_t s) {
   const int nsm = cached && sms[dev] > 0 ? sms[dev] : 148;
   TcParams tp;
   tp.w = p;
+  tp.w.wait_ns = wait_limit_ns();
   tp.n_tiles = p.N / kTcN;
   if (p.T >= 2 * kTcM) {
     static unsigned attr2 = 0;

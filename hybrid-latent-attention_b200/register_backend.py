@@ -7,15 +7,21 @@ the reference's ops module (``hla/vllm_latent/s6_ops.py``) at run time, without 
     ctx = s6_layer.StepContext(..., s6_ops.select_backends(), ...)     # Backends('b200', 'b200', 'b200', 'b200')
     out = s6_layer.attend(...)                                         # the reference's attend, B200 kernels
 
-What changes in the module (the backend dispatch points of s6_ops.py:23, :128, :234, :262, :317, :334,
+What changes in the module (the backend dispatch points of s6_ops.py:23, :44, :128, :234, :262, :317, :334,
 :364):
 
 * ``history_attention_kv``, ``chunk_attention``, ``merge_states`` and ``latent_rope`` gain a ``'b200'`` branch in
-  front of the reference's dispatch; every other backend string reaches the original function unchanged.
-  ``history_attention`` needs no wrapper: the reference implements it through the module's
+  front of the reference's dispatch; for these four, every other backend string reaches the original function
+  unchanged.  ``history_attention`` needs no wrapper: the reference implements it through the module's
   ``history_attention_kv``.
 * ``window_attention_fa`` / ``window_history_fa`` (the exact window of the decode and prefill branches of
-  ``s6_layer.attend``) take no backend argument; with ``window=True`` they are replaced by the B200 kernels.
+  ``s6_layer.attend``) take no backend argument, so they cannot dispatch: with ``window=True`` (the default)
+  they are REPLACED by the B200 kernels for every caller, whatever backends its ``StepContext`` holds - a
+  ``'torch'`` or FA2 set-up then runs the B200 window too (and, on CPU tensors, gets this package's
+  ``ValueError``).  Pass ``window=False`` to keep the reference's FA2 window ops.
+* ``probe_latent_rope`` (no backend argument either; the adapter calls it once at start-up, right after
+  ``select_backends``) is replaced by this package's probe of the B200 latent-RoPE kernel, whose answer is
+  ``(flat=False, exact)``.
 * ``select_backends`` returns the module's own ``Backends`` namedtuple filled with ``'b200'``.
 
 ``unregister`` restores the originals.  The B200 functions keep the reference's signatures, layouts and
@@ -68,6 +74,8 @@ def register(s6_ops, window=True):
         for name in _WINDOW_OPS:
             originals[name] = getattr(s6_ops, name)
             setattr(s6_ops, name, functools.wraps(originals[name])(getattr(mine, name)))
+    originals['probe_latent_rope'] = s6_ops.probe_latent_rope
+    s6_ops.probe_latent_rope = functools.wraps(originals['probe_latent_rope'])(mine.probe_latent_rope)
     originals['select_backends'] = s6_ops.select_backends
 
     @functools.wraps(originals['select_backends'])

@@ -51,6 +51,10 @@ def latent_query(q_pre_rope, A, positions, table, backend, flat=False):
 class StepContext:
     """Per-step tensors shared by every layer and loop (reference s6_layer.py:43-84).
 
+    The integer fields (``token_requests``, ``valid``, ``invalid``, ``ctx``, ``ctx_latent``, ``empty``,
+    ``empty_latent``) come from one metadata kernel and the per-token block tables from one gather each,
+    bit-exact with the reference's torch ops; ``ctx`` / ``ctx_latent`` are int32, the masks bool.
+
     ``query_start_loc=None`` means a metadata-less (profiling) step: one request spanning all tokens,
     no history and no cache writes.  ``tables`` maps a latent width to its ``[max_position, w]`` RoPE
     table.  All shapes depend only on ``num_tokens`` and CPU ints; nothing here syncs with the host.
@@ -68,24 +72,18 @@ class StepContext:
             query_start_loc = torch.tensor([0, num_tokens], dtype=torch.int32, device=device)
             seq_lens, max_query_len = query_start_loc[1:], num_tokens
         self.query_start_loc, self.seq_lens, self.max_query_len = query_start_loc, seq_lens, max_query_len
-        self.token_requests, self.valid = s6_ops.token_requests(query_start_loc, num_tokens)
-        history = s6_ops.history_lengths(seq_lens, query_start_loc)
-        self.ctx = torch.where(self.valid, history[self.token_requests], 0)
-        self.invalid, self.empty = ~self.valid, self.ctx == 0
-        self.ctx_latent = (self.ctx - window).clamp_(min=0) if window else self.ctx
-        self.empty_latent = self.ctx_latent == 0
-        if self.ctx.dtype != torch.int32:
-            self.ctx = self.ctx.int()
-            self.ctx_latent = self.ctx_latent.int()
+        # every integer field in one launch, bit-exact with the reference's torch chain
+        (self.token_requests, self.valid, self.invalid, self.ctx, self.ctx_latent, self.empty,
+         self.empty_latent) = s6_ops.step_metadata(query_start_loc, seq_lens, num_tokens, window)
         self._block_tables = {}
         if workspace is not None:
             workspace.ensure(device)
 
     def block_table(self, table):
-        """Per-token gather of a per-request block table, once per distinct tensor per step."""
+        """Per-token gather of a per-request block table, once per distinct tensor per step (one launch)."""
         key = table.data_ptr()
         if key not in self._block_tables:
-            self._block_tables[key] = table[self.token_requests]
+            self._block_tables[key] = s6_ops.gather_block_table(table, self.token_requests)
         return self._block_tables[key]
 
     def latent_query(self, sl, loop, q_pre_rope):

@@ -38,19 +38,67 @@ def _check_cuda(*tensors):
 
 
 # ----------------------------------------------------------------------------- step metadata
+def _int32(x):
+    return x if x.dtype == torch.int32 else x.int()
+
+
 def token_requests(query_start_loc, num_tokens):
     """Request index per token (long, clamped into range) and ``valid = arange(T) < query_start_loc[-1]``.
 
-    Same contract as reference s6_ops.py:61-68; sync-free.  Padding tokens are ``~valid``.
+    Same contract as reference s6_ops.py:61-68; one sync-free launch (``hla_s6_step_metadata``).
+    Padding tokens are ``~valid``.
     """
-    idx = torch.arange(num_tokens, dtype=query_start_loc.dtype, device=query_start_loc.device)
-    req = torch.searchsorted(query_start_loc[1:], idx, right=True).clamp_(max=query_start_loc.shape[0] - 2)
-    return req.long(), idx < query_start_loc[-1]
+    _check_cuda(query_start_loc)
+    qsl = _int32(query_start_loc).contiguous()
+    device = qsl.device
+    req = torch.empty(num_tokens, dtype=torch.int64, device=device)
+    valid = torch.empty(num_tokens, dtype=torch.bool, device=device)
+    _lib.call('hla_s6_step_metadata', _lib.ptr(qsl), qsl.shape[0] - 1, None, num_tokens, 0, _lib.ptr(req),
+              _lib.ptr(valid), None, None, None, None, None, None, _lib.stream_of(qsl))
+    return req, valid
 
 
 def history_lengths(seq_lens, query_start_loc):
-    """Per-request history length ``seq_len - query_len``, clamped at 0 (reference s6_ops.py:71-73)."""
-    return (seq_lens - (query_start_loc[1:] - query_start_loc[:-1])).clamp_(min=0)
+    """Per-request history length ``seq_len - query_len``, clamped at 0 (reference s6_ops.py:71-73); one
+    launch.  The result has ``seq_lens``' dtype, as the reference's torch arithmetic gives."""
+    _check_cuda(seq_lens, query_start_loc)
+    qsl = _int32(query_start_loc).contiguous()
+    sl = _int32(seq_lens).contiguous()
+    hist = torch.empty(sl.shape[0], dtype=torch.int32, device=sl.device)
+    _lib.call('hla_s6_step_metadata', _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(sl), 0, 0, None, None, None,
+              _lib.ptr(hist), None, None, None, None, _lib.stream_of(sl))
+    return hist if seq_lens.dtype == torch.int32 else hist.to(seq_lens.dtype)
+
+
+def step_metadata(query_start_loc, seq_lens, num_tokens, window=0):
+    """Every integer field of ``StepContext`` in one launch: ``(token_requests int64, valid, invalid,
+    ctx int32, ctx_latent int32, empty, empty_latent)`` (the masks bool), as s6_layer.py:52-70 derives
+    them with torch ops (bit-exact)."""
+    _check_cuda(query_start_loc, seq_lens)
+    qsl = _int32(query_start_loc).contiguous()
+    sl = _int32(seq_lens).contiguous()
+    device = qsl.device
+    req = torch.empty(num_tokens, dtype=torch.int64, device=device)
+    masks = torch.empty(4, num_tokens, dtype=torch.bool, device=device)
+    ints = torch.empty(2, num_tokens, dtype=torch.int32, device=device)
+    valid, invalid, empty, empty_latent = masks.unbind(0)
+    ctx, ctx_latent = ints.unbind(0)
+    _lib.call('hla_s6_step_metadata', _lib.ptr(qsl), qsl.shape[0] - 1, _lib.ptr(sl), num_tokens, int(window),
+              _lib.ptr(req), _lib.ptr(valid), _lib.ptr(invalid), None, _lib.ptr(ctx), _lib.ptr(ctx_latent),
+              _lib.ptr(empty), _lib.ptr(empty_latent), _lib.stream_of(qsl))
+    return req, valid, invalid, ctx, ctx_latent, empty, empty_latent
+
+
+def gather_block_table(table, token_requests):
+    """``table[token_requests]`` for a per-request int32 block table (one launch)."""
+    _check_cuda(table, token_requests)
+    if table.dtype != torch.int32 or table.dim() != 2 or table.stride(-1) != 1:
+        raise ValueError('block table must be int32 [num_reqs, max_blocks] with a unit last-dim stride')
+    T = token_requests.shape[0]
+    out = torch.empty(T, table.shape[1], dtype=torch.int32, device=table.device)
+    _lib.call('hla_s6_gather_block_table', _lib.ptr(table), table.stride(0), table.shape[1], table.shape[0],
+              _lib.ptr(token_requests), T, _lib.ptr(out), out.stride(0), _lib.stream_of(table))
+    return out
 
 
 def num_kv_splits(max_seq_len, num_tokens, split_max_tokens, sm_count, head_blocks=1):
@@ -328,6 +376,29 @@ def latent_rope(x, positions, table, backend):
     _lib.call('hla_s6_latent_rope', _lib.ptr(x), st, sh, T, H, w, _lib.ptr(pos), _lib.ptr(table), table.stride(0),
               table.shape[0], _lib.stream_of(x))
     return x
+
+
+def probe_latent_rope(table, heads=2, tokens=3):
+    """[RUNTIME CHECK] the B200 latent-RoPE kernel against the torch formula on an einsum-shaped ``[T,H,w]``
+    input (head stride ``T*w``), as the reference probes its vLLM rotary kernel at model start-up
+    (s6_ops.py:44-58, called at ouro_latent.py:203).
+
+    Returns ``(flat, exact)``: ``flat`` is always False here - the kernel honours any head stride, so callers
+    never need a contiguous ``[T, H*w]`` copy - and ``exact`` is bit-equality with the torch formula
+    ``x*cos + rotate_half(x)*sin`` in the bf16 operation order of ``LatentLayer.pack`` (register.py:73-79).
+    Raises ``RuntimeError`` when the kernel disagrees with the formula beyond bf16 rounding."""
+    _check_cuda(table)
+    w = table.shape[1]
+    gen = torch.Generator(device=table.device).manual_seed(0)   # own generator: the model's RNG stays untouched
+    x = torch.randn(heads, tokens, w, dtype=table.dtype, device=table.device, generator=gen).transpose(0, 1)
+    pos = torch.randint(0, table.shape[0], (tokens,), device=table.device, generator=gen)
+    cos, sin = (t.repeat(1, 1, 2) for t in table[pos].view(-1, 1, 2, w // 2).unbind(2))
+    half = w // 2
+    ref = (x * cos + torch.cat((-x[..., half:], x[..., :half]), -1) * sin).float()
+    out = latent_rope(x.clone(), pos, table, BACKEND).float()
+    if not torch.allclose(out, ref, atol=1e-2, rtol=1e-2):
+        raise RuntimeError('b200 latent_rope disagrees with the latent RoPE reference')
+    return False, bool(torch.equal(out, ref))
 
 
 def select_backends(head_size=128):

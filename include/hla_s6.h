@@ -14,8 +14,14 @@
  * message of the calling thread's last failure.
  *
  * Data-dependent conditions are never errors: a row with no history gives o = 0 and
- * lse = -inf.  error_flag (optional, device int, may be NULL) receives a non-zero code if a
- * kernel's bounded wait ran out; the kernel then returns instead of hanging.
+ * lse = -inf.  error_flag (optional, device int, may be NULL; the first code written stays)
+ * receives a non-zero code when a kernel met a condition it could not honour, and the kernel
+ * returns normally instead of hanging or reading outside its buffers:
+ *   1, 2  a bounded wait for a shared-memory copy ran out (HLA_S6_ERR_WAIT_COPY, _WAIT_STAGE);
+ *   3     a partial or a block id fell outside the workspace or the cache (HLA_S6_ERR_RANGE);
+ *   4     a sequence-split part from another GPU did not arrive in time (HLA_S6_ERR_WAIT_PEER);
+ *   5     a history block-table entry outside [0, num_blocks): that page reads as zeros
+ *         (HLA_S6_ERR_BLOCK; the reference's torch indexing raises IndexError there).
  *
  * Layouts (bf16 = __nv_bfloat16, unit last-dim stride everywhere):
  *   q_lat  [T, H, W]                latent query (absorbed and latent-RoPE'd)
@@ -40,8 +46,22 @@ extern "C" {
 #define HLA_S6_EOVERFLOW 2
 #define HLA_S6_ECUDA 3
 
+#define HLA_S6_ERR_WAIT_COPY 1
+#define HLA_S6_ERR_WAIT_STAGE 2
+#define HLA_S6_ERR_RANGE 3
+#define HLA_S6_ERR_WAIT_PEER 4
+#define HLA_S6_ERR_BLOCK 5
+
 int hla_s6_version(void);
 const char* hla_s6_last_error(void);
+
+/* Limit, in nanoseconds of device time, of every bounded wait in the kernels launched after this
+ * call (mbarrier phases of the TMA rings, the sequence-split combine's wait for the other GPUs'
+ * parts): when it runs out the kernel writes its error code to error_flag and returns.
+ * Process-wide; 0 restores the default of 2 s.  A CUDA graph keeps the limit its launches were
+ * captured with.  Returns the previous limit.  No counterpart in the reference (its Triton and
+ * FA2 kernels never wait on another agent). */
+uint64_t hla_s6_set_wait_limit_ns(uint64_t ns);
 
 /* Fully visible attention of q_lat over the first ctx[t] paged latent rows (split-K + reduce).
  * Replaces hla/vllm_latent/s6_ops.py:117 history_attention (-> history_attention_kv :128,
@@ -62,9 +82,10 @@ int hla_s6_history_attention(const void* q_lat, int64_t q_stride_t, int64_t q_st
  * reserved up front): same arguments and results, minus the workspace, which is taken from a
  * fixed 8 MiB device array inside the library instead.  No counterpart in the reference.
  * Limit: T * num_kv_splits * H * (W + 1) <= 2 * 1024 * 1024 floats, else HLA_S6_EOVERFLOW.
- * The first call on each device looks up that array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture.  All calls share the array: calls whose
- * kernels overlap on the GPU race on it.  It allocates nothing. */
+ * The first call in each CUDA context (per device, and again after cudaDeviceReset) looks up that
+ * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the array: calls whose kernels overlap on the GPU race on it.  It allocates
+ * nothing. */
 int hla_s6_history_attention_static(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
                                     int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,
                                     const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
@@ -142,6 +163,30 @@ int hla_s6_history_attention_heads(const void* q, int64_t q_stride_t, int64_t q_
  * it exposes the split choice the reference makes in s6_ops.py:76-89 (num_kv_splits). */
 int hla_s6_history_plan(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page, int32_t num_kv_splits,
                         int64_t workspace_floats, int32_t* stream_mode, int32_t* grid, int32_t* slots);
+
+/* Integer step metadata of a varlen batch, one launch (the integer fields of s6_layer.StepContext,
+ * hla/vllm_latent/s6_layer.py:52-70, with s6_ops.token_requests :61-68 and history_lengths :71-73):
+ *   token_requests[t] = #{i in 1..R : query_start_loc[i] <= t}, clamped to R - 1   (int64 [T])
+ *   valid[t] = t < query_start_loc[R]; invalid[t] = !valid[t]                     (uint8 0/1 [T])
+ *   history[r] = max(seq_lens[r] - (query_start_loc[r + 1] - query_start_loc[r]), 0) (int32 [R])
+ *   ctx[t] = valid[t] ? history[token_requests[t]] : 0                            (int32 [T])
+ *   ctx_latent[t] = window ? max(ctx[t] - window, 0) : ctx[t]                      (int32 [T])
+ *   empty[t] = ctx[t] == 0; empty_latent[t] = ctx_latent[t] == 0                   (uint8 0/1 [T])
+ * R = num_reqs >= 1 and query_start_loc non-decreasing (vLLM pads requests by repeating its last
+ * entry).  Every output is optional (NULL skips it); seq_lens may be NULL only when history, ctx,
+ * ctx_latent, empty and empty_latent all are.  Bit-exact with the reference's torch ops. */
+int hla_s6_step_metadata(const int32_t* query_start_loc, int32_t num_reqs, const int32_t* seq_lens,
+                         int32_t num_tokens, int32_t window, int64_t* token_requests, uint8_t* valid,
+                         uint8_t* invalid, int32_t* history, int32_t* ctx, int32_t* ctx_latent, uint8_t* empty,
+                         uint8_t* empty_latent, void* stream);
+
+/* Per-token gather of a per-request block table: out[t, 0 .. max_blocks) = table[token_requests[t],
+ * 0 .. max_blocks) (int32, row strides in elements); a request index outside [0, num_reqs) gives a
+ * row of zeros.  Replaces s6_layer.StepContext.block_table (hla/vllm_latent/s6_layer.py:72-77,
+ * table[token_requests]). */
+int hla_s6_gather_block_table(const int32_t* table, int64_t table_stride, int32_t max_blocks, int32_t num_reqs,
+                              const int64_t* token_requests, int32_t num_tokens, int32_t* out, int64_t out_stride,
+                              void* stream);
 
 /* Exact window attention of the roped q over keys [pos - window, pos] of a paged exact cache
  * (the current token already written; pos = seq_len - query_len + index, i.e. seq_len - 1 in

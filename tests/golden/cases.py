@@ -221,6 +221,31 @@ def meta_cases():
     )
 
 
+def step_context_cases():
+    """vLLM-style step metadata for s6_layer.StepContext (s6_layer.py:52-77): (query_start_loc,
+    seq_lens, num_tokens, window, block_table [R, max_blocks]).  Decode batches (one token per request,
+    contexts below, at and above the window), padded tokens without and with padded requests (the
+    repeated last query_start_loc entry), prefill and mixed prefill/decode chunks, window 0, and a
+    64-request decode step at context 8192 (BASELINE config 2's metadata)."""
+    rng = np.random.default_rng(88)
+    out = []
+
+    def add(qsl, seq_lens, T, window, max_blocks=6):
+        R = len(qsl) - 1
+        table = rng.integers(0, 1000, (R, max_blocks)).astype(np.int32)
+        out.append((list(qsl), list(seq_lens), T, window, table.tolist()))
+
+    add([0, 1, 2, 3, 4], [5, 40, 33, 1], 4, 32)
+    add([0, 1, 2, 3, 3, 3], [100, 2, 1, 0, 0], 6, 32)
+    add([0, 1, 2], [9, 70], 5, 32)
+    add([0, 3, 4, 6], [3, 10, 50], 8, 32)
+    add([0, 3, 4, 6], [3, 10, 50], 8, 0)
+    add([0, 2, 3, 3, 3], [4, 7, 0, 0], 5, 16)
+    add([0, 5], [5], 5, 32)
+    add(list(range(65)), [8193] * 64, 64, 32, max_blocks=513)
+    return out
+
+
 def _neox_rope(x, positions, base=10000.0):
     """Rotate-half RoPE over the last dim (head_dim 128) at integer positions, float64."""
     d = x.shape[-1]

@@ -11,6 +11,7 @@ reference modules import without vLLM or a GPU (their GPU imports are lazy, s6_o
 from __future__ import annotations
 
 import argparse
+import os
 import importlib
 import inspect
 import json
@@ -23,7 +24,7 @@ MIRRORED = {
     's6_ops': ('hla.vllm_latent.s6_ops',
                ['latent_rope', 'token_requests', 'history_lengths', 'num_kv_splits', 'S6Workspace',
                 'history_attention', 'history_attention_kv', 'chunk_attention', 'merge_states', 'window_attention_fa',
-                'window_history_fa', 'merge_lse', 'select_backends']),
+                'window_history_fa', 'merge_lse', 'select_backends', 'probe_latent_rope']),
     's6_layer': ('hla.vllm_latent.s6_layer',
                  ['latent_inv_freq', 'latent_rope_table', 'latent_query', 'StepContext', 'attend', 'write_rows',
                   'committed_row']),
@@ -67,8 +68,11 @@ def describe(obj):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', default='/root/reference')
+    ap.add_argument('--reference', default=os.environ.get('HLA_REFERENCE_ROOT'),
+                    help='checkout of the reference project (default: $HLA_REFERENCE_ROOT)')
     args = ap.parse_args()
+    if not args.reference:
+        ap.error('pass --reference or set HLA_REFERENCE_ROOT to a checkout of the reference project')
     sys.path.insert(0, args.reference)
     table = {}
     for mine, (ref_name, names) in MIRRORED.items():

@@ -1,7 +1,8 @@
 """Generate the golden fixtures by running the REFERENCE's own torch code on the inputs of cases.py.
 
 Usage (needs the reference checkout, read-only):
-    python tests/golden/gen_golden.py --reference /path/to/hybrid-latent-attention
+    python tests/golden/gen_golden.py --reference /path/to/hybrid-latent-attention [--only step_context]
+    (or set HLA_REFERENCE_ROOT instead of passing --reference)
 
 Writes tests/golden/<name>.npz with the reference outputs and a sha256 of the inputs.
 The reference functions called (file:line in the reference project):
@@ -9,6 +10,7 @@ The reference functions called (file:line in the reference project):
   hla/vllm_latent/s6_ops.py:290 window_attention, :234 chunk_attention('torch'), :353 merge_lse
   hla/vllm_latent/s6_ops.py:262 merge_states('torch'), :23 latent_rope('torch'), :61 token_requests,
   :71 history_lengths, :76 num_kv_splits
+  hla/vllm_latent/s6_layer.py:43 StepContext (the integer fields and block_table; step_context.json)
   hla/vllm_latent/s6_layer.py:16 latent_inv_freq, :21 latent_rope_table, :32 latent_query,
   :124 write_rows, :135 committed_row
   hla/latent/register.py:28 LatentLayer (write_step / write1 / pack / fields)
@@ -24,6 +26,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
 import sys
 from pathlib import Path
 
@@ -34,16 +37,39 @@ sys.path.insert(0, str(HERE))
 import cases  # noqa: E402
 
 
+def step_context_fixture(s6_layer, s6_ops, torch):
+    """Integer fields of the reference's StepContext (s6_layer.py:52-77) on cases.step_context_cases()."""
+    rows = []
+    for qsl, seq_lens, T, window, table in cases.step_context_cases():
+        ctx = s6_layer.StepContext(torch.zeros(T, dtype=torch.long), torch.tensor(qsl, dtype=torch.int32),
+                                   torch.tensor(seq_lens, dtype=torch.int32), 1, T, {}, 1.0,
+                                   s6_ops.TORCH_BACKENDS, window=window)
+        rows.append(dict(token_requests=ctx.token_requests.tolist(), valid=ctx.valid.tolist(),
+                         invalid=ctx.invalid.tolist(), ctx=ctx.ctx.tolist(), ctx_latent=ctx.ctx_latent.tolist(),
+                         empty=ctx.empty.tolist(), empty_latent=ctx.empty_latent.tolist(),
+                         ctx_dtype=str(ctx.ctx.dtype), ctx_latent_dtype=str(ctx.ctx_latent.dtype),
+                         block_table=ctx.block_table(torch.tensor(table, dtype=torch.int32)).tolist()))
+    (HERE / 'step_context.json').write_text(json.dumps(rows))
+    print('wrote step_context.json', len(rows))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', default='/root/reference')
+    ap.add_argument('--reference', default=os.environ.get('HLA_REFERENCE_ROOT'),
+                    help='checkout of the reference project (default: $HLA_REFERENCE_ROOT)')
+    ap.add_argument('--only', choices=['step_context'], help='write only this fixture')
     args = ap.parse_args()
+    if not args.reference:
+        ap.error('pass --reference or set HLA_REFERENCE_ROOT to a checkout of the reference project')
     sys.path.insert(0, args.reference)
     import torch
     from hla.latent.register import LatentLayer
     from hla.vllm_latent import s6_layer, s6_ops
     torch.set_num_threads(4)
     T_ = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    step_context_fixture(s6_layer, s6_ops, torch)
+    if args.only:
+        return
 
     def save(name, inputs, **outputs):
         np.savez_compressed(HERE / f'{name}.npz', input_sha256=np.array(cases.digest(inputs)), **outputs)

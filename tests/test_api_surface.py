@@ -68,5 +68,5 @@ def test_reference_signature_fixture_covers_the_mirrored_modules():
     assert {m: TABLE[m]['reference'] for m in TABLE} == {
         's6_ops': 'hla.vllm_latent.s6_ops', 's6_layer': 'hla.vllm_latent.s6_layer',
         'fused_history': 'hla.latent.fused_history'}
-    assert len(CASES) == 21
+    assert len(CASES) == 22
     assert inspect.isfunction(signature_text)

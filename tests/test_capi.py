@@ -19,7 +19,7 @@ def lib():
 
 def declared():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r'^\s*(?:int|const char\*|void)\s+(hla_s6_\w+)\s*\(', text, re.M)))
+    return sorted(set(re.findall(r'^\s*(?:int|const char\*|void|uint64_t)\s+(hla_s6_\w+)\s*\(', text, re.M)))
 
 
 def test_header_declares_the_boundary():
@@ -51,6 +51,17 @@ def test_invalid_arguments_return_einval_with_message(lib):
     rc = fn(None, 0, 0, None, 1, 0, 0, None, 0, 0, None, None, 1, 17, 512, 16, 1.0, 1, None, 0, None, 0, 0, None,
             None, None)
     assert rc == _lib.EINVAL and b'heads' in lib.hla_s6_last_error()
+
+
+def test_wait_limit_is_process_wide_and_restorable(lib):
+    _lib = pkg('_lib')
+    prev = _lib.set_wait_limit_ns(5_000_000)
+    try:
+        assert prev == 2_000_000_000
+        assert _lib.set_wait_limit_ns(7_000_000) == 5_000_000
+    finally:
+        assert _lib.set_wait_limit_ns(0) == 7_000_000      # 0 restores the 2 s default
+    assert _lib.set_wait_limit_ns(0) == 2_000_000_000
 
 
 def test_workspace_overflow_is_reported(lib):

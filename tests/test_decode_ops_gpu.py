@@ -352,3 +352,14 @@ def test_decode_prepare_fuses_latent_query_and_exact_append():
             np.testing.assert_array_equal(flat[want[t], :, d:], v[t])
     untouched = np.setdiff1d(np.arange(nb * page), want[want >= 0])
     assert np.isnan(flat[untouched]).all()
+
+
+def test_probe_latent_rope_checks_the_b200_kernel():
+    """The start-up probe the adapter runs (s6_ops.py:44-58, ouro_latent.py:203) answers for the B200
+    kernel: the head stride is honoured (flat False) and the rotation is bit-exact with the torch formula."""
+    lay = pkg('s6_layer')
+    inv = lay.latent_inv_freq(128, 1e6)
+    for w in (512, 256):
+        table = lay.latent_rope_table(4096, inv, w, BF16).to(CUDA)
+        assert ops().probe_latent_rope(table, 16) == (False, True)
+        assert ops().probe_latent_rope(table) == (False, True)

@@ -29,6 +29,9 @@ int main(void) {
   rc = hla_s6_history_attention_static(0, 0, 0, 0, 1, 0, 0, 0, 0, 0, 0, 0, 64, 16, 512, 16, 1.0f, 16, 0, 0, 0, 0, 0,
                                        0);
   if (rc != HLA_S6_EOVERFLOW) return 13;
+  /* bounded waits: process-wide limit, 0 restores the 2 s default */
+  if (hla_s6_set_wait_limit_ns(1000000ull) != 2000000000ull) return 14;
+  if (hla_s6_set_wait_limit_ns(0) != 1000000ull) return 15;
   printf("ok %d\n", hla_s6_version());
   return 0;
 }

@@ -220,3 +220,33 @@ def test_full_size_decode_call_spot_rows():
     o_ref, lse_ref = orc.history_attention(qc, sub, tsub, np.full(len(rows), ctx_lat), SCALE)
     np.testing.assert_allclose(o[rows].float().cpu().numpy(), o_ref, **O_TOL)
     np.testing.assert_allclose(lse[:, rows].cpu().numpy(), lse_ref, atol=LSE_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize('splits', [1, 16])
+def test_block_id_outside_the_cache_is_reported(splits):
+    """A block-table entry at or past num_blocks (or negative) inside a row's pages: the reference's torch
+    indexing raises IndexError; the kernel reads that page as zeros - never outside the cache - and sets
+    HLA_S6_ERR_BLOCK in the error word.  A valid table leaves the word at 0."""
+    lib = pkg('_lib')
+    q, cache, table, ctx = random_case(3, 512, 16, 8, [300, 40, 0, 17], num_blocks=64)
+    T, H, W = q.shape
+    qd, cd, cx = dev(q, BF16), dev(cache, BF16), dev(ctx)
+    for bad, expect in ((None, 0), (64, lib.ERR_BLOCK), (-3, lib.ERR_BLOCK)):
+        tab = table.copy()
+        if bad is not None:
+            tab[1, 1] = bad                                 # row 1 (ctx 40) reads pages 0..2
+        td = dev(tab)
+        err = torch.zeros(1, dtype=I32, device=CUDA)
+        ws = torch.empty(T * splits * H * (W + 1), dtype=torch.float32, device=CUDA)
+        o = torch.empty(T, H, W, dtype=BF16, device=CUDA)
+        lse = torch.empty(H, T, dtype=torch.float32, device=CUDA)
+        lib.call('hla_s6_history_attention', lib.ptr(qd), qd.stride(0), qd.stride(1), lib.ptr(cd), cd.shape[0],
+                 cd.stride(0), cd.stride(2), lib.ptr(td), td.stride(0), td.shape[1], lib.ptr(cx), None, T, H, W, 16,
+                 SCALE, splits, lib.ptr(ws), ws.numel(), lib.ptr(o), o.stride(0), o.stride(1), lib.ptr(lse),
+                 lib.ptr(err), lib.stream_of(qd))
+        torch.cuda.synchronize()
+        assert int(err.item()) == expect
+        assert torch.isfinite(o.float()).all()
+        if bad is None:
+            o_ref, lse_ref = orc.history_attention(q, cache, tab, ctx, SCALE)
+            check(o, lse, o_ref, lse_ref, ctx)

@@ -160,6 +160,18 @@ def test_integer_metadata_matches_reference():
         assert orc.num_kv_splits(*c) == want
 
 
+def test_oracle_step_context_matches_reference():
+    """The oracle's StepContext restatement against the reference's own fields (step_context.json)."""
+    ref = json.loads((GOLDEN / 'step_context.json').read_text())
+    assert len(ref) == len(cases.step_context_cases())
+    for (qsl, seq_lens, T, window, table), want in zip(cases.step_context_cases(), ref):
+        req, valid, ctx, ctx_lat = orc.step_context(qsl, seq_lens, T, window)
+        assert req.tolist() == want['token_requests'] and valid.tolist() == want['valid']
+        assert ctx.tolist() == want['ctx'] and ctx_lat.tolist() == want['ctx_latent']
+        assert (ctx == 0).tolist() == want['empty'] and (ctx_lat == 0).tolist() == want['empty_latent']
+        assert np.asarray(table, dtype=np.int32)[req].tolist() == want['block_table']
+
+
 def test_oracle_decode_attend_equals_joint_softmax():
     """Independent check of the composed oracle (window + history + B + merge) against one
     joint softmax, as batched_engine.mixed_attention computes it."""

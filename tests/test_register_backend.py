@@ -2,8 +2,7 @@
 (hla/vllm_latent/s6_ops.py), read-only from a reference checkout: every other backend keeps running
 the reference's code, 'b200' reaches this package's ops (which refuse CPU tensors - there is no CPU
 path - proving the routing without a GPU), select_backends answers 'b200', and unregister restores the
-module.  CPU only; skipped where no reference checkout is present (REFERENCE_ROOT, default
-/root/reference)."""
+module.  CPU only; skipped unless HLA_REFERENCE_ROOT names a checkout of the reference project."""
 import importlib
 import os
 import sys
@@ -14,9 +13,9 @@ import torch
 
 from conftest import pkg
 
-REF = Path(os.environ.get('REFERENCE_ROOT', '/root/reference'))
+REF = Path(os.environ.get('HLA_REFERENCE_ROOT', '') or '/nonexistent')
 pytestmark = pytest.mark.skipif(not (REF / 'hla' / 'vllm_latent' / 's6_ops.py').exists(),
-                                reason='no reference checkout')
+                                reason='set HLA_REFERENCE_ROOT to a checkout of the reference project')
 
 
 @pytest.fixture()
@@ -80,7 +79,7 @@ def test_select_backends_and_unregister(ref_ops):
     reg = pkg('register_backend')
     originals = {n: getattr(ref_ops, n) for n in ('history_attention_kv', 'merge_states', 'latent_rope',
                                                    'chunk_attention', 'window_attention_fa', 'window_history_fa',
-                                                   'select_backends')}
+                                                   'select_backends', 'probe_latent_rope')}
     reg.register(ref_ops)
     reg.register(ref_ops)                                                     # idempotent
     assert ref_ops.history_attention_kv.__wrapped__ is originals['history_attention_kv']
@@ -92,3 +91,27 @@ def test_select_backends_and_unregister(ref_ops):
     reg.unregister(ref_ops)
     for name, fn in originals.items():
         assert getattr(ref_ops, name) is fn
+
+
+def test_window_ops_are_replaced_whatever_the_backend(ref_ops):
+    """The two window ops take no backend argument: once registered with window=True, the reference's own
+    s6_layer.attend reaches the B200 window even under TORCH_BACKENDS (here: this package's CUDA-only
+    ValueError on CPU tensors); with window=False the reference's own ops stay in place."""
+    layer = importlib.import_module('hla.vllm_latent.s6_layer')
+    reg = pkg('register_backend')
+    T, H, d = 1, 16, 128
+    ctx = layer.StepContext(torch.zeros(T, dtype=torch.long), torch.tensor([0, 1], dtype=torch.int32),
+                            torch.tensor([3], dtype=torch.int32), 1, T, {}, 0.1, ref_ops.TORCH_BACKENDS, window=32)
+    q = torch.randn(T, H, d)
+    window = (torch.randn(2, H, 16, 2 * d), torch.tensor([[1]], dtype=torch.int32))
+    original = ref_ops.window_attention_fa
+    reg.register(ref_ops, window=False)
+    assert ref_ops.window_attention_fa is original
+    reg.unregister(ref_ops)
+    reg.register(ref_ops)
+    assert ref_ops.window_attention_fa is not original
+    with pytest.raises(ValueError, match='CUDA'):
+        layer.attend(None, 1, None, q, q, q, None, None, None, None, ctx, window)
+    # the start-up probe now checks the B200 kernel (CUDA-only: refuses a CPU table)
+    with pytest.raises(ValueError, match='CUDA'):
+        ref_ops.probe_latent_rope(torch.zeros(16, 64, dtype=torch.bfloat16))

@@ -1,0 +1,235 @@
+"""Sequence split of the latent history emulated on ONE GPU, through the C ABI.
+
+The history is cut into N contiguous page slices (``decode.seq_split_rows``).  For each slice r the
+history split runs over that slice alone and ``hla_s6_history_reduce_exchange`` stores the slice's
+fp32 part (z, lse) into slot r of D receive regions (the D GPUs of a real run; here D regions of
+this GPU's memory) and raises flag r of each region.  ``hla_s6_decode_combine`` then waits for the
+N flags of one region, LSE-merges the N parts (the reference's merge semantics, s6_ops.py:353-361),
+up-projects by B and merges the exact window (s6_layer.py:97-115).  Every region must give the same
+output, equal to the oracle over the whole history, step after step, with the flags and CTA
+counters left zeroed for the slot's next use.
+
+All reduces complete before a combine starts (plain stream order, no programmatic launches), so no
+kernel here spins on a flag that a concurrently running kernel on this GPU would raise.
+
+The timeout test leaves one of two flags unraised and lowers the wait limit to a few milliseconds:
+the combine must give up, report HLA_S6_ERR_WAIT_PEER through its error word and return normally.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import pkg
+from oracle import s6_oracle as orc
+from test_attend_gpu import build_step, oracle
+
+pytestmark = pytest.mark.gpu
+CUDA, BF16, F32, I32 = 'cuda', torch.bfloat16, torch.float32, torch.int32
+O_TOL = dict(atol=2e-2, rtol=1e-2)
+PAGE, H, D_HEAD = 16, 16, 128
+
+
+class SplitStep:
+    """Device tensors of one decode (layer, loop) and the exchange buffers of an N-way split."""
+
+    def __init__(self, s, parts, regions, splits=16):
+        lib = pkg('_lib')
+        self.lib, self.s, self.N, self.D, self.splits = lib, s, parts, regions, splits
+        T, R, W = s['T'], s['R'], s['width']
+        self.T, self.W = T, W
+        dv = lambda a, dt=None: (lambda t: t.to(dt) if dt else t)(torch.from_numpy(np.ascontiguousarray(a)).to(CUDA))
+        self.q_lat, self.q_rope = dv(s['q_lat'], BF16), dv(s['q_rope'], BF16)
+        self.lat, self.B = dv(s['lat'], BF16), dv(s['B'], BF16)
+        self.ex = dv(s['ex'], BF16).transpose(1, 2)            # logical [nb, H, page, 2d]
+        self.etab, self.qsl, self.seq_lens = dv(s['etab']), dv(s['qsl']), dv(s['seq_lens'])
+        ltab_tok = np.zeros((T, s['ltab'].shape[1]), dtype=np.int32)
+        ltab_tok[:R] = s['ltab']
+        ctx_lat = np.zeros(T, dtype=np.int64)
+        ctx_lat[:R] = s['ctx_lat']
+        dec = pkg('decode')
+        self.slices = []
+        for r in range(parts):
+            split = dec.seq_split_rows(ctx_lat.tolist(), PAGE, r, parts)
+            table = np.zeros_like(ltab_tok)
+            rows = np.zeros(T, dtype=np.int32)
+            for t, (p0, n) in enumerate(split):
+                npg = -(-n // PAGE)
+                table[t, :npg] = ltab_tok[t, p0:p0 + npg]
+                rows[t] = n
+            self.slices.append((dv(table), dv(rows)))
+        self.ws_floats = T * splits * H * (W + 1)
+        self.ws = torch.empty(self.ws_floats, dtype=F32, device=CUDA)
+        self.part = -(-(T * H * W + H * T) // 4) * 4              # floats per part, a multiple of 4
+        self.recv = torch.full((regions, parts, self.part), float('nan'), dtype=F32, device=CUDA)
+        self.flags = torch.zeros(regions, parts, dtype=I32, device=CUDA)
+        self.done = torch.zeros(parts, dtype=I32, device=CUDA)
+        self.seen = torch.zeros(regions, dtype=I32, device=CUDA)
+        self.err = torch.zeros(1, dtype=I32, device=CUDA)
+        self.scale = 1 / math.sqrt(D_HEAD)
+
+    def reduce_slice(self, r, world=None):
+        """History split over slice r, then its part stored into slot r of every region (world
+        regions, default all) with flag r raised there."""
+        lib, T, W = self.lib, self.T, self.W
+        table, rows = self.slices[r]
+        stream = lib.stream_of(self.q_lat)
+        lib.call('hla_s6_history_partials', lib.ptr(self.q_lat), self.q_lat.stride(0), self.q_lat.stride(1),
+                 lib.ptr(self.lat), self.lat.shape[0], self.lat.stride(0), self.lat.stride(2), lib.ptr(table),
+                 table.stride(0), table.shape[1], lib.ptr(rows), T, H, W, PAGE, float(self.scale), self.splits,
+                 lib.ptr(self.ws), self.ws_floats, lib.ptr(self.err), 0, stream)
+        world = self.D if world is None else world
+        parts = [self.recv[d, r].data_ptr() for d in range(world)]
+        flags = [self.flags[d, r:].data_ptr() for d in range(world)]
+        lib.call('hla_s6_history_reduce_exchange', T, H, W, PAGE, self.splits, lib.ptr(self.ws), self.ws_floats,
+                 None, lib.pointer_array(parts), lib.pointer_array(flags), lib.ptr(self.done[r:]), world, 0, stream)
+
+    def combine(self, d):
+        lib, s, T, W = self.lib, self.s, self.T, self.W
+        out = torch.empty(T, H, D_HEAD, dtype=BF16, device=CUDA)
+        z = self.recv[d, 0]
+        stream = lib.stream_of(out)
+        lib.call('hla_s6_decode_combine', T, H, W, PAGE, self.splits, lib.ptr(self.ws), self.ws_floats, lib.ptr(z),
+                 lib.ptr(z[T * H * W:]), self.N, self.part, lib.ptr(self.flags[d]), lib.ptr(self.seen[d:]), None,
+                 lib.ptr(self.B), self.B.stride(0), self.B.stride(1), lib.ptr(self.q_rope), self.q_rope.stride(0),
+                 self.q_rope.stride(1), lib.ptr(self.ex), self.ex.shape[0], self.ex.stride(0), self.ex.stride(1),
+                 self.ex.stride(2), PAGE, lib.ptr(self.etab), self.etab.stride(0), self.etab.shape[1],
+                 lib.ptr(self.qsl), s['R'], lib.ptr(self.seq_lens), s['window'], float(self.scale), None, 0, 0, None,
+                 lib.ptr(out), out.stride(0), out.stride(1), None, 0, lib.ptr(self.err), stream)
+        return out
+
+    def step(self):
+        for r in range(self.N):
+            self.reduce_slice(r)
+        return [self.combine(d) for d in range(self.D)]
+
+
+@pytest.mark.parametrize('width', [512, 256])
+@pytest.mark.parametrize('parts', [2, 4])
+def test_n_part_merge_matches_whole_history_oracle(width, parts):
+    """N slices reduced into N regions, each region combined: every output equals the oracle over the
+    whole history, over two steps (slots, flags and counters reused; new q each step)."""
+    ctxs = [4096, 1000, 40, 2000, 0, 33, 31, 700]
+    for step in range(2):
+        s = build_step(100 * parts + width + step, width, ctxs)
+        run = SplitStep(s, parts, parts)
+        if step:   # the second step reuses the first step's exchange buffers and counters
+            run.recv, run.flags, run.done, run.seen = prev.recv, prev.flags, prev.done, prev.seen
+        outs = run.step()
+        torch.cuda.synchronize()
+        ref = oracle(s, run.scale)
+        for out in outs:
+            got = out.float().cpu().numpy()
+            assert np.isfinite(got).all() and (got[s['R']:] == 0).all()
+            np.testing.assert_allclose(got, ref, **O_TOL)
+            assert torch.equal(out, outs[0])           # every region merges the same parts
+        assert int(run.err.item()) == 0
+        assert int(run.flags.abs().sum()) == 0 and int(run.seen.abs().sum()) == 0 and int(run.done.abs().sum()) == 0
+        prev = run
+
+
+def test_config5_split_equals_single_gpu_path_at_full_context():
+    """BASELINE config 5's shape: B = 4 at ctx 131072, the history cut into 8 slices; the 8-part merge
+    equals the single-GPU fused decode attend over the whole history (size-independent property)."""
+    lay, ops = pkg('s6_layer'), pkg('s6_ops')
+    width, ctx = 512, 131072
+    rng = np.random.default_rng(5)
+    T = R = 4
+    window = 32
+    g = torch.Generator(device=CUDA).manual_seed(5)
+    pages = -(-(ctx + 1) // PAGE)
+    nb = T * pages + 1
+    lat = torch.randn(nb, 1, PAGE, 2 * width, dtype=BF16, device=CUDA, generator=g)
+    lat[0] = float('inf')
+    perm = torch.from_numpy(rng.permutation(np.arange(1, nb)).astype(np.int32))
+    ltab = perm.view(T, pages).to(CUDA)
+    enb = T * 4 + 1
+    ex = torch.randn(enb, PAGE, H, 2 * D_HEAD, dtype=BF16, device=CUDA, generator=g)
+    etab = torch.zeros(T, pages, dtype=I32)
+    for r in range(T):
+        for j, col in enumerate(range((ctx - window) // PAGE, ctx // PAGE + 1)):
+            etab[r, col] = 1 + 4 * r + j
+    s = dict(q_lat=None, T=T, R=R, width=width, window=window)
+    q_lat = torch.randn(T, H, width, generator=g, device=CUDA).to(BF16)
+    q_rope = torch.randn(T, H, D_HEAD, generator=g, device=CUDA).to(BF16)
+    B = (torch.randn(H, width, D_HEAD, generator=g, device=CUDA) / math.sqrt(width)).to(BF16)
+    qsl = torch.arange(R + 1, dtype=I32, device=CUDA)
+    seq_lens = torch.full((R,), ctx + 1, dtype=I32, device=CUDA)
+    scale = 1 / math.sqrt(D_HEAD)
+    splits = 64
+    ws = ops.S6Workspace(H, width, T * splits)
+    sctx = lay.StepContext(torch.full((T,), ctx, dtype=torch.int64, device=CUDA), qsl, seq_lens, 1, T, {}, scale,
+                           ops.B200_BACKENDS, ws, splits, window=window)
+
+    class SL:
+        def readers(self, loop):
+            return None, B, width
+
+    exl = ex.transpose(1, 2)
+    whole = lay.attend(SL(), 1, q_lat, q_rope, None, None, lat, ltab, None, None, sctx, (exl, etab.to(CUDA)))
+    # the split run, through the same tensors
+    run = SplitStep.__new__(SplitStep)
+    lib = pkg('_lib')
+    run.lib, run.N, run.D, run.splits, run.T, run.W, run.scale = lib, 8, 1, splits, T, width, scale
+    run.s = dict(R=R, window=window)
+    run.q_lat, run.q_rope, run.lat, run.B, run.ex = q_lat, q_rope, lat, B, exl
+    run.etab, run.qsl, run.seq_lens = etab.to(CUDA), qsl, seq_lens
+    dec = pkg('decode')
+    ltab_h = ltab.cpu().numpy()
+    run.slices = []
+    for r in range(8):
+        split = dec.seq_split_rows([ctx - window] * T, PAGE, r, 8)
+        table = np.zeros_like(ltab_h)
+        rows = np.zeros(T, dtype=np.int32)
+        for t, (p0, n) in enumerate(split):
+            npg = -(-n // PAGE)
+            table[t, :npg] = ltab_h[t, p0:p0 + npg]
+            rows[t] = n
+        run.slices.append((torch.from_numpy(table).to(CUDA), torch.from_numpy(rows).to(CUDA)))
+    run.ws_floats = T * splits * H * (width + 1)
+    run.ws = torch.empty(run.ws_floats, dtype=F32, device=CUDA)
+    run.part = -(-(T * H * width + H * T) // 4) * 4
+    run.recv = torch.full((1, 8, run.part), float('nan'), dtype=F32, device=CUDA)
+    run.flags = torch.zeros(1, 8, dtype=I32, device=CUDA)
+    run.done = torch.zeros(8, dtype=I32, device=CUDA)
+    run.seen = torch.zeros(1, dtype=I32, device=CUDA)
+    run.err = torch.zeros(1, dtype=I32, device=CUDA)
+    (split_out,) = run.step()
+    torch.cuda.synchronize()
+    assert int(run.err.item()) == 0
+    assert torch.isfinite(split_out.float()).all()
+    torch.testing.assert_close(split_out.float(), whole.float(), **O_TOL)
+    assert int(run.flags.abs().sum()) == 0 and int(run.seen.abs().sum()) == 0
+
+
+def test_flag_wait_gives_up_and_reports():
+    """Two parts, only part 0 delivered: with a 5 ms wait limit the combine reports
+    HLA_S6_ERR_WAIT_PEER and returns; part 1 (lse -inf) then counts as empty, so the output equals the
+    one-part merge, and the flags are cleared for the slot's next use."""
+    lib = pkg('_lib')
+    s = build_step(77, 512, [900, 40, 3000])
+    run = SplitStep(s, 1, 1)
+    run.N = 2
+    T, W = run.T, run.W
+    run.recv = torch.zeros(1, 2, run.part, dtype=F32, device=CUDA)
+    run.recv[0, 1, T * H * W:] = float('-inf')                   # part 1 never arrives: an empty part
+    run.flags = torch.zeros(1, 2, dtype=I32, device=CUDA)
+    run.reduce_slice(0, world=1)                                  # raises flag 0 only
+    prev = lib.set_wait_limit_ns(5_000_000)
+    try:
+        out = run.combine(0)
+        torch.cuda.synchronize()                                  # the kernel returned
+    finally:
+        lib.set_wait_limit_ns(prev)
+    assert int(run.err.item()) == lib.ERR_WAIT_PEER
+    assert int(run.flags.abs().sum()) == 0 and int(run.seen.abs().sum()) == 0
+    np.testing.assert_allclose(out.float().cpu().numpy(), oracle(s, run.scale), **O_TOL)
+    # the context is still usable: the same combine with both flags raised completes without error
+    run.err.zero_()
+    run.reduce_slice(0, world=1)
+    run.flags[0, 1] = 1
+    out2 = run.combine(0)
+    torch.cuda.synchronize()
+    assert int(run.err.item()) == 0
+    assert torch.equal(out2, out)

@@ -71,6 +71,45 @@ def test_static_scratch_matches_workspace_entry_point_on_consecutive_calls():
         torch.testing.assert_close(lse[:, ~empty], lse_ref[:, ~empty], atol=LSE_ATOL, rtol=0)
 
 
+def test_static_scratch_one_split_per_row():
+    """num_kv_splits = 1: one CTA per row instead of the stream-K page split."""
+    ops = pkg('s6_ops')
+    fn = static_entry()
+    scale = 1 / math.sqrt(128)
+    q, cache, table, ctx = case(5, 40, 512, [1500, 0, 33, 16, 1])
+    ws = ops.S6Workspace(16, 512, 40)
+    o_ref, lse_ref = ops.history_attention(q, cache, table, ctx, scale, 1, ws, None, None, 'b200')
+    for _ in range(2):
+        o, lse = run_static(fn, q, cache, table, ctx, 1, scale)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(o.float(), o_ref.float(), **O_TOL)
+        empty = ctx == 0
+        torch.testing.assert_close(lse[:, ~empty], lse_ref[:, ~empty], atol=LSE_ATOL, rtol=0)
+        assert (lse[:, empty] == -math.inf).all()
+
+
+def test_static_calls_back_to_back_on_one_stream():
+    """Two calls enqueued on the same stream before one synchronize: stream order keeps the second
+    call's split from overwriting the scratch before the first call's reduce has read it."""
+    ops = pkg('s6_ops')
+    fn = static_entry()
+    scale = 1 / math.sqrt(128)
+    a = case(11, 16, 512, [4000, 200, 0, 31])
+    b = case(12, 24, 256, [900, 1, 77, 5000])
+    refs = []
+    for (q, cache, table, ctx), W, splits in ((a, 512, 8), (b, 256, 16)):
+        ws = ops.S6Workspace(16, W, q.shape[0] * splits)
+        refs.append(ops.history_attention(q, cache, table, ctx, scale, splits, ws, None, None, 'b200'))
+    torch.cuda.synchronize()
+    out_a = run_static(fn, *a, 8, scale)
+    out_b = run_static(fn, *b, 16, scale)
+    torch.cuda.synchronize()
+    for (o, lse), (o_ref, lse_ref), (_, _, _, ctx) in zip((out_a, out_b), refs, (a, b)):
+        torch.testing.assert_close(o.float(), o_ref.float(), **O_TOL)
+        empty = ctx == 0
+        torch.testing.assert_close(lse[:, ~empty], lse_ref[:, ~empty], atol=LSE_ATOL, rtol=0)
+
+
 def test_static_scratch_rejects_calls_beyond_its_size():
     fn = static_entry()
     lib = pkg('_lib')
