@@ -97,13 +97,17 @@ int hla_s6_step_metadata(const int32_t* query_start_loc, int32_t num_reqs, const
 int hla_s6_gather_block_table(const int32_t* table, int64_t table_stride, int32_t max_blocks, int32_t num_reqs,
                               const int64_t* token_requests, int32_t num_tokens, int32_t* out, int64_t out_stride,
                               void* stream) {
-  if (max_blocks < 0 || num_reqs < 0 || num_tokens < 0 || table_stride < max_blocks || out_stride < max_blocks) {
+  // a row stride only matters between rows: a one-row table (or output) may carry any stride
+  if (max_blocks < 0 || num_reqs < 0 || num_tokens < 0 || (num_reqs > 1 && table_stride < max_blocks) ||
+      (num_tokens > 1 && out_stride < max_blocks)) {
     set_error("gather block table: bad sizes (max_blocks %d, num_reqs %d, num_tokens %d, strides %lld / %lld)",
               max_blocks, num_reqs, num_tokens, static_cast<long long>(table_stride),
               static_cast<long long>(out_stride));
     return kStatusInvalid;
   }
   if (num_tokens == 0 || max_blocks == 0) return kStatusOk;
+  if (num_reqs <= 1) table_stride = max_blocks;
+  if (num_tokens <= 1) out_stride = max_blocks;
   const bool vec = max_blocks % 4 == 0 && table_stride % 4 == 0 && out_stride % 4 == 0 &&
                    reinterpret_cast<uintptr_t>(table) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
   const int64_t n = static_cast<int64_t>(num_tokens) * (vec ? max_blocks / 4 : max_blocks);

@@ -84,3 +84,15 @@ def test_metadata_survives_graph_replay_with_new_contents():
     assert ctx.token_requests.tolist() == [0, 0, 1, 3]
     assert ctx.valid.tolist() == [True, True, True, False]
     assert ctx.ctx.tolist() == [2, 2, 6, 0] and ctx.ctx_latent.tolist() == [0, 0, 0, 0]
+
+
+def test_one_row_table_with_any_stride():
+    """A one-request table built from a broadcast numpy array can carry row stride 0 (torch keeps it for a
+    size-1 dim): the gather must not care about the stride of a single row."""
+    import numpy as np
+    ops = pkg('s6_ops')
+    row = np.arange(129, dtype=np.int32)
+    table = torch.from_numpy(np.broadcast_to(row, (1, 129)).copy()).as_strided((1, 129), (0, 1)).to(CUDA)
+    req = torch.zeros(3, dtype=torch.int64, device=CUDA)
+    out = ops.gather_block_table(table, req)
+    assert out.tolist() == [row.tolist()] * 3
