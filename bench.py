@@ -22,6 +22,9 @@ through all 24 layers x 4 loops per sample (config 5: one layer of 24, scaled an
 config-2 scale; --config export the rollout cache export of one 8192-token request (24 layers);
 --config heads the per-head (LLA MLA-style) history reader at B = 64, ctx 8192.
 
+--config full times BASELINE config 2 as a whole decode step: the Ouro dense body (RMSNorms, QKV/O
+projections, MLP; torch/cuBLAS) around the same attention path, one CUDA graph.
+
 --profile CASE runs a few eager steps of one workload for profilers (see run_profile).
 
 --config 3 measures the latent writer of a prompt step instead (8 prompts x 4096 tokens, 24 layers x
@@ -532,6 +535,177 @@ def run_ours(args):
     gc.collect()
     torch.cuda.synchronize()
     model.close_exchange()             # peer mappings: every rank, after its last launch
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
+# ----------------------------------------------------------------------------- full decode step
+class FullStep:
+    """BASELINE config 2's whole decode step: the Ouro decoder layer (hla/vllm_latent/ouro_latent.py:134-154)
+    around the B200 attention of OuroLatentAttention.forward (:106-131), 24 layers x 4 loops (:266-275).
+
+    Per (layer, loop): input RMSNorm (with the residual add from the second layer on), the fused QKV
+    projection, the S6 attention through ``S6DecodeModel.layer_loop`` (writer on a side stream, prepare,
+    history split, combine - q, k, v and h come from this dense body), the O projection, RMSNorm,
+    post-attention RMSNorm with the residual add, the SiLU MLP (intermediate 5632) and its RMSNorm;
+    after each loop the final RMSNorm.  Dense weights are random-init bf16 on cuBLAS (torch); they are
+    not this repository's kernels and are read from HBM every step (about 9.8 GB)."""
+
+    def __init__(self, model, seed, intermediate=5632, eps=1e-6):
+        import torch
+        self.torch, self.m, self.eps, self.I = torch, model, eps, intermediate
+        s, B, dev = model.s, model.B, model.device
+        D = s.hidden
+        g = torch.Generator(device=dev).manual_seed(seed + 7)
+        lin = lambda o, i: (torch.randn(o, i, generator=g, device=dev) / math.sqrt(i)).to(torch.bfloat16)
+        norm = lambda: (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+        self.w = [dict(qkv=lin(3 * D, D), o=lin(D, D), gate_up=lin(2 * intermediate, D), down=lin(D, intermediate),
+                       n1=norm(), n2=norm(), n3=norm(), n4=norm()) for _ in range(s.layers)]
+        self.final = norm()
+        self.x0 = torch.randn(B, D, generator=g, device=dev).to(torch.bfloat16)
+        self.out = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+        self.attn = torch.empty(B, s.heads, s.head_dim, dtype=torch.bfloat16, device=dev)
+        self.side = torch.cuda.Stream(dev)
+
+    def weight_bytes_per_step(self):
+        per_layer = sum(v.numel() * v.element_size() for v in self.w[0].values())
+        return per_layer * self.m.s.layers * self.m.s.loops
+
+    def _rms(self, x, w):
+        return self.torch.nn.functional.rms_norm(x, (x.shape[-1],), w, self.eps)
+
+    def step(self):
+        torch, F, m = self.torch, self.torch.nn.functional, self.m
+        s, B, D = m.s, m.B, m.s.hidden
+        main = torch.cuda.current_stream(m.device)
+        stream = pkg_lib().stream_of(self.out)
+        wstream = pkg_lib().ctypes.c_void_p(self.side.cuda_stream)
+        hidden = self.x0
+        for loop in range(s.loops):
+            residual = None
+            for layer in range(s.layers):
+                W = self.w[layer]
+                residual = hidden if residual is None else hidden + residual
+                h = self._rms(residual, W['n1'])
+                qkv = F.linear(h, W['qkv'])
+                q, k, v = (x.view(B, s.heads, s.head_dim) for x in qkv.split(D, -1))
+                self.side.wait_stream(main)               # the writer reads h
+                h.record_stream(self.side)
+                m.layer_loop(layer, loop, stream, wstream, io=(q, k, v, h, self.attn))
+                x = self._rms(F.linear(self.attn.view(B, D), W['o']), W['n2'])
+                residual = x + residual
+                x = self._rms(residual, W['n3'])
+                gu = F.linear(x, W['gate_up'])
+                x = F.linear(F.silu(gu[:, :self.I]) * gu[:, self.I:], W['down'])
+                hidden = self._rms(x, W['n4'])
+            hidden = self._rms(hidden + residual, self.final)
+        self.out.copy_(hidden)
+        main.wait_stream(self.side)
+
+    def capture(self):
+        torch = self.torch
+        warm = torch.cuda.Stream(self.m.device)
+        warm.wait_stream(torch.cuda.current_stream(self.m.device))
+        with torch.cuda.stream(warm):
+            self.step()
+        torch.cuda.current_stream(self.m.device).wait_stream(warm)
+        torch.cuda.synchronize(self.m.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.step()
+        return graph
+
+
+def pkg_lib():
+    return importlib.import_module(f'{PKG}._lib')
+
+
+def run_full(args):
+    """--config full: BASELINE config 2 as a whole Ouro-1.4B-shaped decode step (dense body included), one
+    GPU per rank, weak scaling (64 sequences at ctx 8192 each)."""
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    pkg_lib().load()
+    dec = importlib.import_module(f'{PKG}.decode')
+    ctx, scaling, _, max_pos = config_batch(2, rank, world, args.seed)
+    model = dec.S6DecodeModel(dec.OuroShape(max_position=max_pos), dec.DecodeBatch(ctx), device='cuda',
+                              seed=args.seed + rank)
+    full = FullStep(model, args.seed + rank)
+    full.step()
+    torch.cuda.synchronize()
+    graph = full.capture()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms_total = time_graph(torch, graph, args.steps, dist)
+    clocks = clk.summary()
+    ms_step = ms_total / args.steps
+    tokens_all = len(ctx) * world
+    # e2e: the step's input embeddings in from pinned memory, its final hidden states out
+    host_in = torch.empty(full.x0.shape, dtype=full.x0.dtype, pin_memory=True)
+    host_in.copy_(full.x0)
+    host_out = torch.empty(full.out.shape, dtype=full.out.dtype, pin_memory=True)
+    stream = torch.cuda.current_stream()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        full.x0.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(full.out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([ms_e2e], device='cuda')
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    line = None
+    if rank == 0:
+        attn = model.latent_bytes_per_step() + model.window_bytes_per_step()
+        wbytes = full.weight_bytes_per_step()
+        peak, peak_kind = peaks()
+        line = {
+            'metric': METRIC, 'value': tokens_all / (ms_step / 1e3), 'unit': 'tokens/s', 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded), random-init weights',
+            'config': {'workload': 'BASELINE config 2: whole Ouro-1.4B-shaped S6 decode step - the dense body '
+                                   '(RMSNorms, QKV / O projections, SiLU MLP 5632; torch/cuBLAS bf16) around the B200 '
+                                   'attention path, 24 layers x 4 loops, one CUDA graph',
+                       'global_batch': tokens_all, 'batch_per_gpu': len(ctx), 'ctx': max(ctx), 'seq_len': max(ctx) + 1,
+                       'parallelism': f'request-partitioned x{world} (no collectives)',
+                       'l2': 'inputs larger than L2 (latent caches ~40 GB, dense weights 2.5 GB per GPU), no flush'},
+            'step_bytes': {'latent_and_window': attn, 'dense_weights': wbytes,
+                           'frac_of_peak_in_step': (attn + wbytes) / (ms_step / 1e3) / 1e9 / peak},
+            'roofline': {'bound': 'hbm', 'kernel': 'whole step (attention latent/window bytes + dense weights)',
+                         'achieved': (attn + wbytes) / (ms_step / 1e3) / 1e9, 'peak': peak, 'unit': 'GB/s',
+                         'frac': (attn + wbytes) / (ms_step / 1e3) / 1e9 / peak, 'peak_source': peak_kind,
+                         'traffic': None},
+            'cpu_baseline': None,
+            'e2e': {'value': tokens_all / (ms_e2e / 1e3), 'unit': 'tokens/s',
+                    'h2d_bytes_per_step': host_in.numel() * host_in.element_size(),
+                    'd2h_bytes_per_step': host_out.numel() * host_out.element_size(),
+                    'path': 'FullStep graph: input embeddings copied in from pinned memory, final hidden states out'},
+            'gpu_launches': model.launches_per_step() * args.steps,
+            'clocks': clocks}
+        print(json.dumps(line), flush=True)
+    del graph
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -1096,7 +1270,7 @@ def main():
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5', 'contig', 'export', 'heads'])
+    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5', 'full', 'contig', 'export', 'heads'])
     ap.add_argument('--heads-rank', type=int, default=128, help='--config heads: latent rank r of the LLA rows')
     ap.add_argument('--heads-rope', type=int, default=32, help='--config heads: RoPE tail d_rope of the LLA rows')
     ap.add_argument('--seed', type=int, default=0)
@@ -1121,6 +1295,13 @@ def main():
         return
     if args.warmup < 3:
         raise SystemExit('--warmup must be >= 3')
+    if args.config == 'full':
+        if args.impl == 'reference':
+            args.config = 2          # the CPU arm times the same attention path per token (dense body excluded)
+            run_reference(args)
+            return
+        run_full(args)
+        return
     if args.config in ('contig', 'export', 'heads'):
         if args.impl == 'reference':
             print(json.dumps({'impl': 'reference', 'unavailable': f'--config {args.config} has no reference arm; '

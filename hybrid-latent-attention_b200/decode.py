@@ -277,13 +277,16 @@ class S6DecodeModel:
                   self.latent_table.stride(0), self.latent_table.shape[1], _lib.ptr(self.ctx_latent), B, s.heads,
                   width, s.page, float(self.scale), self.splits, _lib.ptr(self.ws), self.ws_floats, None, flags, stream)
 
-    def layer_loop(self, layer, loop, stream, wstream=None):
+    def layer_loop(self, layer, loop, stream, wstream=None, io=None):
         """The four launches of one (layer, loop); the writer goes to ``wstream`` when given (it reads only
-        ``h`` and feeds only the commit and the next loop's writer, so it overlaps the attention chain)."""
+        ``h`` and feeds only the commit and the next loop's writer, so it overlaps the attention chain).
+        ``io = (q, k, v, h, out)`` takes the pre-RoPE q, k, v ``[B, H, d]`` (any token / head strides), the
+        attention input ``h [B, hidden]`` and the output ``[B, H, d]`` from the caller - a dense body around
+        the attention - instead of the resident activation and output buffers."""
         wstream = stream if wstream is None else wstream
         s, B = self.s, self.B
         lat = self.layers[layer]
-        q, k, v, h = self._views(layer, loop)
+        q, k, v, h = self._views(layer, loop) if io is None else io[:4]
         A, Bm, width = lat.readers(loop)
         table = self.tables[width]
         # 1. writer; at loop 0 (loop-1 latent) and the last loop (main latent) the row is committed in
@@ -371,7 +374,7 @@ class S6DecodeModel:
             torch.distributed.all_gather_into_tensor(recv, send, group=group)
             z_in, lse_in, parts, flags = recv, recv[zf:], world, 0
         # 4. fused combine -> out (with the side stream's window part when window_overlap)
-        out = self.out[layer, loop]
+        out = self.out[layer, loop] if io is None else io[4]
         if win_done is not None:
             torch.cuda.current_stream(self.device).wait_event(win_done)
             chunk = (_lib.ptr(self.win_o), self.win_o.stride(0), self.win_o.stride(1), _lib.ptr(self.win_lse))
