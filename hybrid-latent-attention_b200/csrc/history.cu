@@ -178,6 +178,9 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tmap);
+      // pages are read once: evict them from L2 first, so that what the step reads again - the partials,
+      // the combine's up-projection and window rows - stays resident
+      const uint64_t stream_policy = l2_policy_evict_first();
       int r = row0, base, n;
       row_pages_base(r, base, n);
       int it = 0;
@@ -205,7 +208,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
           // a page outside the table or the cache loads as zeros (TMA out-of-range fill): never a read
           // outside the buffers, but the caller learns of it through the error word
           if (blk < 0 || blk >= p.num_blocks) record_error(p.err, kErrBlock);
-          tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk);
+          tma_load_4d_hint(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk, stream_policy);
         }
       }
     }
