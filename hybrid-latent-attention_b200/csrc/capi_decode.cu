@@ -150,9 +150,9 @@ int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_strid
     set_error("latent query needs head_dim 128 and width 256, 512 or 1024 (got %d, %d)", head_dim, width);
     return kStatusInvalid;
   }
-  if (max_position < 1 || table_stride < width || !aligned(q_pre, 16) || (q_stride_t % 8) || (q_stride_h % 8) ||
-      !aligned(A, 16) || (a_stride_h % 8) || (a_stride_k % 8)) {
-    set_error("latent query needs a [max_position, width] table and 16-byte aligned q rows / A rows");
+  if (max_position < 1 || table_stride < width || !aligned(table, 16) || (table_stride % 8) || !aligned(q_pre, 16) ||
+      (q_stride_t % 8) || (q_stride_h % 8) || !aligned(A, 16) || (a_stride_h % 8) || (a_stride_k % 8)) {
+    set_error("latent query needs a [max_position, width] table and 16-byte aligned table / q / A rows");
     return kStatusInvalid;
   }
   if (k && (page < 1 || num_reqs < 1 || cos_sin_rows < 1 || cos_sin_stride < 128 || (cos_sin_stride % 4) || !q_rope ||

@@ -147,6 +147,8 @@ template <int W>
 __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
   __shared__ __align__(128) uint8_t qs[64 * 256];   // q tile [64 tokens][128] bf16
   __shared__ __align__(128) uint8_t as[128 * 128];  // A tile [128 k][64 cols] bf16
+  __shared__ __align__(16) __nv_bfloat16 cs_s[64][64];  // RoPE rows of the tile: [token][cos 32 | sin 32]
+  __shared__ int64_t pos_s[64];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int x = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * 64;
   constexpr int HALF = W / 2;
@@ -204,6 +206,8 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
     return;
   }
   // ---------------- latent query tile
+  // one memory round for everything the tile reads: q, A and - once the positions are known - the RoPE
+  // rows of the tile's 32 pair columns, all in flight together
   const int n0 = 32 * x;
   for (int idx = tid; idx < 64 * 16; idx += 128) {  // q: 64 rows x 16 chunks
     const int row = idx >> 4, ch = idx & 15, t = t0 + row;
@@ -216,6 +220,14 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
     const int k = idx >> 3, ch = idx & 7;
     const int col = ch < 4 ? n0 + ch * 8 : HALF + n0 + (ch - 4) * 8;
     cp_async16(as + swz(k, ch, 128), Ah + static_cast<int64_t>(k) * p.a_sk + col);
+  }
+  cp_async_commit();
+  if (tid < 64) pos_s[tid] = t0 + tid < p.T ? clamp_pos(p.positions[t0 + tid], p.max_pos) : 0;
+  __syncthreads();
+  for (int idx = tid; idx < 64 * 8; idx += 128) {  // RoPE: 64 tokens x (4 cos chunks, 4 sin chunks)
+    const int row = idx >> 3, ch = idx & 7;
+    const __nv_bfloat16* tab = p.table + pos_s[row] * p.tab_st + (ch < 4 ? n0 + ch * 8 : HALF + n0 + (ch - 4) * 8);
+    cp_async16(&cs_s[row][ch * 8], tab);
   }
   cp_async_commit();
   cp_async_wait<0>();
@@ -241,18 +253,17 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
   // tile column of n-tile jn: jn < 4 -> n0 + 8 jn (+2c), jn >= 4 -> HALF + n0 + 8 (jn - 4)
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    const int t = t0 + warp * 16 + g + half * 8;
+    const int row = warp * 16 + g + half * 8, t = t0 + row;
     if (t >= p.T) continue;
-    const __nv_bfloat16* tab = p.table + clamp_pos(p.positions[t], p.max_pos) * p.tab_st;
     __nv_bfloat16* dst = p.q_lat + static_cast<int64_t>(t) * p.ql_st + static_cast<int64_t>(h) * p.ql_sh;
 #pragma unroll
     for (int jn = 0; jn < 4; ++jn) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int a = n0 + 8 * jn + 2 * c + e;
+        const int a = n0 + 8 * jn + 2 * c + e, la = 8 * jn + 2 * c + e;  // la: column within the tile's 32
         float y1, y2;
         rope_pair_torch(bf16_round(acc[jn][2 * half + e]), bf16_round(acc[jn + 4][2 * half + e]),
-                        __bfloat162float(tab[a]), __bfloat162float(tab[HALF + a]), y1, y2);
+                        __bfloat162float(cs_s[row][la]), __bfloat162float(cs_s[row][32 + la]), y1, y2);
         dst[a] = __float2bfloat16_rn(y1);
         dst[a + HALF] = __float2bfloat16_rn(y2);
       }

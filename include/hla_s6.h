@@ -270,7 +270,7 @@ int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const v
  * q_rope = exact neox RoPE of q_pre (a separate output; q_pre is not modified) plus the
  * exact-cache append of RoPE(k) | v as hla_s6_exact_append (slot_out optional).
  * Replaces s6_layer.py:82-84 latent_query + the model rotary_emb + unified_kv_cache_update at
- * hla/vllm_latent/ouro_latent.py:112-123.  q_pre and A rows must be 16-byte aligned. */
+ * hla/vllm_latent/ouro_latent.py:112-123.  q_pre, A and latent-table rows must be 16-byte aligned. */
 int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A,
                           int64_t a_stride_h, int64_t a_stride_k, const int64_t* positions, const void* table,
                           int64_t table_stride, int64_t max_position, void* q_lat, int64_t q_lat_stride_t,
