@@ -118,7 +118,7 @@ def history_attention(q, cache, block_table, ctx, scale, dt=np.float64):
             continue
         pages = -(-n // page)
         ids = np.asarray(block_table[t, :pages], dtype=np.int64)
-        rows = cache[ids, 0].reshape(pages * page, 2 * W)[:n].astype(dt)
+        rows = np.take(cache[:, 0], ids, axis=0).reshape(pages * page, 2 * W)[:n].astype(dt, copy=False)
         s = (q[t] @ rows[:, :W].T) * dt(scale)                    # [H, n]
         m = s.max(-1, keepdims=True)
         e = np.exp(s - m)
