@@ -437,22 +437,23 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
 // Stage-2 merge of one (row t, head h), 128 columns (chunk blockIdx.z) per CTA: the LSE-weighted
 // mean of the row's split partials (slots [lo, hi) from meta in stream mode, else slot t) and its
 // lse.  A long row can have ~100 partials (a few rows over a whole GPU), so the slots are spread
-// over kReduceLanes slot-lanes of 32 threads: the lse's max and the slot weights are computed once
-// into shared memory, every thread accumulates its float4 column over its lane's slots with four
-// loads in flight, and the lanes are summed through shared memory.  Thread (lane 0, c) returns
-// columns 128 z + 4c .. + 3 (other lanes return zeros).  An empty row (flagged, or no partial with
-// a finite lse) gives 0 and -inf.
+// over kReduceLanes slot-lanes (one warp each; 32 threads = 32 float4 columns): a warp loads the lse
+// and the column values of up to kReduceU of its slots in ONE memory round, the CTA agrees on the
+// running max through shared memory, and each thread accumulates its column; more slots take more
+// passes with an online rescale.  The lanes are summed through shared memory.  Thread (lane 0, c)
+// returns columns 128 z + 4c .. + 3 (other lanes return zeros).  An empty row (flagged, or no partial
+// with a finite lse) gives 0 and -inf.
 constexpr int kReduceLanes = 8, kReduceCols = 32, kReduceThreads = kReduceLanes * kReduceCols;
-constexpr int kReduceWBuf = 1024;  // slot weights per pass
+constexpr int kReduceU = 12;  // slots per slot-lane in one pass: 96 slots per pass
 
 template <int W>
 __device__ __forceinline__ float4 reduce_row(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
                                              const int2* __restrict__ meta, int stream_mode, int t, int h, int H,
                                              const uint8_t* __restrict__ empty, float& lse) {
-  __shared__ float wbuf[kReduceWBuf];
-  __shared__ float red[kReduceThreads / 32];
+  __shared__ float red[kReduceLanes];
+  __shared__ float sums[kReduceLanes];
   __shared__ float4 part[(kReduceLanes - 1) * kReduceCols];
-  const int tid = threadIdx.x, col = tid % kReduceCols, lane = tid / kReduceCols;
+  const int tid = threadIdx.x, col = tid % kReduceCols, lane = tid / kReduceCols;  // lane = warp
   const int colg = blockIdx.z * kReduceCols + col;  // float4 column of the row
   int lo, hi;
   if (stream_mode) {
@@ -463,49 +464,49 @@ __device__ __forceinline__ float4 reduce_row(const float* __restrict__ ws_o, con
     lo = t;
     hi = t + 1;
   }
-  const int n = hi - lo;
-  float mx = -INFINITY;
-  for (int i = tid; i < n; i += kReduceThreads) mx = fmaxf(mx, ws_lse[static_cast<int64_t>(lo + i) * H + h]);
-  mx = warp_max(mx);
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
-  __syncthreads();
-  mx = red[0];
-#pragma unroll
-  for (int i = 1; i < kReduceThreads / 32; ++i) mx = fmaxf(mx, red[i]);
-  const bool is_empty = (empty && empty[t]) || mx == -INFINITY;
+  const int n = (empty && empty[t]) ? 0 : hi - lo;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float wsum = 0.f;
-  if (!is_empty) {
-    for (int base = 0; base < n; base += kReduceWBuf) {
-      const int m = min(n - base, kReduceWBuf);
-      __syncthreads();  // the previous pass's weights are consumed
-      for (int i = tid; i < m; i += kReduceThreads)
-        wbuf[i] = expf(ws_lse[static_cast<int64_t>(lo + base + i) * H + h] - mx);
-      __syncthreads();
-      for (int i = 0; i < m; ++i) wsum += wbuf[i];  // same order in every thread
-      int i = lane;
-      for (; i + 3 * kReduceLanes < m; i += 4 * kReduceLanes) {
-        float4 v[4];
+  float wsum = 0.f, mx = -INFINITY;  // mx: the CTA's running max (the same in every thread)
+  for (int base = 0; base < n; base += kReduceLanes * kReduceU) {
+    float ls[kReduceU];
+    float4 v[kReduceU];
+    float pm = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          v[u] = reinterpret_cast<const float4*>(
-              ws_o + (static_cast<int64_t>(lo + base + i + u * kReduceLanes) * H + h) * W)[colg];
+    for (int u = 0; u < kReduceU; ++u) {  // one round: every load of this pass in flight together
+      const int i = base + lane + u * kReduceLanes;
+      const int64_t slot = lo + (i < n ? i : 0);
+      ls[u] = i < n ? ws_lse[slot * H + h] : -INFINITY;
+      v[u] = i < n ? reinterpret_cast<const float4*>(ws_o + (slot * H + h) * W)[colg] : make_float4(0.f, 0.f, 0.f, 0.f);
+      pm = fmaxf(pm, ls[u]);
+    }
+    if (col == 0) red[lane] = pm;
+    __syncthreads();
+    float m2 = mx;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float w = wbuf[i + u * kReduceLanes];
-          acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
-        }
-      }
-      for (; i < m; i += kReduceLanes) {
-        const float4 v =
-            reinterpret_cast<const float4*>(ws_o + (static_cast<int64_t>(lo + base + i) * H + h) * W)[colg];
-        const float w = wbuf[i];
-        acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
-      }
+    for (int l = 0; l < kReduceLanes; ++l) m2 = fmaxf(m2, red[l]);
+    __syncthreads();  // red is read by every thread before the next pass writes it
+    if (m2 == -INFINITY) continue;
+    if (m2 != mx) {
+      const float sc = expf(mx - m2);  // 0 while nothing has been summed (mx = -inf)
+      wsum *= sc;
+      acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+      mx = m2;
+    }
+#pragma unroll
+    for (int u = 0; u < kReduceU; ++u) {
+      if (ls[u] == -INFINITY) continue;  // past the row's slots, or a slot without keys
+      const float w = expf(ls[u] - mx);
+      wsum += w;
+      acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
     }
   }
   if (lane > 0) part[(lane - 1) * kReduceCols + col] = acc;
+  if (col == 0) sums[lane] = wsum;
   __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int l = 0; l < kReduceLanes; ++l) total += sums[l];
+  const bool is_empty = mx == -INFINITY;
   if (lane == 0) {
 #pragma unroll
     for (int l = 1; l < kReduceLanes; ++l) {
@@ -513,11 +514,13 @@ __device__ __forceinline__ float4 reduce_row(const float* __restrict__ ws_o, con
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     if (!is_empty) {
-      const float inv = 1.f / wsum;
+      const float inv = 1.f / total;
       acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+    } else {
+      acc = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-  lse = is_empty ? -INFINITY : mx + logf(wsum);
+  lse = is_empty ? -INFINITY : mx + logf(total);
   return acc;
 }
 
