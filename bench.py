@@ -502,7 +502,7 @@ def run_ours(args):
             'config': {'workload': f'BASELINE config {args.config}: Ouro-1.4B-shaped S6 decode step, attention path '
                                    f'(24 layers x 4 loops), dense body excluded' +
                                    ((', latent history sequence-split across GPUs, (z, lse) parts stored into '
-                                     'every GPU by the reduce kernel over NVLink (peer memory + flags) per (layer, '
+                                     'every GPU by the reduce kernel over NVLink (peer memory, tagged exchange words) per (layer, '
                                      'loop)' if args.exchange == 'peer' else
                                      ', latent history sequence-split across GPUs, NCCL all-gather of (z, lse) per '
                                      '(layer, loop)') if exchange is not None else ''),
@@ -1177,7 +1177,7 @@ def run_profile(args):
                N = 512 at loop 0 and 1024 at loops 1-3, 4096 tokens per prompt; 1 layer x 8 prompts: ~1 GB)
     seq-split  rank 0's share of an --split N-way sequence split (config 5: --batch 4 --ctx 131072) as a
                one-rank job: the latent rows of the first of N page slices, the reduce with its peer-store
-               exchange (to this GPU only) and the one-part flag wait in the combine; with --time it also
+               exchange (to this GPU only) and the one-part poll in the combine; with --time it also
                times the step and its history launches alone as CUDA graphs
     contig / heads / export   two calls of the other readers at the config-2 shape
     """

@@ -13,7 +13,7 @@ import torch
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get('HLA_S6_LIB', _PKG / 'libhla_s6.so'))
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
 # codes a kernel writes to its optional device error word (HLA_S6_ERR_*)
@@ -22,6 +22,7 @@ COMBINE_AFTER_PARTIALS = 1   # hla_s6_decode_combine flag (include/hla_s6.h)
 PARTIALS_AFTER_QUERY = 1     # hla_s6_history_partials flag
 REDUCE_AFTER_PARTIALS = 1    # hla_s6_history_reduce_exchange flag
 PEER_HANDLE_BYTES = 64       # HLA_S6_PEER_HANDLE_BYTES
+EXCHANGE_WORD_BYTES = 8      # HLA_S6_EXCHANGE_WORD_BYTES: fp32 value | 32-bit tag
 
 _c_void_p, _i32, _i64, _f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
 P = _c_void_p
@@ -64,7 +65,7 @@ SIGNATURES = {
     'hla_s6_peer_open': [P, P],
     'hla_s6_peer_close': [P],
     'hla_s6_peer_free': [P],
-    'hla_s6_history_reduce_exchange': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, P, _i32, _i32, P],
+    'hla_s6_history_reduce_exchange': [_i32, _i32, _i32, _i32, _i32, P, _i64, P, P, P, _i32, _i32, P],
     'hla_s6_window_history': [P, _i64, _i64, P, _i64, _i64, _i64, _i64, _i32, P, _i64, _i32, P, _i32, _f32, _i32,
                               _i32, _i32, P, _i64, _i64, P, P],
     'hla_s6_step_metadata': [P, _i32, P, _i32, _i32, P, P, P, P, P, P, P, P, P],

@@ -390,23 +390,22 @@ int hla_s6_history_attention_contig(const void* q, int64_t q_stride_b, int64_t q
 
 int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,
                                    int32_t num_kv_splits, float* workspace, int64_t workspace_floats,
-                                   const uint8_t* empty, float* const* parts, int32_t* const* flags, int32_t* done,
+                                   const uint8_t* empty, uint64_t* const* parts, const int32_t* epoch,
                                    int32_t world, int32_t launch_flags, void* stream) {
-  if (world < 1 || world > kMaxExchangeRanks || !parts || !flags || !done) {
-    set_error("history reduce exchange needs 1..%d ranks, their part and flag pointers and a counter",
+  if (world < 1 || world > kMaxExchangeRanks || !parts || !epoch) {
+    set_error("history reduce exchange needs 1..%d ranks, their part pointers and the slot's epoch counter",
               kMaxExchangeRanks);
     return kStatusInvalid;
   }
   ExchangeTargets x{};
   for (int d = 0; d < world; ++d) {
-    if (!parts[d] || !flags[d] || (reinterpret_cast<uintptr_t>(parts[d]) % 16)) {
-      set_error("history reduce exchange: rank %d's part must be 16-byte aligned and its flag set", d);
+    if (!parts[d] || (reinterpret_cast<uintptr_t>(parts[d]) % 16)) {
+      set_error("history reduce exchange: rank %d's part must be set and 16-byte aligned", d);
       return kStatusInvalid;
     }
     x.part[d] = parts[d];
-    x.flag[d] = flags[d];
   }
-  x.done = done;
+  x.epoch = epoch;
   x.world = world;
   HistoryArgs a = make_history_args(nullptr, 0, 0, nullptr, 0, 0, 0, nullptr, 0, 0, nullptr, num_tokens, num_heads,
                                     width, page, 1.f, num_kv_splits, workspace, workspace_floats, nullptr);

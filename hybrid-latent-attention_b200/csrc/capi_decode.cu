@@ -366,8 +366,8 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
 }
 
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
-                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
-                          const float* lse_in, int32_t num_parts, int64_t part_stride, int32_t* part_flags,
+                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const void* z_in,
+                          const void* lse_in, int32_t num_parts, int64_t part_stride, int32_t* epoch,
                           int32_t* part_seen, const uint8_t* empty,
                           const void* B, int64_t b_stride_h,
                           int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
@@ -415,24 +415,28 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
     a.ws_floats = workspace_floats;
     a.waves = 1;
     if ((rc = history_plan(a, &plan))) return rc;
-  } else if (!lse_in || !aligned(z_in, 16) || num_parts < 1 || (num_parts > 1 && (part_stride % 4))) {
+  } else if (!lse_in || !aligned(z_in, 16) || num_parts < 1 ||
+             (num_parts > 1 && (part_stride % (epoch ? 2 : 4)))) {
     set_error("a reduced history input needs >= 1 part of 16-byte aligned z [T, H, W] with its lse [H, T] "
-              "(part stride a multiple of 4 floats)");
+              "(part stride a multiple of 4 floats, or of 2 exchange words)");
+    return kStatusInvalid;
+  }
+  if (epoch && (!z_in || !part_seen || num_parts > 32 || !aligned(lse_in, 8))) {
+    set_error("decode combine: exchange words need reduced parts (z_in, 8-byte aligned lse_in, <= 32 parts), "
+              "the slot's epoch counter and a CTA counter");
     return kStatusInvalid;
   }
   p.ws_o = plan.ws_o;
   p.ws_lse = plan.ws_lse;
   p.meta = plan.meta;
   p.stream_mode = plan.stream_mode;
-  p.z_in = z_in;
-  p.lse_in = lse_in;
+  p.z_in = epoch ? nullptr : static_cast<const float*>(z_in);
+  p.lse_in = epoch ? nullptr : static_cast<const float*>(lse_in);
+  p.zw_in = epoch ? static_cast<const uint64_t*>(z_in) : nullptr;
+  p.lw_in = epoch ? static_cast<const uint64_t*>(lse_in) : nullptr;
   p.num_parts = z_in ? num_parts : 0;
   p.part_stride = part_stride;
-  if (part_flags && (!z_in || !part_seen)) {
-    set_error("decode combine: part flags need reduced parts (z_in) and a CTA counter");
-    return kStatusInvalid;
-  }
-  p.part_flags = z_in ? part_flags : nullptr;
+  p.epoch = epoch;
   p.part_seen = part_seen;
   p.err = error_flag;
   p.wait_ns = wait_limit_ns();

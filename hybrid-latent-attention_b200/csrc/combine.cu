@@ -86,19 +86,6 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
       lse_w = -INFINITY;
     }
     griddep_wait();
-    if (p.part_flags) {
-      // every rank's part of this exchange slot has landed (bounded wait); the last CTA through
-      // clears the flags for the slot's next use
-      if (threadIdx.x == 0) {
-        if (!wait_flags_sys(p.part_flags, p.num_parts, p.wait_ns)) record_error(p.err, kErrWaitPeer);
-        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
-        if (atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(p.part_seen), 1u) == total - 1) {
-          for (int q = 0; q < p.num_parts; ++q) p.part_flags[q] = 0;
-          *p.part_seen = 0;
-        }
-      }
-      __syncthreads();
-    }
     constexpr int NV = W / 128;  // float4 per lane
     float4 acc[NV];
 #pragma unroll
@@ -133,6 +120,61 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
           }
           lse_h = mx + logf(wsum);
         }
+      } else if (p.zw_in) {
+        // num_parts parts as exchange words stored by the parts' GPUs (history_reduce_exchange): each
+        // word is polled until it carries this exchange's tag.  The lse words first (lane q polls part
+        // q's), then the z words of two parts per memory round; the merge order is the one above.
+        WordPoll poll(static_cast<uint32_t>(*p.epoch) + 1u, p.wait_ns);
+        float lq = -INFINITY;
+        if (lane < p.num_parts) {
+          const uint64_t* src = p.lw_in + lane * p.part_stride + static_cast<int64_t>(h) * T + t;
+          uint64_t w = ld_word(src);
+          if (poll.wait1(src, w)) lq = word_value(w);
+        }
+        const float mx = warp_max(lq);
+        if (mx != -INFINITY) {
+          float wsum = 0.f;
+          for (int q0 = 0; q0 < p.num_parts; q0 += 2) {
+            float lu[2];
+            uint64_t wv[2][NV][4];
+            const uint64_t* src[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int q = q0 + u;
+              lu[u] = __shfl_sync(0xffffffffu, lq, q < p.num_parts ? q : 0);
+              if (q >= p.num_parts) lu[u] = -INFINITY;
+              src[u] = p.zw_in + q * p.part_stride + (static_cast<int64_t>(t) * H + h) * W;
+              if (lu[u] == -INFINITY) continue;  // past the parts, or a part without keys
+#pragma unroll
+              for (int i = 0; i < NV; ++i) {
+                ld_words2(src[u] + (i * 32 + lane) * 4, wv[u][i][0], wv[u][i][1]);
+                ld_words2(src[u] + (i * 32 + lane) * 4 + 2, wv[u][i][2], wv[u][i][3]);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (lu[u] == -INFINITY) continue;
+              const float wgt = expf(lu[u] - mx);
+              wsum += wgt;
+#pragma unroll
+              for (int i = 0; i < NV; ++i) {
+                // words that never arrived count as zeros (after a timeout, words already there are taken)
+                bool ok = poll.wait2(src[u] + (i * 32 + lane) * 4, wv[u][i][0], wv[u][i][1]);
+                ok = poll.wait2(src[u] + (i * 32 + lane) * 4 + 2, wv[u][i][2], wv[u][i][3]) && ok;
+                if (!ok) continue;
+                acc[i].x += wgt * word_value(wv[u][i][0]); acc[i].y += wgt * word_value(wv[u][i][1]);
+                acc[i].z += wgt * word_value(wv[u][i][2]); acc[i].w += wgt * word_value(wv[u][i][3]);
+              }
+            }
+          }
+          const float inv = 1.f / wsum;
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            acc[i].x *= inv; acc[i].y *= inv; acc[i].z *= inv; acc[i].w *= inv;
+          }
+          lse_h = mx + logf(wsum);
+        }
+        if (poll.failed) record_error(p.err, kErrWaitPeer);
       } else {
         int lo = t, hi = t + 1;
         if (p.stream_mode) {
@@ -213,6 +255,15 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
   const uint32_t zb = smem_u32(smem + S::Z_OFF);
   if (!mbar_wait(bbar, 0, p.wait_ns)) record_error(p.err, kErrWaitFull);
   __syncthreads();
+  if (p.epoch && tid == 0) {
+    // every warp of this CTA has taken its exchange words (the z tile is complete); the last CTA
+    // through advances the slot's use counter, so the slot's next exchange carries a new tag
+    const unsigned total = gridDim.x * gridDim.y;
+    if (atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(p.part_seen), 1u) == total - 1) {
+      *p.epoch += 1;
+      *p.part_seen = 0;
+    }
+  }
   for (int kc = 0; kc < NK; ++kc) {
     const uint32_t bb = smem_u32(smem + S::B_OFF + kc * kCChunkBytes);
 #pragma unroll

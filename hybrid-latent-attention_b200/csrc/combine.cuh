@@ -14,14 +14,17 @@ struct CombineParams {
   int stream_mode;
   const float* z_in;    // part q: z [T, H, W] at z_in + q * part_stride
   const float* lse_in;  // part q: lse [H, T] at lse_in + q * part_stride
+  // or the parts as exchange words (8 bytes per value, part_stride counting words) stored by other
+  // GPUs' history_reduce_exchange: polled until tagged *epoch + 1; the last CTA through advances
+  // *epoch and re-zeroes part_seen (a count of the CTAs)
+  const uint64_t* zw_in;
+  const uint64_t* lw_in;
   int num_parts;
-  int64_t part_stride;  // floats between consecutive parts
-  // parts written by other GPUs (history_reduce_exchange): wait until part_flags[0 .. num_parts)
-  // are all set, then clear them once every CTA has passed (part_seen counts the CTAs)
-  int* part_flags;
+  int64_t part_stride;
+  int* epoch;
   int* part_seen;
   int* err;  // optional device error word (a peer that never delivers)
-  uint64_t wait_ns;  // bound of the flag wait and of the B-load wait (device ns)
+  uint64_t wait_ns;  // bound of the exchange-word polls and of the B-load wait (device ns)
   const uint8_t* empty;  // optional [T]: rows whose latent history is empty
   int T, H;
   const __nv_bfloat16* B;  // [H, W, 128] up-projection

@@ -1,7 +1,7 @@
 // Shared device helpers for the S6 sm_100a kernels: mbarriers, TMA bulk-tensor loads,
 // ldmatrix / mma.sync fragments, bf16 packing and bounded waits.
 //
-// Every wait on an mbarrier or a peer flag is bounded by a limit in nanoseconds of device time
+// Every wait on an mbarrier or a peer's exchange words is bounded by a limit in nanoseconds of device time
 // (%globaltimer) that the launch passes in its parameters (hla_s6_set_wait_limit_ns, default
 // kDefaultWaitNs); when it runs out the kernel records an error code in the caller's error word
 // and the caller's loops unwind, so a lost copy turns into a status, never into a hung GPU.
@@ -34,16 +34,64 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// ---------------------------------------------------------------- cross-GPU flags (peer memory)
-// System-scope release / acquire on a flag word that another GPU writes or reads over NVLink.
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// ---------------------------------------------------------------- exchange words (peer memory)
+// A sequence-split part travels as 8-byte words: an fp32 value in the low half and the tag of the
+// exchange it belongs to in the high half.  An aligned 8-byte access is single-copy atomic, so a
+// reader that sees the expected tag in a word sees that word's value: the receiver polls the
+// words themselves and no fence or flag stands between the sender's stores and their use.  The
+// 16-byte accesses below are two such words each (each checked on its own).  Volatile global
+// accesses are relaxed at system scope: they bypass the non-coherent L1 and see NVLink stores.
+__device__ __forceinline__ uint64_t exchange_word(float v, uint32_t tag) {
+  return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
 }
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_words2(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
+__device__ __forceinline__ void st_word(uint64_t* p, uint64_t a) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+__device__ __forceinline__ void ld_words2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t a;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+__device__ __forceinline__ bool word_tagged(uint64_t w, uint32_t tag) { return static_cast<uint32_t>(w >> 32) == tag; }
+__device__ __forceinline__ float word_value(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
+// Bounded poll of exchange words for one thread: `limit_ns` of device time counted from the first
+// word that was not there yet, over all the thread's words.  The words passed in are the ones
+// already loaded; after a timeout a word that is there is still taken, one that is not is reported
+// missing at once (the caller records the error and uses zeros).
+struct WordPoll {
+  uint32_t tag;
+  uint64_t limit_ns;
+  uint64_t t0 = 0;
+  bool failed = false;
+  __device__ WordPoll(uint32_t tag_, uint64_t limit) : tag(tag_), limit_ns(limit) {}
+  // false when the words are still missing once the limit has run out
+  __device__ __forceinline__ bool wait2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    for (uint32_t it = 0; !(word_tagged(a, tag) && word_tagged(b, tag)); ++it) {
+      if (failed) return false;
+      if (t0 == 0) t0 = global_ns();
+      else if ((it & 15u) == 15u && global_ns() - t0 > limit_ns) failed = true;
+      ld_words2(p, a, b);
+    }
+    return true;
+  }
+  __device__ __forceinline__ bool wait1(const uint64_t* p, uint64_t& a) {
+    for (uint32_t it = 0; !word_tagged(a, tag); ++it) {
+      if (failed) return false;
+      if (t0 == 0) t0 = global_ns();
+      else if ((it & 15u) == 15u && global_ns() - t0 > limit_ns) failed = true;
+      a = ld_word(p);
+    }
+    return true;
+  }
+};
+
 __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
   unsigned old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
@@ -97,17 +145,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
   }
-}
-
-// Bounded wait until flags[0 .. n) are all nonzero (`limit_ns` of device time in total).
-__device__ __forceinline__ bool wait_flags_sys(const int* flags, int n, uint64_t limit_ns) {
-  const uint64_t t0 = global_ns();
-  for (int q = 0; q < n; ++q) {
-    for (uint32_t it = 0; ld_acquire_sys(flags + q) == 0; ++it) {
-      if ((it & 63u) == 63u && global_ns() - t0 > limit_ns) return false;
-    }
-  }
-  return true;
 }
 
 // ---------------------------------------------------------------- TMA

@@ -632,13 +632,12 @@ __global__ void __launch_bounds__(32 * kReduceWarpHeads)
   if (lane == 0 && lse_out) lse_out[static_cast<int64_t>(h) * lse_sh + t * lse_st] = is_empty ? -INFINITY : mx + logf(wsum);
 }
 
-// The sequence-split exchange fused into the reduce: this GPU's part - z fp32 [T, H, W] followed by
-// lse [H, T] - is stored straight into every rank's receive slot (peer memory over NVLink, this
-// GPU's own slot included).  Once every CTA's stores are visible system-wide, the last CTA to
-// finish raises this rank's flag word in every rank's flag array for the slot (release, system
-// scope); the consuming combine waits for all ranks' flags (acquire) and clears them.  Launched as
-// a programmatic dependent of the history kernel (griddepcontrol), it lets its own dependent - the
-// combine - start at once, so the combine's window phase overlaps this reduce.
+// The sequence-split exchange fused into the reduce: this GPU's part - z [T, H, W] followed by lse
+// [H, T], as exchange words tagged epoch + 1 - is stored straight into every rank's receive slot
+// (peer memory over NVLink, this GPU's own slot included).  The receivers poll the words, so the
+// kernel ends with its stores: no fence, flag or CTA counter.  Launched as a programmatic dependent
+// of the history kernel (griddepcontrol), it lets its own dependent - the combine - start at once,
+// so the combine's window phase overlaps this reduce and its merge consumes each row as it lands.
 template <int W>
 __global__ void __launch_bounds__(kReduceThreads)
     history_reduce_exchange_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
@@ -650,30 +649,21 @@ __global__ void __launch_bounds__(kReduceThreads)
   float lse;
   const float4 acc = reduce_row<W>(ws_o, ws_lse, meta, stream_mode, t, h, H, empty, lse);
   if (tid < kReduceCols) {
+    // the slot's use counter was last advanced by the combine of its previous use, which completed
+    // before this grid started (stream order)
+    const uint32_t tag = static_cast<uint32_t>(*x.epoch) + 1u;
     const int64_t zoff = (static_cast<int64_t>(t) * H + h) * W + (blockIdx.z * kReduceCols + tid) * 4;
     const int64_t loff = static_cast<int64_t>(T) * H * W + static_cast<int64_t>(h) * T + t;
     const bool lse_here = tid == 0 && blockIdx.z == 0;
+    const uint64_t w0 = exchange_word(acc.x, tag), w1 = exchange_word(acc.y, tag);
+    const uint64_t w2 = exchange_word(acc.z, tag), w3 = exchange_word(acc.w, tag);
+    const uint64_t wl = exchange_word(lse, tag);
 #pragma unroll
     for (int d = 0; d < kMaxExchangeRanks; ++d) {  // constant indices keep the targets in registers
       if (d >= x.world) break;
-      *reinterpret_cast<float4*>(x.part[d] + zoff) = acc;
-      if (lse_here) x.part[d][loff] = lse;
-    }
-    // each writer makes its own peer stores visible system-wide before the CTA barrier; the other
-    // threads stored nothing (a fence in every thread stalled the kernel on membar)
-    __threadfence_system();
-  }
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
-    if (atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(x.done), 1u) == total - 1) {
-      *x.done = 0;  // the slot's next use is a later launch (stream order)
-      __threadfence_system();
-#pragma unroll
-      for (int d = 0; d < kMaxExchangeRanks; ++d) {
-        if (d >= x.world) break;
-        st_release_sys(x.flag[d], 1);
-      }
+      st_words2(x.part[d] + zoff, w0, w1);
+      st_words2(x.part[d] + zoff + 2, w2, w3);
+      if (lse_here) st_word(x.part[d] + loff, wl);
     }
   }
 }

@@ -110,14 +110,13 @@ int heads_cache_tmap(CUtensorMap* map, const void* base, int64_t num_blocks, int
 int contig_rows_tmap(CUtensorMap* map, const void* base, int64_t B, int64_t N, int W, int64_t st_b, int64_t st_n,
                      int tile);
 
-// Targets of the fused sequence-split exchange (history_reduce_exchange): this rank's part in every
-// rank's receive slot, this rank's flag word in every rank's flag array for the slot, and the
-// local counter of finished CTAs.
+// Targets of the fused sequence-split exchange (history_reduce_exchange): this rank's part - exchange
+// words z [T, H, W] then lse [H, T] - in every rank's receive slot, and the slot's local use counter
+// (the words carry the tag epoch + 1).
 constexpr int kMaxExchangeRanks = 8;
 struct ExchangeTargets {
-  float* part[kMaxExchangeRanks];
-  int* flag[kMaxExchangeRanks];
-  int* done;
+  uint64_t* part[kMaxExchangeRanks];
+  const int* epoch;
   int world;
 };
 // pdl: launch as a programmatic dependent of the immediately preceding launch (the history split).

@@ -78,8 +78,8 @@ class S6DecodeModel:
 
     * ``'peer'`` (default): the reduce stores its part straight into every rank's receive slot over
       NVLink (CUDA IPC mappings of one exchange region per GPU: a slot per (layer, loop), each
-      holding ``world`` parts, plus a flag word per part) and raises the flags; the combine waits
-      for them.  No collective library call is on the step.
+      holding ``world`` parts) as tagged exchange words, which the combine polls.  No fence, flag or
+      collective library call is on the step.
     * ``'nccl'``: the reduce writes a local part and an NCCL ``all_gather_into_tensor`` moves it.
 
     ``pdl`` (default on): the history split is launched as a programmatic dependent of the prepare
@@ -194,17 +194,21 @@ class S6DecodeModel:
     # ------------------------------------------------------------------ peer exchange
     def _init_peer_exchange(self, rank, world, group):
         """One exchange region per GPU, mapped by every rank: ``slots x world`` parts of ``x_part``
-        floats (z [B, H, rank] then lse [H, B]), then ``slots x world`` int32 flags; plus two local
-        counters per slot (reduce CTAs done, combine CTAs through)."""
+        exchange words (z [B, H, rank] then lse [H, B]; 8 bytes each, zeroed so that no tag matches
+        before the first exchange); plus two local counters per slot (its epoch, which tags the
+        slot's exchanges, and the combine's CTA count).  A step cycles through all the slots, so a
+        slot's next exchange follows every rank's combine of its previous one."""
         import ctypes
         import torch.distributed as dist
         s, B = self.s, self.B
         slots = s.layers * s.loops
-        self.x_part = -(-(B * s.heads * s.rank + s.heads * B) // 4) * 4
-        self.x_region = slots * world * self.x_part * 4
+        if slots < 2:
+            raise ValueError('the peer exchange needs two or more (layer, loop) slots per step')
+        self.x_part = -(-(B * s.heads * s.rank + s.heads * B) // 2) * 2
+        self.x_region = slots * world * self.x_part * _lib.EXCHANGE_WORD_BYTES
         handle = ctypes.create_string_buffer(_lib.PEER_HANDLE_BYTES)
         base = ctypes.c_void_p()
-        _lib.call('hla_s6_peer_alloc', self.x_region + slots * world * 4, ctypes.byref(base), handle)
+        _lib.call('hla_s6_peer_alloc', self.x_region, ctypes.byref(base), handle)
         handles = [None] * world
         dist.all_gather_object(handles, handle.raw, group=group)
         bases = []
@@ -345,23 +349,21 @@ class S6DecodeModel:
         z_in = lse_in = None
         after = _lib.COMBINE_AFTER_PARTIALS if self.pdl else 0
         parts, part_stride, flags = 0, 0, after
-        part_flags = part_seen = None
+        x_epoch = part_seen = None        # the slot's epoch and CTA counter (peer exchange)
         if self.exchange is not None and self.exchange_mode == 'peer':
             import ctypes
             rank, world, _ = self.exchange
             i = loop * s.layers + layer          # exchange slot of this (layer, loop)
-            part_stride = self.x_part
-            parts = [b + (i * world + rank) * part_stride * 4 for b in self.x_bases]
-            flags_out = [b + self.x_region + (i * world + rank) * 4 for b in self.x_bases]
+            part_stride, wb = self.x_part, _lib.EXCHANGE_WORD_BYTES
+            parts = [b + (i * world + rank) * part_stride * wb for b in self.x_bases]
+            epoch = _lib.ptr(self.x_counters[2 * i])
             _lib.call('hla_s6_history_reduce_exchange', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws),
-                      self.ws_floats, None, _lib.pointer_array(parts), _lib.pointer_array(flags_out),
-                      _lib.ptr(self.x_counters[2 * i]), world, _lib.REDUCE_AFTER_PARTIALS if self.pdl else 0,
-                      stream)
-            own = self.x_bases[rank] + i * world * part_stride * 4
+                      self.ws_floats, None, _lib.pointer_array(parts), epoch, world,
+                      _lib.REDUCE_AFTER_PARTIALS if self.pdl else 0, stream)
+            own = self.x_bases[rank] + i * world * part_stride * wb
             z_in = ctypes.c_void_p(own)
-            lse_in = ctypes.c_void_p(own + B * s.heads * width * 4)
-            part_flags = ctypes.c_void_p(self.x_bases[rank] + self.x_region + i * world * 4)
-            part_seen = _lib.ptr(self.x_counters[2 * i + 1])
+            lse_in = ctypes.c_void_p(own + B * s.heads * width * wb)
+            x_epoch, part_seen = epoch, _lib.ptr(self.x_counters[2 * i + 1])
             parts, flags = world, after   # its producer is the reduce just launched
         elif self.exchange is not None:
             rank, world, group = self.exchange
@@ -381,7 +383,7 @@ class S6DecodeModel:
         else:
             chunk = (None, 0, 0, None)
         _lib.call('hla_s6_decode_combine', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws), self.ws_floats,
-                  _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, part_flags, part_seen, None, _lib.ptr(Bm),
+                  _lib.ptr(z_in), _lib.ptr(lse_in), parts, part_stride, x_epoch, part_seen, None, _lib.ptr(Bm),
                   Bm.stride(0), Bm.stride(1), _lib.ptr(qr), qr.stride(0), qr.stride(1),
                   _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
                   _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],

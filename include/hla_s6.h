@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define HLA_S6_ABI_VERSION 1
+#define HLA_S6_ABI_VERSION 2
 #define HLA_S6_OK 0
 #define HLA_S6_EINVAL 1
 #define HLA_S6_EOVERFLOW 2
@@ -328,10 +328,12 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
  * outside (prefill / mixed steps: hla_s6_chunk_attention merged with hla_s6_window_history),
  * used instead of the decode window; the window arguments other than query_start_loc /
  * num_reqs are then ignored (s6_layer.py:101-115, non-fused branch).
- * part_flags / part_seen (optional, with z_in): the parts are written by other GPUs
- * (hla_s6_history_reduce_exchange); the combine first waits - bounded, error_flag receives 4 on
- * a timeout - until part_flags[0 .. num_parts) are all set, and its last CTA clears them and the
- * CTA counter part_seen (a zeroed device int) for the slot's next use.
+ * epoch / part_seen (optional, with z_in): the parts are exchange words (HLA_S6_EXCHANGE_WORD_BYTES
+ * per value; z_in, lse_in and part_stride count words, part_stride even, <= 32 parts) that other
+ * GPUs store (hla_s6_history_reduce_exchange with the same slot's epoch counter).  Each word is
+ * polled until it carries the tag *epoch + 1 - bounded; error_flag receives 4 and the part counts
+ * as zeros on a timeout - and the combine's last CTA advances *epoch and re-zeroes the CTA counter
+ * part_seen (a zeroed device int) for the slot's next exchange.
  * flags: HLA_S6_COMBINE_AFTER_PARTIALS declares that the immediately preceding launch on the
  * stream produced this combine's history input - the hla_s6_history_partials call (partials) or,
  * with z_in, the hla_s6_history_reduce_exchange call; the combine is then launched as a
@@ -339,8 +341,8 @@ int hla_s6_commit_rows(const void* row, int64_t row_stride_t, int32_t width, con
  * before that launch) overlap the producer's tail. */
 #define HLA_S6_COMBINE_AFTER_PARTIALS 1
 int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t latent_page,
-                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const float* z_in,
-                          const float* lse_in, int32_t num_parts, int64_t part_stride, int32_t* part_flags,
+                          int32_t num_kv_splits, float* workspace, int64_t workspace_floats, const void* z_in,
+                          const void* lse_in, int32_t num_parts, int64_t part_stride, int32_t* epoch,
                           int32_t* part_seen, const uint8_t* empty,
                           const void* B, int64_t b_stride_h,
                           int64_t b_stride_k, const void* q_rope, int64_t q_stride_t, int64_t q_stride_h,
@@ -354,9 +356,15 @@ int hla_s6_decode_combine(int32_t num_tokens, int32_t num_heads, int32_t width, 
 
 /* ---------------------------------------------------------------- sequence-split exchange
  * The reference merges a sequence-split history through NCCL (the all_gather of (z, lse) parts
- * planned for hla/vllm_latent on 8 GPUs); here the reduce writes its part straight into every
- * rank's memory over NVLink and raises a flag there, and the combine waits for the flags.
+ * planned for hla/vllm_latent on 8 GPUs); here the reduce stores its part straight into every
+ * rank's memory over NVLink as exchange words - 8 bytes each: an fp32 value in the low 32 bits and
+ * the exchange's tag in the high 32 bits - and the combine polls the words themselves, so no fence,
+ * flag or collective call stands between a part's stores and its use.  The tag of a slot's k-th
+ * exchange is k: every rank keeps a device int32 epoch counter per slot (zeroed, as the receive
+ * slots are), which the combine advances.  A slot's next exchange must start after every rank's
+ * combine of its previous one has completed (true when a step cycles through two or more slots).
  * No counterpart call in the reference. */
+#define HLA_S6_EXCHANGE_WORD_BYTES 8
 
 /* Device memory that the other processes of this node can map (CUDA IPC), zero-filled.
  * handle receives HLA_S6_PEER_HANDLE_BYTES opaque bytes to pass to hla_s6_peer_open. */
@@ -366,12 +374,11 @@ int hla_s6_peer_open(const void* handle, void** ptr);
 int hla_s6_peer_close(void* ptr);
 int hla_s6_peer_free(void* ptr);
 
-/* hla_s6_history_reduce, with this GPU's reduced part (z fp32 [T, H, width] then lse [H, T])
- * stored into parts[d] for every rank d < world (device pointers into each rank's receive slot,
- * this rank's own included; 16-byte aligned), after which flags[d] (this rank's flag word in rank
- * d's flag array for the slot) is set to 1 with system-scope release.  done: a zeroed device
- * counter private to the slot (left zeroed).  world <= 8.  Pass the same slot's receive region,
- * flag array and a second counter to hla_s6_decode_combine (z_in, part_flags, part_seen).
+/* hla_s6_history_reduce, with this GPU's reduced part (z [T, H, width] then lse [H, T], exchange
+ * words tagged *epoch + 1) stored into parts[d] for every rank d < world (device pointers into each
+ * rank's receive slot, this rank's own included; 16-byte aligned; T * H * width + H * T words).
+ * epoch: this rank's counter for the slot, which the slot's combine (hla_s6_decode_combine with
+ * the same epoch) advances.  world <= 8.
  * launch_flags: HLA_S6_REDUCE_AFTER_PARTIALS declares that the immediately preceding launch on the
  * stream is the hla_s6_history_partials call that produced the partials (the reduce is then a
  * programmatic dependent of it, and in turn lets a combine launched with
@@ -379,7 +386,7 @@ int hla_s6_peer_free(void* ptr);
 #define HLA_S6_REDUCE_AFTER_PARTIALS 1
 int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,
                                    int32_t num_kv_splits, float* workspace, int64_t workspace_floats,
-                                   const uint8_t* empty, float* const* parts, int32_t* const* flags, int32_t* done,
+                                   const uint8_t* empty, uint64_t* const* parts, const int32_t* epoch,
                                    int32_t world, int32_t launch_flags, void* stream);
 
 /* Rollout cache export: the latent rows of one finished request - positions 0 .. length-1 of every

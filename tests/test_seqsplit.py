@@ -3,7 +3,8 @@
 CPU: two gloo ranks each attend over their page slice with the oracle, all-gather (z, lse) and
 LSE-merge; the result equals the oracle over the whole history, and the slices tile it exactly.
 GPU (two or more devices): two ranks run the kernel path - history split on the local slice, fp32
-reduce, exchange of the packed parts (peer stores + flags, or an NCCL all-gather), N-part combine -
+reduce, exchange of the packed parts (peer stores of tagged exchange words, or an NCCL all-gather), N-part
+combine -
 and match the single-GPU path over the whole history, over two steps.
 """
 import math
@@ -138,7 +139,7 @@ def _gpu_rank(rank, world, init, out, mode):
             a.load_state_dict(b.state_dict())
         stream = lib.stream_of(full.out)
         acts0 = full.acts.clone()
-        # two steps: every exchange slot (and, in peer mode, its flags and counters) is used twice
+        # two steps: every exchange slot (and, in peer mode, its epoch and CTA counter) is used twice
         for step in range(2):
             for loop in range(shape.loops):
                 full.acts[0, loop].copy_(acts0[0, loop])
@@ -149,7 +150,9 @@ def _gpu_rank(rank, world, init, out, mode):
             torch.testing.assert_close(part.out.float(), full.out.float(), atol=2e-2, rtol=1e-2)
             part.out.zero_()
         if mode == 'peer':
-            assert int(part.x_counters.abs().sum()) == 0       # counters left zeroed for the next use
+            counters = part.x_counters.view(-1, 2).cpu()
+            assert (counters[:, 0] == 2).all()                 # every slot's epoch advanced once per step
+            assert (counters[:, 1] == 0).all()                 # CTA counters left zeroed for the next use
         if rank == 0:
             with open(out, 'w') as f:
                 f.write('ok')
@@ -163,8 +166,9 @@ def _gpu_rank(rank, world, init, out, mode):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs two GPUs')
 @pytest.mark.parametrize('mode', ['peer', 'nccl'])
 def test_two_ranks_match_the_whole_history_path(mode):
-    """peer: the reduce stores each part into both GPUs' memory and raises flags (one GPU per rank,
-    so the flag waits never run as two launches on one GPU); nccl: all_gather of the parts."""
+    """peer: the reduce stores each part into both GPUs' memory as exchange words that the combine
+    polls (one GPU per rank, so the polls never wait on a launch of the same GPU); nccl: all_gather
+    of the parts."""
     with tempfile.TemporaryDirectory() as d:
         init, out = f'file://{os.path.join(d, "rdv")}', os.path.join(d, 'result')
         _run_ranks(_gpu_rank, 2, init, out, 300, mode)

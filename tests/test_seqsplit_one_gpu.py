@@ -2,18 +2,19 @@
 
 The history is cut into N contiguous page slices (``decode.seq_split_rows``).  For each slice r the
 history split runs over that slice alone and ``hla_s6_history_reduce_exchange`` stores the slice's
-fp32 part (z, lse) into slot r of D receive regions (the D GPUs of a real run; here D regions of
-this GPU's memory) and raises flag r of each region.  ``hla_s6_decode_combine`` then waits for the
-N flags of one region, LSE-merges the N parts (the reference's merge semantics, s6_ops.py:353-361),
-up-projects by B and merges the exact window (s6_layer.py:97-115).  Every region must give the same
-output, equal to the oracle over the whole history, step after step, with the flags and CTA
-counters left zeroed for the slot's next use.
+part (z, lse) as tagged exchange words into slot r of D receive regions (the D GPUs of a real run;
+here D regions of this GPU's memory).  ``hla_s6_decode_combine`` then polls the N parts of one region,
+LSE-merges them (the reference's merge semantics, s6_ops.py:353-361), up-projects by B and merges the
+exact window (s6_layer.py:97-115).  Every region must give the same output, equal to the oracle over
+the whole history, step after step, with each region's epoch advanced once per step and its CTA
+counter left zeroed.
 
 All reduces complete before a combine starts (plain stream order, no programmatic launches), so no
-kernel here spins on a flag that a concurrently running kernel on this GPU would raise.
+kernel here polls words that a concurrently running kernel on this GPU would store.
 
-The timeout test leaves one of two flags unraised and lowers the wait limit to a few milliseconds:
-the combine must give up, report HLA_S6_ERR_WAIT_PEER through its error word and return normally.
+The timeout tests never deliver one of two parts (or leave last exchange's words in it) and lower the
+wait limit to a few milliseconds: the combine must give up, report HLA_S6_ERR_WAIT_PEER through its
+error word and return normally.
 """
 import math
 
@@ -26,7 +27,7 @@ from oracle import s6_oracle as orc
 from test_attend_gpu import build_step, oracle
 
 pytestmark = pytest.mark.gpu
-CUDA, BF16, F32, I32 = 'cuda', torch.bfloat16, torch.float32, torch.int32
+CUDA, BF16, F32, I32, I64 = 'cuda', torch.bfloat16, torch.float32, torch.int32, torch.int64
 O_TOL = dict(atol=2e-2, rtol=1e-2)
 PAGE, H, D_HEAD = 16, 16, 128
 
@@ -61,17 +62,16 @@ class SplitStep:
             self.slices.append((dv(table), dv(rows)))
         self.ws_floats = T * splits * H * (W + 1)
         self.ws = torch.empty(self.ws_floats, dtype=F32, device=CUDA)
-        self.part = -(-(T * H * W + H * T) // 4) * 4              # floats per part, a multiple of 4
-        self.recv = torch.full((regions, parts, self.part), float('nan'), dtype=F32, device=CUDA)
-        self.flags = torch.zeros(regions, parts, dtype=I32, device=CUDA)
-        self.done = torch.zeros(parts, dtype=I32, device=CUDA)
+        self.part = -(-(T * H * W + H * T) // 2) * 2              # exchange words per part, even
+        self.recv = torch.zeros(regions, parts, self.part, dtype=I64, device=CUDA)   # tag 0: nothing yet
+        self.epochs = torch.zeros(regions, dtype=I32, device=CUDA)
         self.seen = torch.zeros(regions, dtype=I32, device=CUDA)
         self.err = torch.zeros(1, dtype=I32, device=CUDA)
         self.scale = 1 / math.sqrt(D_HEAD)
 
     def reduce_slice(self, r, world=None):
         """History split over slice r, then its part stored into slot r of every region (world
-        regions, default all) with flag r raised there."""
+        regions, default all), tagged with the regions' common epoch + 1."""
         lib, T, W = self.lib, self.T, self.W
         table, rows = self.slices[r]
         stream = lib.stream_of(self.q_lat)
@@ -81,9 +81,8 @@ class SplitStep:
                  lib.ptr(self.ws), self.ws_floats, lib.ptr(self.err), 0, stream)
         world = self.D if world is None else world
         parts = [self.recv[d, r].data_ptr() for d in range(world)]
-        flags = [self.flags[d, r:].data_ptr() for d in range(world)]
         lib.call('hla_s6_history_reduce_exchange', T, H, W, PAGE, self.splits, lib.ptr(self.ws), self.ws_floats,
-                 None, lib.pointer_array(parts), lib.pointer_array(flags), lib.ptr(self.done[r:]), world, 0, stream)
+                 None, lib.pointer_array(parts), lib.ptr(self.epochs), world, 0, stream)
 
     def combine(self, d):
         lib, s, T, W = self.lib, self.s, self.T, self.W
@@ -91,7 +90,7 @@ class SplitStep:
         z = self.recv[d, 0]
         stream = lib.stream_of(out)
         lib.call('hla_s6_decode_combine', T, H, W, PAGE, self.splits, lib.ptr(self.ws), self.ws_floats, lib.ptr(z),
-                 lib.ptr(z[T * H * W:]), self.N, self.part, lib.ptr(self.flags[d]), lib.ptr(self.seen[d:]), None,
+                 lib.ptr(z[T * H * W:]), self.N, self.part, lib.ptr(self.epochs[d:]), lib.ptr(self.seen[d:]), None,
                  lib.ptr(self.B), self.B.stride(0), self.B.stride(1), lib.ptr(self.q_rope), self.q_rope.stride(0),
                  self.q_rope.stride(1), lib.ptr(self.ex), self.ex.shape[0], self.ex.stride(0), self.ex.stride(1),
                  self.ex.stride(2), PAGE, lib.ptr(self.etab), self.etab.stride(0), self.etab.shape[1],
@@ -109,13 +108,13 @@ class SplitStep:
 @pytest.mark.parametrize('parts', [2, 4])
 def test_n_part_merge_matches_whole_history_oracle(width, parts):
     """N slices reduced into N regions, each region combined: every output equals the oracle over the
-    whole history, over two steps (slots, flags and counters reused; new q each step)."""
+    whole history, over two steps (slots, epochs and counters reused; new q each step)."""
     ctxs = [4096, 1000, 40, 2000, 0, 33, 31, 700]
     for step in range(2):
         s = build_step(100 * parts + width + step, width, ctxs)
         run = SplitStep(s, parts, parts)
         if step:   # the second step reuses the first step's exchange buffers and counters
-            run.recv, run.flags, run.done, run.seen = prev.recv, prev.flags, prev.done, prev.seen
+            run.recv, run.epochs, run.seen = prev.recv, prev.epochs, prev.seen
         outs = run.step()
         torch.cuda.synchronize()
         ref = oracle(s, run.scale)
@@ -125,7 +124,7 @@ def test_n_part_merge_matches_whole_history_oracle(width, parts):
             np.testing.assert_allclose(got, ref, **O_TOL)
             assert torch.equal(out, outs[0])           # every region merges the same parts
         assert int(run.err.item()) == 0
-        assert int(run.flags.abs().sum()) == 0 and int(run.seen.abs().sum()) == 0 and int(run.done.abs().sum()) == 0
+        assert (run.epochs == step + 1).all() and int(run.seen.abs().sum()) == 0
         prev = run
 
 
@@ -189,10 +188,9 @@ def test_config5_split_equals_single_gpu_path_at_full_context():
         run.slices.append((torch.from_numpy(table).to(CUDA), torch.from_numpy(rows).to(CUDA)))
     run.ws_floats = T * splits * H * (width + 1)
     run.ws = torch.empty(run.ws_floats, dtype=F32, device=CUDA)
-    run.part = -(-(T * H * width + H * T) // 4) * 4
-    run.recv = torch.full((1, 8, run.part), float('nan'), dtype=F32, device=CUDA)
-    run.flags = torch.zeros(1, 8, dtype=I32, device=CUDA)
-    run.done = torch.zeros(8, dtype=I32, device=CUDA)
+    run.part = -(-(T * H * width + H * T) // 2) * 2
+    run.recv = torch.zeros(1, 8, run.part, dtype=I64, device=CUDA)
+    run.epochs = torch.zeros(1, dtype=I32, device=CUDA)
     run.seen = torch.zeros(1, dtype=I32, device=CUDA)
     run.err = torch.zeros(1, dtype=I32, device=CUDA)
     (split_out,) = run.step()
@@ -200,22 +198,27 @@ def test_config5_split_equals_single_gpu_path_at_full_context():
     assert int(run.err.item()) == 0
     assert torch.isfinite(split_out.float()).all()
     torch.testing.assert_close(split_out.float(), whole.float(), **O_TOL)
-    assert int(run.flags.abs().sum()) == 0 and int(run.seen.abs().sum()) == 0
+    assert int(run.epochs.item()) == 1 and int(run.seen.item()) == 0
 
 
-def test_flag_wait_gives_up_and_reports():
+def exchange_words(values, tag):
+    """Exchange words (int64) of fp32 ``values`` tagged ``tag``: value bits low, tag high."""
+    bits = torch.as_tensor(values, dtype=F32).view(I32).to(I64) & 0xFFFFFFFF
+    return bits | (int(tag) << 32)
+
+
+def test_exchange_wait_gives_up_and_reports():
     """Two parts, only part 0 delivered: with a 5 ms wait limit the combine reports
-    HLA_S6_ERR_WAIT_PEER and returns; part 1 (lse -inf) then counts as empty, so the output equals the
-    one-part merge, and the flags are cleared for the slot's next use."""
+    HLA_S6_ERR_WAIT_PEER and returns; the missing part counts as empty, so the output equals the
+    one-part merge, and the slot's epoch still advances.  The next exchange of the slot, with part 1
+    delivered as an empty part, completes without error."""
     lib = pkg('_lib')
     s = build_step(77, 512, [900, 40, 3000])
     run = SplitStep(s, 1, 1)
     run.N = 2
     T, W = run.T, run.W
-    run.recv = torch.zeros(1, 2, run.part, dtype=F32, device=CUDA)
-    run.recv[0, 1, T * H * W:] = float('-inf')                   # part 1 never arrives: an empty part
-    run.flags = torch.zeros(1, 2, dtype=I32, device=CUDA)
-    run.reduce_slice(0, world=1)                                  # raises flag 0 only
+    run.recv = torch.zeros(1, 2, run.part, dtype=I64, device=CUDA)   # part 1's words stay untagged
+    run.reduce_slice(0, world=1)
     prev = lib.set_wait_limit_ns(5_000_000)
     try:
         out = run.combine(0)
@@ -223,13 +226,38 @@ def test_flag_wait_gives_up_and_reports():
     finally:
         lib.set_wait_limit_ns(prev)
     assert int(run.err.item()) == lib.ERR_WAIT_PEER
-    assert int(run.flags.abs().sum()) == 0 and int(run.seen.abs().sum()) == 0
+    assert int(run.epochs.item()) == 1 and int(run.seen.item()) == 0
     np.testing.assert_allclose(out.float().cpu().numpy(), oracle(s, run.scale), **O_TOL)
-    # the context is still usable: the same combine with both flags raised completes without error
+    # the context is still usable: the slot's next exchange (tag 2) with both parts completes cleanly
     run.err.zero_()
     run.reduce_slice(0, world=1)
-    run.flags[0, 1] = 1
+    lse1 = run.recv[0, 1, T * H * W:T * H * W + H * T]
+    lse1.copy_(exchange_words(torch.full((H * T,), float('-inf')), 2).to(CUDA))
     out2 = run.combine(0)
     torch.cuda.synchronize()
-    assert int(run.err.item()) == 0
+    assert int(run.err.item()) == 0 and int(run.epochs.item()) == 2
     assert torch.equal(out2, out)
+
+
+def test_stale_tags_are_not_taken():
+    """A part left over from the slot's previous exchange (tag = epoch) is not taken for the current
+    one: with part 1 holding last exchange's words the combine times out on it, exactly as if it were
+    missing."""
+    lib = pkg('_lib')
+    s = build_step(78, 256, [500, 70])
+    run = SplitStep(s, 1, 1)
+    run.N = 2
+    T, W = run.T, run.W
+    run.recv = torch.zeros(1, 2, run.part, dtype=I64, device=CUDA)
+    run.epochs.fill_(4)                                           # this exchange's tag is 5
+    run.recv[0, 1, :T * H * W] = exchange_words(torch.ones(T * H * W), 4).to(CUDA)
+    run.recv[0, 1, T * H * W:T * H * W + H * T] = exchange_words(torch.zeros(H * T), 4).to(CUDA)
+    run.reduce_slice(0, world=1)
+    prev = lib.set_wait_limit_ns(5_000_000)
+    try:
+        out = run.combine(0)
+        torch.cuda.synchronize()
+    finally:
+        lib.set_wait_limit_ns(prev)
+    assert int(run.err.item()) == lib.ERR_WAIT_PEER and int(run.epochs.item()) == 5
+    np.testing.assert_allclose(out.float().cpu().numpy(), oracle(s, run.scale), **O_TOL)
