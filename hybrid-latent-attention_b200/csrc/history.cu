@@ -636,15 +636,17 @@ __global__ void __launch_bounds__(32 * kReduceWarpHeads)
 // [H, T], as exchange words tagged epoch + 1 - is stored straight into every rank's receive slot
 // (peer memory over NVLink, this GPU's own slot included).  The receivers poll the words, so the
 // kernel ends with its stores: no fence, flag or CTA counter.  Launched as a programmatic dependent
-// of the history kernel (griddepcontrol), it lets its own dependent - the combine - start at once,
-// so the combine's window phase overlaps this reduce and its merge consumes each row as it lands.
+// of the history kernel (griddepcontrol), it releases its own dependent - the combine - before it
+// waits for the history grid: the combine's window phase, whose inputs were complete before the
+// history kernel passed its own wait, then overlaps the history's tail and this reduce, and its
+// merge consumes each remote row as it lands.
 template <int W>
 __global__ void __launch_bounds__(kReduceThreads)
     history_reduce_exchange_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
                                    const int2* __restrict__ meta, int stream_mode, int T, int H,
                                    const uint8_t* __restrict__ empty, const ExchangeTargets x) {
-  griddep_wait();
   griddep_launch_dependents();
+  griddep_wait();
   const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   float lse;
   const float4 acc = reduce_row<W>(ws_o, ws_lse, meta, stream_mode, t, h, H, empty, lse);

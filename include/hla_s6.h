@@ -382,7 +382,8 @@ int hla_s6_peer_free(void* ptr);
  * launch_flags: HLA_S6_REDUCE_AFTER_PARTIALS declares that the immediately preceding launch on the
  * stream is the hla_s6_history_partials call that produced the partials (the reduce is then a
  * programmatic dependent of it, and in turn lets a combine launched with
- * HLA_S6_COMBINE_AFTER_PARTIALS start its window phase during the reduce). */
+ * HLA_S6_COMBINE_AFTER_PARTIALS start its window phase while the history kernel and the reduce
+ * finish: that combine's exact-window inputs must come from launches before the history call). */
 #define HLA_S6_REDUCE_AFTER_PARTIALS 1
 int hla_s6_history_reduce_exchange(int32_t num_tokens, int32_t num_heads, int32_t width, int32_t page,
                                    int32_t num_kv_splits, float* workspace, int64_t workspace_floats,
