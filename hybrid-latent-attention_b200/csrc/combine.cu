@@ -30,12 +30,13 @@ struct CombineSmem {
   static constexpr int Q_OFF = OW_OFF + kCTok * 128 * 4;          // float [8 warps][128]
   static constexpr int L_OFF = Q_OFF + 8 * 128 * 4;               // float lse_h[16], lse_w[16]
   static constexpr int QSL_OFF = L_OFF + 2 * kCTok * 4;         // int32 query_start_loc copy
-  static constexpr int BAR_OFF = QSL_OFF + kQslCap * 4;          // mbarrier: all of B[h] landed
+  static constexpr int V_OFF = QSL_OFF + kQslCap * 4;            // per warp: the window's V rows
+  static constexpr int BAR_OFF = V_OFF + kCTok * kWindowVBytes;  // mbarrier: all of B[h] landed
   static constexpr int BYTES = BAR_OFF + 16 + 1024;              // + slack to align the base to 1024 B
 };
 
 template <int W>
-__global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_constant__ CUtensorMap tmap_b,
+__global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_constant__ CUtensorMap tmap_b,
                                                              const CombineParams p) {
   using S = CombineSmem<W>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -79,7 +80,8 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
       o[3] = __bfloat162float(b[1].y);
       lse_w = p.chunk_lse[static_cast<int64_t>(h) * T + t];
     } else if (t < T) {
-      if (!win.ctx_tok && win.window <= 32) window_warp_short(win, t, h, q_s + warp * 128, o, lse_w);
+      if (!win.ctx_tok && win.window <= 32)
+        window_warp_short(win, t, h, q_s + warp * 128, smem + S::V_OFF + warp * kWindowVBytes, o, lse_w);
       else window_warp(win, t, h, q_s + warp * 128, o, lse_w);
     } else {
       o[0] = o[1] = o[2] = o[3] = 0.f;

@@ -21,13 +21,14 @@ __global__ void __launch_bounds__(128) window_kernel(const WindowArgs a, __nv_bf
                                                      int H) {
   __shared__ float q_s[4][128];
   __shared__ int32_t qsl_s[kQslCap];
+  __shared__ __align__(16) uint8_t v_s[4][kWindowVBytes];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x, h = blockIdx.y * 4 + warp;
   WindowArgs w = a;
   if (!a.ctx_tok) w.qsl = stage_qsl(a.qsl, a.R, qsl_s);
   if (h >= H) return;
   float o[4], lse;
-  if (!w.ctx_tok && w.window <= 32) window_warp_short(w, t, h, q_s[warp], o, lse);
+  if (!w.ctx_tok && w.window <= 32) window_warp_short(w, t, h, q_s[warp], v_s[warp], o, lse);
   else window_warp(w, t, h, q_s[warp], o, lse);
   __nv_bfloat16* dst = out + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(h) * o_sh + lane * 4;
   reinterpret_cast<__nv_bfloat162*>(dst)[0] = __floats2bfloat162_rn(o[0], o[1]);

@@ -220,13 +220,17 @@ __device__ __forceinline__ void window_warp(const WindowArgs& a, int t, int h, f
 
 // window_warp for a window of at most 32 history keys (the decode window, W = 32) in two dependent
 // memory rounds instead of one per 16 keys: round 1 fetches q and the block-table entries of every
-// key, round 2 issues all K and V loads at once - lane l's K row (history key first + l) and, for
-// the value accumulation, its 4 dims of every key's V row.  A 33rd key (the current token when the
-// window is full) is scored by the whole warp (4 dims per lane, warp sum).  Same math and key order
-// as window_warp; the current token's dot product is summed across lanes.  Only for the decode
-// mode (ctx_tok unset) with window <= 32.
-__device__ __forceinline__ void window_warp_short(const WindowArgs& a, int t, int h, float* q_s, float (&o)[4],
-                                                  float& lse) {
+// key, round 2 puts every K and V load in flight at once - lane l's K row (history key first + l)
+// into registers and its V row into this warp's shared buffer with cp.async, so the 32 V rows take
+// no registers (held in registers they outgrew what the compiler keeps in flight, and the loads
+// went out in several rounds).  The value accumulation then reads its 4 dims of every key's V row
+// from shared memory.  A 33rd key (the current token when the window is full) is scored by the
+// whole warp (4 dims per lane, warp sum).  Same math and key order as window_warp.  Only for the
+// decode mode (ctx_tok unset) with window <= 32.  v_s: kWindowVBytes of this warp's shared memory,
+// 16-byte aligned; rows are stored with their 16-byte chunks XOR-swizzled by key % 16.
+constexpr int kWindowVBytes = 32 * 256;
+__device__ __forceinline__ void window_warp_short(const WindowArgs& a, int t, int h, float* q_s, uint8_t* v_s,
+                                                  float (&o)[4], float& lse) {
   const int lane = threadIdx.x & 31;
   o[0] = o[1] = o[2] = o[3] = 0.f;
   lse = -INFINITY;
@@ -259,18 +263,19 @@ __device__ __forceinline__ void window_warp_short(const WindowArgs& a, int t, in
     q_s[lane * 4 + 3] = __bfloat162float(b[1].y);
   }
   __syncwarp();
-  // ---- round 2: every K and V load of the window
+  // ---- round 2: every K and V load of the window.  V row of key l -> v_s + 256 l (zeros for a key
+  //      without a row), chunk c at chunk position c ^ (l % 16)
+  {
+    const __nv_bfloat16* vrow = a.cache + (off >= 0 ? off : 0) + 128;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) cp_async16(v_s + lane * 256 + ((c ^ (lane & 15)) << 4), vrow + c * 8, off >= 0 ? 16 : 0);
+    cp_async_commit();
+  }
   uint4 kr[16];
   if (off >= 0) {
     const uint4* kp = reinterpret_cast<const uint4*>(a.cache + off);
 #pragma unroll
     for (int v = 0; v < 16; ++v) kr[v] = __ldg(kp + v);
-  }
-  uint2 vv[32];
-#pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    const int64_t ro = __shfl_sync(0xffffffffu, off, e);
-    vv[e] = ro >= 0 ? __ldg(reinterpret_cast<const uint2*>(a.cache + ro + 128 + lane * 4)) : make_uint2(0u, 0u);
   }
   uint2 kx = make_uint2(0u, 0u), vx = make_uint2(0u, 0u);
   if (offx >= 0) {
@@ -301,15 +306,19 @@ __device__ __forceinline__ void window_warp_short(const WindowArgs& a, int t, in
     part = fmaf(q_s[lane * 4 + 3], __bfloat162float(b[1].y), part);
     scx = warp_sum(part) * a.scale;
   }
+  cp_async_wait<0>();  // this lane's V row has landed
+  __syncwarp();        // ... and every other lane's
   const float mx = fmaxf(warp_max(sc), scx);
   if (mx == -INFINITY) return;
   const float p = sc == -INFINITY ? 0.f : expf(sc - mx);
   const float px = scx == -INFINITY ? 0.f : expf(scx - mx);
   const float l = warp_sum(p) + px;
+  const int vchunk = lane >> 1, vhalf = (lane & 1) * 8;  // dims 4 lane .. + 3 of a V row
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const float pw = __shfl_sync(0xffffffffu, p, e);
-    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&vv[e]);
+    const uint2 vv = *reinterpret_cast<const uint2*>(v_s + e * 256 + ((vchunk ^ (e & 15)) << 4) + vhalf);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&vv);
     o[0] = fmaf(pw, __bfloat162float(b[0].x), o[0]);
     o[1] = fmaf(pw, __bfloat162float(b[0].y), o[1]);
     o[2] = fmaf(pw, __bfloat162float(b[1].x), o[2]);
