@@ -132,7 +132,7 @@ int hla_s6_latent_query(const void* q_pre, int64_t q_stride_t, int64_t q_stride_
   return hla_s6_decode_prepare(q_pre, q_stride_t, q_stride_h, A, a_stride_h, a_stride_k, positions, table,
                                table_stride, max_position, out, out_stride_t, out_stride_h, num_tokens, num_heads,
                                head_dim, width, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0, 0, nullptr, 0,
-                               0, 0, 0, 0, nullptr, 0, 0, nullptr, 0, nullptr, stream);
+                               0, 0, 0, 0, nullptr, 0, 0, nullptr, 0, nullptr, 0, stream);
 }
 
 int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A,
@@ -145,7 +145,7 @@ int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_strid
                           void* cache, int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
                           int64_t cache_stride_row, int32_t page, const int32_t* block_table,
                           int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
-                          int32_t num_reqs, int64_t* slot_out, void* stream) {
+                          int32_t num_reqs, int64_t* slot_out, int32_t flags, void* stream) {
   if (head_dim != 128 || (width != 256 && width != 512 && width != 1024)) {
     set_error("latent query needs head_dim 128 and width 256, 512 or 1024 (got %d, %d)", head_dim, width);
     return kStatusInvalid;
@@ -204,6 +204,7 @@ int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_strid
   p.qsl = query_start_loc;
   p.R = num_reqs;
   p.slot_out = slot_out;
+  p.pdl = (flags & HLA_S6_PREPARE_EARLY_LAUNCH) != 0;
   return prepare(p, static_cast<cudaStream_t>(stream));
 }
 

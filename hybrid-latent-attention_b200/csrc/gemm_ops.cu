@@ -153,8 +153,10 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
   const int x = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * 64;
   constexpr int HALF = W / 2;
   // a history split launched as this grid's programmatic dependent may start streaming pages now;
-  // it reads q_lat only after this grid has completed
+  // it reads q_lat only after this grid has completed.  Launched early itself (PrepareParams::pdl),
+  // this grid touches memory only once the launch before it has completed.
   if (tid == 0) griddep_launch_dependents();
+  griddep_wait();
   if (x >= W / 64) {
     const int32_t* qsl = stage_qsl(p.qsl, p.R, reinterpret_cast<int32_t*>(qs));  // q tile unused here
     // ---------------- exact part: 16 tokens of head h per CTA; thread = (token, 8 rotation pairs)
@@ -275,13 +277,23 @@ int prepare(const PrepareParams& p, cudaStream_t s) {
   if (p.T == 0) return kStatusOk;
   const int extra = p.k ? 4 : 0;  // exact-part CTAs per (head, 64-token block): 16 tokens each
   dim3 grid(p.W / 64 + extra, p.H, (p.T + 63) / 64);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.pdl ? 1 : 0;
+  cudaError_t e;
   switch (p.W) {
-    case 256: prepare_kernel<256><<<grid, 128, 0, s>>>(p); break;
-    case 512: prepare_kernel<512><<<grid, 128, 0, s>>>(p); break;
-    case 1024: prepare_kernel<1024><<<grid, 128, 0, s>>>(p); break;
+    case 256: e = cudaLaunchKernelEx(&cfg, prepare_kernel<256>, p); break;
+    case 512: e = cudaLaunchKernelEx(&cfg, prepare_kernel<512>, p); break;
+    case 1024: e = cudaLaunchKernelEx(&cfg, prepare_kernel<1024>, p); break;
     default: set_error("latent query width %d unsupported (256, 512, 1024)", p.W); return kStatusInvalid;
   }
-  return cuda_status(cudaGetLastError(), "prepare_kernel launch");
+  return cuda_status(e, "prepare_kernel launch");
 }
 
 }  // namespace hla

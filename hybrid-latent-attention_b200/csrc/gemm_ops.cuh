@@ -60,6 +60,7 @@ struct PrepareParams {
   const int32_t* qsl;
   int R;
   int64_t* slot_out;
+  bool pdl;  // launch as a programmatic dependent of the preceding launch (the kernel waits for it)
 };
 
 int writer(const WriterParams& p, cudaStream_t s);

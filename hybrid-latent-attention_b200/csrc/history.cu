@@ -119,19 +119,13 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     __syncthreads();
     P = pref[T];
     G = p.grid < P ? static_cast<int64_t>(p.grid) : P;
-    if (blockIdx.x == 0) {
-      for (int t = tid; t < T; t += blockDim.x) {
-        const int a = pref[t], b = pref[t + 1];
-        int2 m = make_int2(0, 0);
-        if (b > a) {
-          const int lo = static_cast<int>(stream_owner(a, P, G)) + t;
-          const int hi = static_cast<int>(stream_owner(b - 1, P, G)) + t + 1;
-          m = make_int2(lo, hi);
-        }
-        p.meta[t] = m;
+    if (static_cast<int64_t>(blockIdx.x) >= G) {
+      if (blockIdx.x == 0) {  // no pages at all: every row's slot range is empty
+        griddep_wait();
+        for (int t = tid; t < T; t += blockDim.x) p.meta[t] = make_int2(0, 0);
       }
+      return;
     }
-    if (static_cast<int64_t>(blockIdx.x) >= G) return;
     p0 = stream_start(blockIdx.x, P, G);
     p1 = stream_start(blockIdx.x + 1, P, G);
     int lo = 0, hi = T;  // largest r with pref[r] <= p0
@@ -222,6 +216,20 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
   // its own wait) start on the SMs this grid frees.  Both are no-ops for an ordinary launch.
   griddep_wait();
   if (tid == 0) griddep_launch_dependents();
+  if (p.stream_mode && blockIdx.x == 0) {
+    // each row's slot range, written only after the wait: until the launch this grid waited for has
+    // completed, a combine before it may still be reading the workspace
+    for (int t = tid; t < T; t += NC * 32) {
+      const int a = pref[t], b = pref[t + 1];
+      int2 m = make_int2(0, 0);
+      if (b > a) {
+        const int lo = static_cast<int>(stream_owner(a, P, G)) + t;
+        const int hi = static_cast<int>(stream_owner(b - 1, P, G)) + t + 1;
+        m = make_int2(lo, hi);
+      }
+      p.meta[t] = m;
+    }
+  }
   const int g8 = lane >> 2, c4 = lane & 3;
   const int col0 = warp * 128;  // first latent column owned by this warp
   uint32_t qa[8][4];

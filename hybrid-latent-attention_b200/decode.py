@@ -321,7 +321,8 @@ class S6DecodeModel:
                   qr.stride(0), qr.stride(1), _lib.ptr(k), k.stride(0), k.stride(1), _lib.ptr(v), v.stride(0),
                   v.stride(1), _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(ex),
                   ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
-                  self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, None, stream)
+                  self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, None,
+                  _lib.PREPARE_EARLY_LAUNCH if self.pdl else 0, stream)
         # 2b. (window_overlap) exact window on a side stream, beside the history kernel (it needs prepare's
         #     q_rope and appended row only); the combine then takes it as its external exact part.  Measured
         #     slower than the window inside the combine (config 2: 18.3 vs 17.2 ms per step), so off by default

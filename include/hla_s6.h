@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define HLA_S6_ABI_VERSION 2
+#define HLA_S6_ABI_VERSION 3
 #define HLA_S6_OK 0
 #define HLA_S6_EINVAL 1
 #define HLA_S6_EOVERFLOW 2
@@ -270,7 +270,13 @@ int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const v
  * q_rope = exact neox RoPE of q_pre (a separate output; q_pre is not modified) plus the
  * exact-cache append of RoPE(k) | v as hla_s6_exact_append (slot_out optional).
  * Replaces s6_layer.py:82-84 latent_query + the model rotary_emb + unified_kv_cache_update at
- * hla/vllm_latent/ouro_latent.py:112-123.  q_pre, A and latent-table rows must be 16-byte aligned. */
+ * hla/vllm_latent/ouro_latent.py:112-123.  q_pre, A and latent-table rows must be 16-byte aligned.
+ * flags: HLA_S6_PREPARE_EARLY_LAUNCH launches the prepare as a programmatic dependent of the
+ * preceding launch on the stream: its CTAs are staged before that launch completes and wait for it
+ * before they read or write memory, which hides the launch gap.  A history split launched after it
+ * with HLA_S6_PARTIALS_AFTER_QUERY may then start streaming before that preceding launch has
+ * completed, so the block table and ctx the split reads must not be written by it. */
+#define HLA_S6_PREPARE_EARLY_LAUNCH 1
 int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A,
                           int64_t a_stride_h, int64_t a_stride_k, const int64_t* positions, const void* table,
                           int64_t table_stride, int64_t max_position, void* q_lat, int64_t q_lat_stride_t,
@@ -281,7 +287,7 @@ int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_strid
                           void* cache, int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_head,
                           int64_t cache_stride_row, int32_t page, const int32_t* block_table,
                           int64_t block_table_stride, int32_t max_blocks, const int32_t* query_start_loc,
-                          int32_t num_reqs, int64_t* slot_out, void* stream);
+                          int32_t num_reqs, int64_t* slot_out, int32_t flags, void* stream);
 
 /* Writer projection: reg_out = bf16(reg_in + bf16(h . weight^T)) (reg_in may be NULL), weight
  * [out_features, in_features] as nn.Linear; in_features % 128 == 0, out_features % 16 == 0.

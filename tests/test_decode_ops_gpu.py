@@ -335,7 +335,7 @@ def test_decode_prepare_fuses_latent_query_and_exact_append():
              lib.ptr(kd), kd.stride(0), kd.stride(1), lib.ptr(vd), vd.stride(0), vd.stride(1), lib.ptr(cos_sin),
              cos_sin.stride(0), cos_sin.shape[0], lib.ptr(logical), nb, logical.stride(0), logical.stride(1),
              logical.stride(2), page, lib.ptr(btd), btd.stride(0), btd.shape[1], lib.ptr(qsl), R, lib.ptr(slots),
-             lib.stream_of(qd))
+             lib.PREPARE_EARLY_LAUNCH, lib.stream_of(qd))   # staged early behind the torch ops above
     torch.cuda.synchronize()
     assert torch.equal(qd, q_before)   # q_pre is read only
     np.testing.assert_allclose(q_lat.float().cpu().numpy(), orc.latent_query(q, A, pos, ltab.float().cpu().numpy()),
