@@ -553,9 +553,10 @@ class FullStep:
     after each loop the final RMSNorm.  Dense weights are random-init bf16 on cuBLAS (torch); they are
     not this repository's kernels and are read from HBM every step (about 9.8 GB)."""
 
-    def __init__(self, model, seed, intermediate=5632, eps=1e-6):
+    def __init__(self, model, seed, intermediate=5632, eps=1e-6, dropin=False):
         import torch
         self.torch, self.m, self.eps, self.I = torch, model, eps, intermediate
+        self.dropin = dropin
         s, B, dev = model.s, model.B, model.device
         D = s.hidden
         g = torch.Generator(device=dev).manual_seed(seed + 7)
@@ -568,6 +569,18 @@ class FullStep:
         self.out = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
         self.attn = torch.empty(B, s.heads, s.head_dim, dtype=torch.bfloat16, device=dev)
         self.side = torch.cuda.Stream(dev)
+        if dropin:
+            # the drop-in path: the adapter's per-layer attention (ouro_attention.LatentAttention, a mirror of
+            # OuroLatentAttention.forward) over the model's own caches, with a reference-style StepContext
+            oa = importlib.import_module(f'{PKG}.ouro_attention')
+            lay = importlib.import_module(f'{PKG}.s6_layer')
+            ops = importlib.import_module(f'{PKG}.s6_ops')
+            self.mods = [oa.LatentAttention(model.layers[l], self.w[l]['qkv'], self.w[l]['o'], model.cos_sin, s.window)
+                         for l in range(s.layers)]
+            self.caches = [oa.PagedCaches(model.main[l], model.l1[l], model.latent_table, model.exact[l],
+                                          model.exact_table) for l in range(s.layers)]
+            self.sctx = lay.StepContext(model.positions, model.qsl, model.seq_lens, 1, B, model.tables, model.scale,
+                                        ops.B200_BACKENDS, model.workspace, model.splits, window=s.window)
 
     def weight_bytes_per_step(self):
         per_layer = sum(v.numel() * v.element_size() for v in self.w[0].values())
@@ -583,12 +596,23 @@ class FullStep:
         stream = pkg_lib().stream_of(self.out)
         wstream = pkg_lib().ctypes.c_void_p(self.side.cuda_stream)
         hidden = self.x0
+        states = [None] * s.layers
         for loop in range(s.loops):
             residual = None
             for layer in range(s.layers):
                 W = self.w[layer]
                 residual = hidden if residual is None else hidden + residual
                 h = self._rms(residual, W['n1'])
+                if self.dropin:
+                    o, states[layer] = self.mods[layer].forward(m.positions, h, loop, states[layer], self.sctx,
+                                                                self.caches[layer])
+                    x = self._rms(o, W['n2'])
+                    residual = x + residual
+                    x = self._rms(residual, W['n3'])
+                    gu = F.linear(x, W['gate_up'])
+                    x = F.linear(F.silu(gu[:, :self.I]) * gu[:, self.I:], W['down'])
+                    hidden = self._rms(x, W['n4'])
+                    continue
                 qkv = F.linear(h, W['qkv'])
                 q, k, v = (x.view(B, s.heads, s.head_dim) for x in qkv.split(D, -1))
                 self.side.wait_stream(main)               # the writer reads h
@@ -602,7 +626,8 @@ class FullStep:
                 hidden = self._rms(x, W['n4'])
             hidden = self._rms(hidden + residual, self.final)
         self.out.copy_(hidden)
-        main.wait_stream(self.side)
+        if not self.dropin:
+            main.wait_stream(self.side)
 
     def capture(self):
         torch = self.torch
@@ -639,7 +664,16 @@ def run_full(args):
     ctx, scaling, _, max_pos = config_batch(2, rank, world, args.seed)
     model = dec.S6DecodeModel(dec.OuroShape(max_position=max_pos), dec.DecodeBatch(ctx), device='cuda',
                               seed=args.seed + rank)
-    full = FullStep(model, args.seed + rank)
+    native_ms = None
+    if args.dropin:
+        # the native step of the same build first, on the same model and weights, for comparison
+        native = FullStep(model, args.seed + rank)
+        ngraph = native.capture()
+        for _ in range(args.warmup):
+            ngraph.replay()
+        native_ms = time_graph(torch, ngraph, args.steps, dist) / args.steps
+        del ngraph
+    full = FullStep(model, args.seed + rank, dropin=args.dropin)
     full.step()
     torch.cuda.synchronize()
     graph = full.capture()
@@ -684,7 +718,10 @@ def run_full(args):
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded), random-init weights',
             'config': {'workload': 'BASELINE config 2: whole Ouro-1.4B-shaped S6 decode step - the dense body '
                                    '(RMSNorms, QKV / O projections, SiLU MLP 5632; torch/cuBLAS bf16) around the B200 '
-                                   'attention path, 24 layers x 4 loops, one CUDA graph',
+                                   'attention path, 24 layers x 4 loops, one CUDA graph' +
+                                   ('; attention through the drop-in mirror of the adapter\'s per-layer path '
+                                    '(ouro_attention.LatentAttention over s6_layer.StepContext / attend, as '
+                                    'hla/vllm_latent/ouro_latent.py:106-131 calls them)' if args.dropin else ''),
                        'global_batch': tokens_all, 'batch_per_gpu': len(ctx), 'ctx': max(ctx), 'seq_len': max(ctx) + 1,
                        'parallelism': f'request-partitioned x{world} (no collectives)',
                        'l2': 'inputs larger than L2 (latent caches ~40 GB, dense weights 2.5 GB per GPU), no flush'},
@@ -701,6 +738,14 @@ def run_full(args):
                     'path': 'FullStep graph: input embeddings copied in from pinned memory, final hidden states out'},
             'gpu_launches': model.launches_per_step() * args.steps,
             'clocks': clocks}
+        if args.dropin:
+            line['native_step'] = {'ms_per_step': native_ms, 'value': tokens_all / (native_ms / 1e3),
+                                   'note': 'the same step with the attention through S6DecodeModel.layer_loop '
+                                           '(writer on a forked branch, prepare, history split, combine)'}
+            # per (layer, loop): writer, latent query, exact RoPE + append, history split, combine; plus the
+            # row commits at loops 0 and 3
+            sh = model.s
+            line['gpu_launches'] = (5 * sh.layers * sh.loops + 2 * sh.layers) * args.steps
         print(json.dumps(line), flush=True)
     del graph
     import gc
@@ -1280,6 +1325,8 @@ def main():
     ap.add_argument('--exchange', default='peer', choices=['peer', 'nccl'],
                     help='config 5 on several GPUs: how the (z, lse) parts move')
     ap.add_argument('--no-cpu', action='store_true', help='skip the CPU baseline leg')
+    ap.add_argument('--dropin', action='store_true',
+                    help='--config full: run the attention through the drop-in mirror of the adapter (ouro_attention)')
     prof = ap.add_argument_group('profiler workloads (--profile CASE; no JSON line, for ncu)')
     prof.add_argument('--profile', choices=['decode', 'prefill', 'seq-split', 'contig', 'heads', 'export'])
     prof.add_argument('--profile-steps', type=int, default=2, help='eager steps of the profiled workload')
