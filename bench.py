@@ -119,7 +119,8 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms during the timed region (the first sample is
+    taken just before it starts)."""
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
@@ -134,10 +135,20 @@ class ClockSampler:
         try:
             self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
             self.proc = subprocess.Popen(['nvidia-smi', '-i', self.gpu, f'--query-gpu={self.FIELDS}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=self.file,
+                                          '--format=csv,noheader,nounits', '-lms', '100'], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a while to start: wait (up to 3 s) for its first sample, so that a timed region
+        # shorter than the sampling period still has samples around it
+        import time
+        deadline = time.time() + 3
+        while time.time() < deadline and self.proc.poll() is None:
+            self.file.flush()
+            if Path(self.file.name).stat().st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
