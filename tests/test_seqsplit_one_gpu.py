@@ -261,3 +261,39 @@ def test_stale_tags_are_not_taken():
         lib.set_wait_limit_ns(prev)
     assert int(run.err.item()) == lib.ERR_WAIT_PEER and int(run.epochs.item()) == 5
     np.testing.assert_allclose(out.float().cpu().numpy(), oracle(s, run.scale), **O_TOL)
+
+
+def test_one_rank_peer_exchange_step_matches_the_plain_step(tmp_path):
+    """The model's peer-exchange step on one rank (world 1): the reduce stores its part as exchange
+    words into this GPU's region and releases the combine early, the combine polls the words - the
+    programmatic-launch chain of a real sequence split, without a second GPU.  Eagerly and over two
+    graph replays (every slot reused), its output matches the plain step (partials merged directly
+    in the combine) within the output tolerance, and every slot's epoch advances once per step."""
+    import torch.distributed as dist
+    dec = pkg('decode')
+    dist.init_process_group('gloo', init_method=f'file://{tmp_path / "rdv"}', rank=0, world_size=1)
+    try:
+        shape = dec.OuroShape(layers=2)
+        ctx = [3000, 40, 8192, 700]
+        plain = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device=CUDA, seed=3)
+        split = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device=CUDA, seed=3,
+                                  exchange=(0, 1, dist.group.WORLD))
+        try:
+            plain.step()
+            split.step()
+            torch.cuda.synchronize()
+            torch.testing.assert_close(split.out.float(), plain.out.float(), **O_TOL)
+            graph = split.capture()
+            for _ in range(2):
+                split.out.zero_()
+                graph.replay()
+                torch.cuda.synchronize()
+                torch.testing.assert_close(split.out.float(), plain.out.float(), **O_TOL)
+            epochs = split.x_counters.view(-1, 2).cpu()
+            steps = int(epochs[0, 0])
+            assert steps >= 3 and (epochs[:, 0] == steps).all() and (epochs[:, 1] == 0).all()
+            del graph
+        finally:
+            split.close_exchange()
+    finally:
+        dist.destroy_process_group()
