@@ -118,7 +118,11 @@ def history_attention(q, cache, block_table, ctx, scale, dt=np.float64):
             continue
         pages = -(-n // page)
         ids = np.asarray(block_table[t, :pages], dtype=np.int64)
-        rows = np.take(cache[:, 0], ids, axis=0).reshape(pages * page, 2 * W)[:n].astype(dt, copy=False)
+        if pages > 1 and ids[0] >= 0 and np.array_equal(ids, ids[0] + np.arange(pages)):
+            block = cache[ids[0]:ids[0] + pages, 0]               # consecutive blocks: a view, no gather copy
+        else:
+            block = np.take(cache[:, 0], ids, axis=0)
+        rows = block.reshape(pages * page, 2 * W)[:n].astype(dt, copy=False)
         s = (q[t] @ rows[:, :W].T) * dt(scale)                    # [H, n]
         m = s.max(-1, keepdims=True)
         e = np.exp(s - m)
