@@ -18,8 +18,15 @@
 //    lengths balance across the 148 SMs; each CTA emits one fp32 partial (o, lse) per row
 //    segment it touched into the caller's workspace.  CTA c writes row t's partial at slot
 //    c + t, and CTA 0 records each row's slot range in `meta`.
+//  * tail stealing (the STEAL kernel, for steps with about as many rows as CTAs): the last eighth
+//    of every CTA's range goes to a shared pool that CTAs drain once their own part is done, so
+//    CTAs slowed by the memory system finish with the others.  Units - a CTA's main part, or a
+//    tail - keep fixed partial slots (unit u, row t: slot u + t), so the result does not depend
+//    on which CTA ran a unit.
 //  * a reduce kernel (the Triton stage-2 equivalent) or the fused decode combine turns the
 //    partials into the op outputs.
+#include <mutex>
+
 #include "common.cuh"
 #include "hla_s6_internal.h"
 
@@ -48,6 +55,9 @@ struct HistoryParams {
   int32_t contig_n;
   const uint8_t* mask;  // [rows, N], nonzero = visible
   int64_t mask_st;
+  // paged stream mode: [0] tail ticket, [1] CTAs done; zero between launches (the last CTA of a
+  // launch re-zeroes them).  NULL: every CTA keeps its whole page range (no tail stealing).
+  unsigned* steal;
 };
 
 template <int W, int PG>
@@ -75,7 +85,7 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t v, int key_lo, int valid)
 // `tmap` covers K [rows, N, W] and `tmap_v` V, both as (64, N, W/64, rows) boxes of PG keys, so a
 // tile lands in shared memory exactly as a page of the paged cache does (K slabs, then V slabs);
 // rows have p.contig_n keys and a per-key mask instead of a prefix length.
-template <int W, int PG, bool CONTIG = false>
+template <int W, int PG, bool CONTIG = false, bool STEAL = false>
 __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>::MIN_CTAS)
     history_split_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_v,
                          const HistoryParams p) {
@@ -85,15 +95,19 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
   float4* xbuf = reinterpret_cast<float4*>(smem + STAGES * C::PAGE_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::PAGE_BYTES + C::XBUF_BYTES);
+  // per stage: row, local page, slot, flags (16-byte aligned: it follows the 16-byte multiples above)
+  int4* smeta = reinterpret_cast<int4*>(smem + STAGES * C::PAGE_BYTES + C::XBUF_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smeta + STAGES);
   uint64_t* empty = full + STAGES;
-  int* misc = reinterpret_cast<int*>(empty + STAGES);  // [0]=abort
+  uint64_t* mready = empty + STAGES;                   // per stage: its descriptor is written
+  int* misc = reinterpret_cast<int*>(mready + STAGES);  // [0]=abort
   int* pref = misc + 4;                                 // [T+1] page prefix (stream mode)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = p.T;
   int64_t P = 0, G = 1, p0 = 0, p1 = 0;
   int row0 = 0;
+  bool steal_on = false;
 
   if (p.stream_mode) {
     for (int t = tid; t < T; t += blockDim.x) {
@@ -119,6 +133,9 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     __syncthreads();
     P = pref[T];
     G = p.grid < P ? static_cast<int64_t>(p.grid) : P;
+    // tail stealing needs at least 16 pages per CTA (so that both units of a CTA are non-empty) and
+    // room for 2 G + T - 1 partial slots; the same decision in every CTA
+    steal_on = STEAL && !CONTIG && p.steal != nullptr && P >= 16 * G && 2 * G + T - 1 <= p.slots_cap;
     if (static_cast<int64_t>(blockIdx.x) >= G) {
       if (blockIdx.x == 0) {  // no pages at all: every row's slot range is empty
         griddep_wait();
@@ -151,6 +168,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
+      mbar_init(&mready[s], 1);
     }
     fence_barrier_init();
     fence_proxy_async();
@@ -167,6 +185,23 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       n = static_cast<int>(p1);
     }
   };
+  // Work units of the stream mode.  Without stealing, unit c is CTA c's page range.  With it, CTA c's
+  // range [s0, s1) is cut into its main unit 2c, [s0, s1 - (s1 - s0) / 8), which CTA c streams, and its
+  // tail unit 2c + 1, the last eighth, which any CTA that has finished its main unit may take from the
+  // shared pool.  A row's partial from unit u goes to slot u + row, whichever CTA ran the unit.
+  auto cta_mid = [&](int64_t c) {
+    const int64_t s0 = stream_start(c, P, G), s1 = stream_start(c + 1, P, G);
+    return s1 - (s1 - s0) / 8;
+  };
+  auto unit_start = [&](int64_t u) -> int64_t {
+    if (!steal_on) return stream_start(u, P, G);
+    return (u & 1) ? cta_mid(u >> 1) : stream_start(u >> 1, P, G);
+  };
+  auto unit_owner = [&](int64_t pg) -> int64_t {
+    const int64_t c = stream_owner(pg, P, G);
+    if (!steal_on) return c;
+    return 2 * c + (pg >= cta_mid(c) ? 1 : 0);
+  };
 
   if (warp == NC) {
     // ------------------------------------------------------------ producer
@@ -175,34 +210,101 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       // pages are read once: evict them from L2 first, so that what the step reads again - the partials,
       // the combine's up-projection and window rows - stays resident
       const uint64_t stream_policy = l2_policy_evict_first();
-      int r = row0, base, n;
-      row_pages_base(r, base, n);
-      int it = 0;
-      for (int64_t g = p0; g < p1; ++g, ++it) {
-        while (g >= base + n) {
-          ++r;
-          row_pages_base(r, base, n);
-        }
-        const int lp = static_cast<int>(g - base);
-        const int s = it % STAGES;
-        if (it >= STAGES) {
-          if (!mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, p.wait_ns)) {
-            record_error(p.err, kErrWaitEmpty);
-            atomicExch(&misc[0], 1);
-            break;
+      if constexpr (CONTIG || !STEAL) {
+        // this CTA's own page range, walked the same way by the consumers
+        int r = row0, base, n;
+        row_pages_base(r, base, n);
+        int it = 0;
+        for (int64_t g = p0; g < p1; ++g, ++it) {
+          while (g >= base + n) {
+            ++r;
+            row_pages_base(r, base, n);
+          }
+          const int lp = static_cast<int>(g - base);
+          const int s = it % STAGES;
+          if (it >= STAGES) {
+            if (!mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, p.wait_ns)) {
+              record_error(p.err, kErrWaitEmpty);
+              atomicExch(&misc[0], 1);
+              break;
+            }
+          }
+          mbar_arrive_expect_tx(&full[s], C::PAGE_BYTES);
+          if constexpr (CONTIG) {
+            // keys [lp * PG, lp * PG + PG) of row r; keys past N arrive zero-filled
+            tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, lp * PG, 0, r);
+            tma_load_4d(stages + s * C::PAGE_BYTES + (W / 64) * C::SLAB_BYTES, &tmap_v, &full[s], 0, lp * PG, 0, r);
+          } else {
+            const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
+            // a page outside the table or the cache loads as zeros (TMA out-of-range fill): never a read
+            // outside the buffers, but the caller learns of it through the error word
+            if (blk < 0 || blk >= p.num_blocks) record_error(p.err, kErrBlock);
+            tma_load_4d_hint(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk, stream_policy);
           }
         }
-        mbar_arrive_expect_tx(&full[s], C::PAGE_BYTES);
-        if constexpr (CONTIG) {
-          // keys [lp * PG, lp * PG + PG) of row r; keys past N arrive zero-filled
-          tma_load_4d(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, lp * PG, 0, r);
-          tma_load_4d(stages + s * C::PAGE_BYTES + (W / 64) * C::SLAB_BYTES, &tmap_v, &full[s], 0, lp * PG, 0, r);
-        } else {
-          const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
-          // a page outside the table or the cache loads as zeros (TMA out-of-range fill): never a read
-          // outside the buffers, but the caller learns of it through the error word
-          if (blk < 0 || blk >= p.num_blocks) record_error(p.err, kErrBlock);
-          tma_load_4d_hint(stages + s * C::PAGE_BYTES, &tmap, &full[s], 0, 0, 0, blk, stream_policy);
+      } else {
+        // tail stealing: units of pages, each page announced to the consumers by its stage descriptor
+        int it = 0;
+        bool aborted = false;
+        int64_t unit = p.stream_mode ? (steal_on ? 2 * static_cast<int64_t>(blockIdx.x) : blockIdx.x) : 0;
+        for (;;) {
+          int64_t u0 = 0, u1 = p1;
+          int r = row0;
+          if (p.stream_mode) {
+            u0 = unit_start(unit);
+            u1 = unit_start(unit + 1);
+            int lo = 0, hi = T;  // the row holding page u0: largest r with pref[r] <= u0
+            while (hi - lo > 1) {
+              const int mid = (lo + hi) >> 1;
+              if (pref[mid] <= u0) lo = mid; else hi = mid;
+            }
+            r = lo;
+          }
+          int base, n;
+          row_pages_base(r, base, n);
+          for (int64_t g = u0; g < u1; ++g, ++it) {
+            while (g >= base + n) {
+              ++r;
+              row_pages_base(r, base, n);
+            }
+            const int lp = static_cast<int>(g - base);
+            const int st = it % STAGES;
+            if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, p.wait_ns)) {
+              record_error(p.err, kErrWaitEmpty);
+              atomicExch(&misc[0], 1);
+              aborted = true;
+              break;
+            }
+            const int flags = ((g == u0 || lp == 0) ? 1 : 0) | ((g + 1 == u1 || lp + 1 == n) ? 2 : 0);
+            smeta[st] = make_int4(r, lp, p.stream_mode ? static_cast<int>(unit) + r : r, flags);
+            mbar_arrive(&mready[st]);
+            mbar_arrive_expect_tx(&full[st], C::PAGE_BYTES);
+            const int blk = lp < p.max_blocks ? p.block_table[static_cast<int64_t>(r) * p.bt_st + lp] : -1;
+            // a page outside the table or the cache loads as zeros (TMA out-of-range fill): never a read
+            // outside the buffers, but the caller learns of it through the error word
+            if (blk < 0 || blk >= p.num_blocks) record_error(p.err, kErrBlock);
+            tma_load_4d_hint(stages + st * C::PAGE_BYTES, &tmap, &full[st], 0, 0, 0, blk, stream_policy);
+          }
+          if (aborted || !steal_on) break;
+          const unsigned ticket = atomicAdd(&p.steal[0], 1u);
+          if (ticket >= static_cast<unsigned>(G)) break;
+          unit = 2 * static_cast<int64_t>(ticket) + 1;
+        }
+        if (!aborted) {
+          // end of this CTA's work: a descriptor without a page, completing the stage's phase
+          const int st = it % STAGES;
+          if (it < STAGES || mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, p.wait_ns)) {
+            smeta[st] = make_int4(-1, 0, 0, 0);
+            mbar_arrive(&mready[st]);
+            mbar_arrive(&full[st]);
+          } else {
+            record_error(p.err, kErrWaitEmpty);
+          }
+        }
+        // the last CTA out re-zeroes the pool for the next launch (every CTA has drawn its last ticket)
+        if (steal_on && atomicAdd(&p.steal[1], 1u) == static_cast<unsigned>(G) - 1) {
+          atomicExch(&p.steal[0], 0u);
+          atomicExch(&p.steal[1], 0u);
         }
       }
     }
@@ -223,8 +325,8 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       const int a = pref[t], b = pref[t + 1];
       int2 m = make_int2(0, 0);
       if (b > a) {
-        const int lo = static_cast<int>(stream_owner(a, P, G)) + t;
-        const int hi = static_cast<int>(stream_owner(b - 1, P, G)) + t + 1;
+        const int lo = static_cast<int>(unit_owner(a)) + t;
+        const int hi = static_cast<int>(unit_owner(b - 1)) + t + 1;
         m = make_int2(lo, hi);
       }
       p.meta[t] = m;
@@ -243,13 +345,36 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
   bool seg_open = false;
   int ctx_r = 0;
 
-  for (int64_t g = p0; g < p1; ++g, ++it) {
-    while (g >= base + n) {
-      ++r;
-      row_pages_base(r, base, n);
+  for (int64_t g = p0;; ++g, ++it) {
+    const int s = it % STAGES;
+    int lp = 0, slot = 0;
+    bool seg_start, seg_end, stop = false;
+    if constexpr (CONTIG || !STEAL) {
+      if (g >= p1) break;  // the same in every consumer warp
+      while (g >= base + n) {
+        ++r;
+        row_pages_base(r, base, n);
+      }
+      lp = static_cast<int>(g - base);
+      seg_start = !seg_open;
+      seg_end = (g + 1 == p1) || (lp + 1 == n);
+      slot = p.stream_mode ? static_cast<int>(blockIdx.x) + r : r;
+    } else {
+      // the page's descriptor (its row, local page, partial slot and segment flags) or the end mark
+      const bool ok_m = mbar_wait(&mready[s], (it / STAGES) & 1, p.wait_ns);
+      const int4 m = ok_m ? smeta[s] : make_int4(-1, 0, 0, 0);
+      if (!ok_m) {
+        record_error(p.err, kErrWaitFull);
+        misc[1] = 1;
+      }
+      stop = m.x < 0;
+      if (!stop) r = m.x;
+      lp = m.y;
+      slot = m.z;
+      seg_start = !stop && (m.w & 1);
+      seg_end = !stop && (m.w & 2);
     }
-    const int lp = static_cast<int>(g - base);
-    if (!seg_open) {
+    if (seg_start) {
       seg_open = true;
       ctx_r = CONTIG ? p.contig_n : max(p.ctx[r], 0);
       const __nv_bfloat16* qr = p.q + static_cast<int64_t>(r) * p.q_st;
@@ -271,7 +396,6 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       m_run[0] = m_run[1] = -INFINITY;
       l_run[0] = l_run[1] = 0.f;
     }
-    const int s = it % STAGES;
     // contiguous mode: visibility of this thread's score keys (j * 8 + 2 c4 + e), fetched before the
     // tile wait so the loads overlap it
     uint32_t vis = 0xffffffffu;
@@ -293,7 +417,7 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       misc[1] = 1;
     }
     const uint32_t sbase = smem_u32(stages + s * C::PAGE_BYTES);
-    const int valid = min(PG, ctx_r - lp * PG);
+    const int valid = stop ? 0 : min(PG, ctx_r - lp * PG);
 
     // ---- partial scores over this warp's 128 columns
     float sc[NT][4];
@@ -330,9 +454,11 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
         }
       }
       buf ^= 1;
-      if (misc[1]) break;  // uniform across consumer warps: every setter wrote it before this barrier
+      // uniform across consumer warps: every setter wrote misc[1] before this barrier, and every warp
+      // read the same descriptor (a warp whose wait ran out took it as the end and set misc[1])
+      if (misc[1] || stop) break;
     } else {
-      if (misc[1]) break;
+      if (misc[1] || stop) break;
     }
 
     // ---- online softmax (log2 domain); keys >= valid are masked
@@ -406,7 +532,6 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
     if (lane == 0) mbar_arrive(&empty[s]);
 
     // ---- segment end: write the normalised partial and its lse
-    const bool seg_end = (g + 1 == p1) || (lp + 1 == n);
     if (seg_end) {
       seg_open = false;
       float l0 = l_run[0], l1 = l_run[1];
@@ -414,7 +539,6 @@ __global__ void __launch_bounds__(HistoryCfg<W, PG>::THREADS, HistoryCfg<W, PG>:
       l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
       l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-      const int slot = p.stream_mode ? static_cast<int>(blockIdx.x) + r : r;
       if (slot >= p.slots_cap) {
         record_error(p.err, kErrSlots);
       } else {
@@ -682,8 +806,53 @@ __global__ void __launch_bounds__(kReduceThreads)
 template <int W, int PG>
 size_t history_smem_bytes(int T) {
   using C = HistoryCfg<W, PG>;
-  return 1024 + static_cast<size_t>(C::STAGES) * C::PAGE_BYTES + C::XBUF_BYTES + 2 * C::STAGES * 8 + 16 +
-         4 * (static_cast<size_t>(T) + 1);
+  // stages, score exchange, full / empty / descriptor-ready barriers, stage descriptors, misc, prefix
+  return 1024 + static_cast<size_t>(C::STAGES) * C::PAGE_BYTES + C::XBUF_BYTES + 3 * C::STAGES * 8 +
+         16 * C::STAGES + 16 + 4 * (static_cast<size_t>(T) + 1);
+}
+
+// Pools of the split kernel's tail stealing: two counters (ticket, CTAs done) per workspace, zero
+// between launches - each launch's last CTA re-zeroes its pair.  A workspace pointer keeps its pair
+// for the life of the process (up to kStealSlots workspaces; later ones run without stealing).  Two
+// launches on one workspace are ordered anyway (they share its partial slots), so a pair is never
+// used by two kernels at once.  The array is a file-scope device variable: its address in the current
+// context is looked up once per context; a look-up that would happen during a stream capture is
+// skipped and that launch runs without stealing.
+constexpr int kStealSlots = 1024;
+static __device__ unsigned g_steal[kStealSlots][2];
+
+static unsigned* steal_counters(const void* ws, cudaStream_t stream) {
+  constexpr int kCtxSlots = 64;
+  static std::mutex mu;
+  static const void* keys[kStealSlots];
+  static int nkeys = 0;
+  static CUcontext ctxs[kCtxSlots] = {nullptr};
+  static unsigned* bases[kCtxSlots] = {nullptr};
+  static int nctx = 0, next_ctx = 0;
+  CtxGetCurrent get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (!get || get(&ctx) != CUDA_SUCCESS || !ctx) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  unsigned* base = nullptr;
+  for (int i = 0; i < nctx; ++i)
+    if (ctxs[i] == ctx) base = bases[i];
+  if (!base) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_steal) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    const int slot = nctx < kCtxSlots ? nctx++ : (next_ctx++ % kCtxSlots);
+    ctxs[slot] = ctx;
+    bases[slot] = base = static_cast<unsigned*>(ptr);
+  }
+  for (int i = 0; i < nkeys; ++i)
+    if (keys[i] == ws) return base + 2 * i;
+  if (nkeys == kStealSlots) return nullptr;
+  keys[nkeys] = ws;
+  return base + 2 * nkeys++;
 }
 
 // CTAs per SM of the split kernel at its largest shared-memory footprint (queried once per device).
@@ -740,8 +909,20 @@ static int launch_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStrea
   p.contig_n = 0;
   p.mask = nullptr;
   p.mask_st = 0;
+  // tail stealing when the workspace holds 2 G + T - 1 slots (the kernel also wants 16 pages per CTA)
+  // Tail stealing (the STEAL kernel) doubles a row's partials, which the combine merges in series: only
+  // where rows are about as many as CTAs (at most 2 CTAs per row on average) and the workspace holds
+  // 2 G + T - 1 slots.  The kernel itself also wants 16 pages per CTA, or keeps its static ranges.
+  p.steal = (plan.stream_mode && plan.grid <= 2 * a.T && 2 * static_cast<int64_t>(plan.grid) + a.T - 1 <= plan.slots_cap)
+                ? steal_counters(a.ws, stream) : nullptr;
+  auto kernel = p.steal ? history_split_kernel<W, PG, false, true> : history_split_kernel<W, PG, false, false>;
+  if (p.steal) {
+    static unsigned steal_mask = 0;
+    ensure_smem_limit(history_split_kernel<W, PG, false, true>,
+                      static_cast<int>(history_smem_bytes<W, PG>(kHistoryMaxStreamRows)), steal_mask);
+  }
   if (!a.pdl) {
-    history_split_kernel<W, PG><<<plan.grid, C::THREADS, smem, stream>>>(tmap, tmap, p);
+    kernel<<<plan.grid, C::THREADS, smem, stream>>>(tmap, tmap, p);
     return cuda_status(cudaGetLastError(), "history_split_kernel launch");
   }
   // programmatic dependent of the preceding launch (the one that writes q): pages stream meanwhile
@@ -755,8 +936,7 @@ static int launch_split(const HistoryArgs& a, const HistoryPlan& plan, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, history_split_kernel<W, PG, false>, tmap, tmap, p),
-                     "history_split_kernel launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmap, tmap, p), "history_split_kernel launch");
 }
 
 int history_plan(const HistoryArgs& a, HistoryPlan* plan) {
@@ -851,6 +1031,7 @@ static int launch_contig(const ContigArgs& c, const HistoryPlan& plan, cudaStrea
   p.wait_ns = wait_limit_ns();
   p.num_blocks = 0;
   p.contig_n = c.N;
+  p.steal = nullptr;
   p.mask = c.mask;
   p.mask_st = c.m_sb;
   static unsigned attr_mask = 0;

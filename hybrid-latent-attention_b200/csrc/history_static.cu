@@ -30,9 +30,7 @@ static __device__ __align__(256) float g_history_scratch[kStaticScratchFloats];
 // ordinal: after cudaDeviceReset, or with another context current on the same device, the array lives
 // at another address and is looked up again.  The look-up may load this library's device code into
 // the context, so the first call in each context must come before any stream capture.
-using CtxGetCurrent = CUresult (*)(CUcontext*);
-
-static CtxGetCurrent ctx_get_current() {
+CtxGetCurrent ctx_get_current() {
   static CtxGetCurrent fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {

@@ -41,6 +41,11 @@ int cuda_status(cudaError_t e, const char* what);
 int latent_cache_tmap(CUtensorMap* map, const void* cache, int64_t num_blocks, int64_t st_block, int64_t st_row,
                       int W, int page);
 
+// cuCtxGetCurrent through the runtime's driver entry point (null when unavailable): the CUDA context
+// that device-symbol addresses belong to (history_static.cu).
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+CtxGetCurrent ctx_get_current();
+
 struct HistoryArgs {
   const void* q;            // bf16 [T, H, W], unit last stride
   int64_t q_st, q_sh;

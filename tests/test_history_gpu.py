@@ -250,3 +250,18 @@ def test_block_id_outside_the_cache_is_reported(splits):
         if bad is None:
             o_ref, lse_ref = orc.history_attention(q, cache, tab, ctx, SCALE)
             check(o, lse, o_ref, lse_ref, ctx)
+
+
+def test_tail_stealing_split_matches_oracle_and_repeats_bit_exactly():
+    """A step with about as many rows as the split kernel has CTAs (160 rows, ~31 pages per CTA) runs the
+    tail-stealing kernel: the last eighth of each CTA's pages is taken by whichever CTA is free first.
+    Partial slots belong to units, not to CTAs, so three calls in a row on the same workspace give
+    bit-identical outputs (the pool's counters are re-zeroed by each launch's last CTA), equal to the
+    oracle within the output tolerances."""
+    q, cache, table, ctx = random_case(11, 512, 16, 160, [3000, 700, 40, 5])
+    o_ref, lse_ref = orc.history_attention(q, cache, table, ctx, SCALE)
+    qd, cd, td, xd = dev(q, BF16), dev(cache, BF16), dev(table), dev(ctx)
+    outs = [run(qd, cd, td, xd, 64) for _ in range(3)]
+    for o, lse in outs:
+        check(o, lse, o_ref, lse_ref, ctx)
+        assert torch.equal(o, outs[0][0]) and torch.equal(lse, outs[0][1])
