@@ -68,7 +68,13 @@ uint64_t hla_s6_set_wait_limit_ns(uint64_t ns);
  * vLLM decode_attention_fwd stage 1 + stage 2).  The workspace must hold at least
  * T * num_kv_splits * H * (W + 1) floats (s6_ops.py:109-114 S6Workspace.attn_logits).
  * out: bf16 [T, H, W] with strides (out_stride_t, out_stride_h, 1); lse: fp32 [H, T].
- * empty (optional, uint8 [T]) forces o = 0 / lse = -inf on marked rows (s6_ops.py:161). */
+ * empty (optional, uint8 [T]) forces o = 0 / lse = -inf on marked rows (s6_ops.py:161).
+ * When a step has about as many rows as the split kernel has CTAs, and the workspace holds twice
+ * as many partial slots as CTAs, the split lets CTAs that finish early take the last eighth of
+ * the others' pages.  Results do not depend on which CTA ran what.  The work pool's counters
+ * are a pair per workspace pointer in an 8 KB device array of the library, zero between calls.
+ * A pair is assigned on a workspace's first such call: make that call outside any stream
+ * capture, or that one call runs without stealing. */
 int hla_s6_history_attention(const void* q_lat, int64_t q_stride_t, int64_t q_stride_h, const void* cache,
                              int64_t num_blocks, int64_t cache_stride_block, int64_t cache_stride_row,
                              const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks,
