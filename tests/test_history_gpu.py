@@ -252,13 +252,14 @@ def test_block_id_outside_the_cache_is_reported(splits):
             check(o, lse, o_ref, lse_ref, ctx)
 
 
-def test_tail_stealing_split_matches_oracle_and_repeats_bit_exactly():
-    """A step with about as many rows as the split kernel has CTAs (160 rows, ~31 pages per CTA) runs the
-    tail-stealing kernel: the last eighth of each CTA's pages is taken by whichever CTA is free first.
-    Partial slots belong to units, not to CTAs, so three calls in a row on the same workspace give
-    bit-identical outputs (the pool's counters are re-zeroed by each launch's last CTA), equal to the
-    oracle within the output tolerances."""
-    q, cache, table, ctx = random_case(11, 512, 16, 160, [3000, 700, 40, 5])
+@pytest.mark.parametrize('width,block', [(512, 16), (256, 32), (512, 32)])
+def test_tail_stealing_split_matches_oracle_and_repeats_bit_exactly(width, block):
+    """A step with about as many rows as the split kernel has CTAs (160 rows, empty ones among them, over
+    16 pages per CTA) runs the tail-stealing kernel: the last eighth of each CTA's pages is taken by
+    whichever CTA is free first.  Partial slots belong to units, not to CTAs, so three calls in a row on
+    the same workspace give bit-identical outputs (the pool's counters are re-zeroed by each launch's
+    last CTA), equal to the oracle within the output tolerances."""
+    q, cache, table, ctx = random_case(11 + width + block, width, block, 160, [3000, 700, 40, 5, 0])
     o_ref, lse_ref = orc.history_attention(q, cache, table, ctx, SCALE)
     qd, cd, td, xd = dev(q, BF16), dev(cache, BF16), dev(table), dev(ctx)
     outs = [run(qd, cd, td, xd, 64) for _ in range(3)]
