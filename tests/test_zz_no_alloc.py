@@ -15,6 +15,7 @@ import pytest
 import torch
 
 from conftest import pkg
+from oracle import s6_oracle as orc
 
 pytestmark = pytest.mark.gpu
 CUDA, BF16, I32 = 'cuda', torch.bfloat16, torch.int32
@@ -69,6 +70,12 @@ def test_static_scratch_matches_workspace_entry_point_on_consecutive_calls():
         empty = ctx == 0
         assert (lse[:, empty] == -math.inf).all() and (o[empty] == 0).all()
         torch.testing.assert_close(lse[:, ~empty], lse_ref[:, ~empty], atol=LSE_ATOL, rtol=0)
+        # and the CPU oracle of the reference's history attention (s6_ops.py:204-222)
+        o_orc, lse_orc = orc.history_attention(q.float().cpu().numpy(), cache.float().cpu().numpy(),
+                                               table.cpu().numpy(), ctx.cpu().numpy(), scale)
+        np.testing.assert_allclose(o.float().cpu().numpy(), o_orc, **O_TOL)
+        keep = ~empty.cpu().numpy()
+        np.testing.assert_allclose(lse.cpu().numpy()[:, keep], lse_orc[:, keep], atol=LSE_ATOL, rtol=0)
 
 
 def test_static_scratch_one_split_per_row():
