@@ -16,6 +16,9 @@ torch, as vLLM's ``QKVParallelLinear`` / ``RowParallelLinear``):
   latent query      StepContext.latent_query                    (:111, before the in-place exact RoPE)
   exact RoPE + append  hla_s6_exact_append: q rotated in place, k rotated, k|v stored at the exact
                     cache's slots (rotary_emb :112 + unified_kv_cache_update :121-123)
+                    - in a decode batch with a window both run as one launch (hla_s6_decode_prepare:
+                    q_lat, and the exact RoPE of q into a separate q_rope), and the history split
+                    is its programmatic dependent
   attend            s6_layer.attend                              (:124-125)
   commit            hla_s6_commit_rows: the K half latent-RoPE'd and the row stored at the latent
                     cache's slots (committed_row + unified_kv_cache_update, :126-129)
@@ -68,23 +71,63 @@ class LatentAttention:
         state = s6_layer.write_rows(sl, current_ut, hidden_states, state)
         qkv = F.linear(hidden_states, self.qkv_weight)
         q, k, v = (x.view(T, H, d) for x in qkv.split(H * d, -1))
+        cache = caches.l1 if current_ut == 0 else caches.main
+        md = ctx.md_present
+        if self.window and md and ctx.max_query_len == 1:
+            # decode batch: latent query, exact RoPE and exact-cache append in one launch, and the history
+            # split as its programmatic dependent (the same values as the separate ops below)
+            cache_e = caches.exact[current_ut].transpose(1, 2)  # logical [nb, H, page, 2d]
+            # the per-token block table the split reads is gathered now, so that no launch comes between the
+            # prepare and the split (whose producer reads the table before it waits for the prepare)
+            ctx.block_table(caches.latent_table)
+            q_lat, q_rope = self._prepare(current_ut, q, k, v, positions, cache_e, caches.exact_table, ctx)
+            ctx.history_after_query = True
+            try:
+                out = s6_layer.attend(sl, current_ut, q_lat, q_rope, None, v, cache, caches.latent_table, None,
+                                      None, ctx, (cache_e, caches.exact_table))
+            finally:
+                ctx.history_after_query = False
+            if current_ut == 0 or current_ut == sl.loops - 1:
+                self._commit(current_ut, state, positions, cache, caches.latent_table, ctx)
+            output = F.linear(out.reshape(T, H * d), self.o_weight)
+            return (output, state, out) if return_attention else (output, state)
         q_lat = ctx.latent_query(sl, current_ut, q)            # before the in-place exact RoPE
         k_rope = torch.empty(T, H, d, dtype=k.dtype, device=k.device)
         window = None
-        if self.window and ctx.md_present:
+        if self.window and md:
             cache_e = caches.exact[current_ut].transpose(1, 2)  # logical [nb, H, page, 2d]
             self._exact_append(q, k, v, k_rope, positions, cache_e, caches.exact_table, ctx)
             window = (cache_e, caches.exact_table)
         else:
             self._exact_append(q, k, v, k_rope, positions, None, None, ctx)
-        cache = caches.l1 if current_ut == 0 else caches.main
-        md = ctx.md_present
         out = s6_layer.attend(sl, current_ut, q_lat, q, k_rope, v, cache if md else None,
                               caches.latent_table if md else None, None, None, ctx, window)
         if md and (current_ut == 0 or current_ut == sl.loops - 1):
             self._commit(current_ut, state, positions, cache, caches.latent_table, ctx)
         output = F.linear(out.reshape(T, H * d), self.o_weight)
         return (output, state, out) if return_attention else (output, state)
+
+    def _prepare(self, loop, q, k, v, positions, cache, table, ctx):
+        """hla_s6_decode_prepare: ``q_lat`` = latent RoPE of ``q . A`` (ctx.latent_query), ``q_rope`` = exact
+        RoPE of q (a separate output), RoPE(k) | v stored at each token's exact-cache slot - one launch."""
+        sl = self.latent
+        T, H, d = q.shape
+        A, _, width = sl.readers(loop)
+        tab = ctx.tables[width]
+        q_lat = torch.empty(T, H, width, dtype=q.dtype, device=q.device)
+        q_rope = torch.empty(T, H, d, dtype=q.dtype, device=q.device)
+        pos = positions if positions.dtype == torch.int64 else positions.long()
+        qsl = ctx.query_start_loc
+        nb, _, page, _ = cache.shape
+        sb, sh, sr, _ = cache.stride()
+        _lib.call('hla_s6_decode_prepare', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(A), A.stride(0),
+                  A.stride(1), _lib.ptr(pos), _lib.ptr(tab), tab.stride(0), tab.shape[0], _lib.ptr(q_lat),
+                  q_lat.stride(0), q_lat.stride(1), T, H, d, width, _lib.ptr(q_rope), q_rope.stride(0),
+                  q_rope.stride(1), _lib.ptr(k), k.stride(0), k.stride(1), _lib.ptr(v), v.stride(0), v.stride(1),
+                  _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(cache), nb, sb, sh,
+                  sr, page, _lib.ptr(table), table.stride(0), table.shape[1], _lib.ptr(qsl), qsl.shape[0] - 1, None,
+                  0, _lib.stream_of(q))
+        return q_lat, q_rope
 
     def _exact_append(self, q, k, v, k_rope, positions, cache, table, ctx):
         """Exact neox RoPE of q (in place) and k (into ``k_rope``), and - with a cache - k_rope | v stored at

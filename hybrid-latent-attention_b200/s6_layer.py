@@ -124,9 +124,12 @@ def attend(sl, loop, q_lat, q_rope, k_rope, v, cache, block_table, k_scale, v_sc
         ws = ctx.workspace.attn_logits(T, H, splits, width, q_lat.device)
         ws_ptr, ws_floats = ctx.workspace.buffer, ws.numel()
         bt = ctx.block_table(block_table)
+        # a caller whose last launch wrote q_lat (ouro_attention's fused prepare) sets history_after_query:
+        # the split then streams pages while that launch runs
+        after_query = _lib.PARTIALS_AFTER_QUERY if getattr(ctx, 'history_after_query', False) else 0
         _lib.call('hla_s6_history_partials', _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), _lib.ptr(cache), nb,
                   sb, sr, _lib.ptr(bt), bt.stride(0), bt.shape[1], _lib.ptr(ctx.ctx_latent), T, H, width, lpage,
-                  float(ctx.scale), int(splits), _lib.ptr(ws_ptr), ws_floats, None, 0, stream)
+                  float(ctx.scale), int(splits), _lib.ptr(ws_ptr), ws_floats, None, after_query, stream)
         z_in = lse_in = None
         empty = ctx.empty_latent
     else:
