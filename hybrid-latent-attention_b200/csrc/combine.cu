@@ -124,38 +124,46 @@ __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_con
         }
       } else if (p.zw_in) {
         // num_parts parts as exchange words stored by the parts' GPUs (history_reduce_exchange): each
-        // word is polled until it carries this exchange's tag.  The lse words first (lane q polls part
-        // q's), then the z words of two parts per memory round; the merge order is the one above.
+        // word is polled until it carries this exchange's tag.  The lse words (lane q polls part q's)
+        // and the first two parts' z words in one memory round, then the z words of two parts per
+        // round; the merge order is the one above.
         WordPoll poll(static_cast<uint32_t>(*p.epoch) + 1u, p.wait_ns);
+        uint64_t wv[2][NV][4];
+        const uint64_t* src[2];
+        auto load_pair = [&](int u, int q) {
+          src[u] = p.zw_in + q * p.part_stride + (static_cast<int64_t>(t) * H + h) * W;
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            ld_words2(src[u] + (i * 32 + lane) * 4, wv[u][i][0], wv[u][i][1]);
+            ld_words2(src[u] + (i * 32 + lane) * 4 + 2, wv[u][i][2], wv[u][i][3]);
+          }
+        };
+        // the first two parts' z words go out with the lse words (one memory round instead of two; a part
+        // that turns out to have no keys has loaded for nothing)
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (u < p.num_parts) load_pair(u, u);
         float lq = -INFINITY;
         if (lane < p.num_parts) {
-          const uint64_t* src = p.lw_in + lane * p.part_stride + static_cast<int64_t>(h) * T + t;
-          uint64_t w = ld_word(src);
-          if (poll.wait1(src, w)) lq = word_value(w);
+          const uint64_t* lsrc = p.lw_in + lane * p.part_stride + static_cast<int64_t>(h) * T + t;
+          uint64_t w = ld_word(lsrc);
+          if (poll.wait1(lsrc, w)) lq = word_value(w);
         }
         const float mx = warp_max(lq);
         if (mx != -INFINITY) {
           float wsum = 0.f;
           for (int q0 = 0; q0 < p.num_parts; q0 += 2) {
             float lu[2];
-            uint64_t wv[2][NV][4];
-            const uint64_t* src[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int q = q0 + u;
               lu[u] = __shfl_sync(0xffffffffu, lq, q < p.num_parts ? q : 0);
               if (q >= p.num_parts) lu[u] = -INFINITY;
-              src[u] = p.zw_in + q * p.part_stride + (static_cast<int64_t>(t) * H + h) * W;
-              if (lu[u] == -INFINITY) continue;  // past the parts, or a part without keys
-#pragma unroll
-              for (int i = 0; i < NV; ++i) {
-                ld_words2(src[u] + (i * 32 + lane) * 4, wv[u][i][0], wv[u][i][1]);
-                ld_words2(src[u] + (i * 32 + lane) * 4 + 2, wv[u][i][2], wv[u][i][3]);
-              }
+              if (q0 > 0 && lu[u] != -INFINITY) load_pair(u, q);  // pair 0 is already in flight
             }
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              if (lu[u] == -INFINITY) continue;
+              if (lu[u] == -INFINITY) continue;  // past the parts, or a part without keys
               const float wgt = expf(lu[u] - mx);
               wsum += wgt;
 #pragma unroll
