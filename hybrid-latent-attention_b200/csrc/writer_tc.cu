@@ -83,7 +83,32 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 struct TcParams {
   WriterParams w;
   int n_tiles, m_tiles;
+  bool v32;  // every epilogue row segment is 32-byte aligned: 256-bit accesses (else 2 x 128-bit)
 };
+
+// 32 contiguous bytes of global memory: one 256-bit access when `v32` (the address is 32-byte
+// aligned), else two 128-bit ones.  A 256-bit access fills a whole L2 sector per lane and halves
+// the epilogue's load / store instructions (each lane of a warp addresses its own row).
+__device__ __forceinline__ void ld32(const void* p, uint4& a, uint4& b, bool v32) {
+  if (v32) {
+    asm volatile("ld.global.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+                 : "l"(p));
+  } else {
+    a = reinterpret_cast<const uint4*>(p)[0];
+    b = reinterpret_cast<const uint4*>(p)[1];
+  }
+}
+__device__ __forceinline__ void st32(void* p, const uint4& a, const uint4& b, bool v32) {
+  if (v32) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z),
+                 "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+                 : "memory");
+  } else {
+    reinterpret_cast<uint4*>(p)[0] = a;
+    reinterpret_cast<uint4*>(p)[1] = b;
+  }
+}
 
 // E rows of the two 128-row boxes of column tile j.
 __device__ __forceinline__ void tc_tile_rows(const WriterParams& p, int j, int& n_lo, int& n_hi) {
@@ -111,29 +136,27 @@ struct TileIn {
   __nv_bfloat16* rout;
 };
 
-__device__ __forceinline__ void tc_load_rope(const TileIn& in, int col, uint4* cs, uint4* sn, int half_w) {
-  const uint4* c = reinterpret_cast<const uint4*>(in.tab + col);
-  const uint4* s = reinterpret_cast<const uint4*>(in.tab + half_w + col);
+__device__ __forceinline__ void tc_load_rope(const TileIn& in, int col, uint4* cs, uint4* sn, int half_w, bool v32) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    cs[i] = c[i];
-    sn[i] = s[i];
+  for (int i = 0; i < 4; i += 2) {
+    ld32(in.tab + col + 8 * i, cs[i], cs[i + 1], v32);
+    ld32(in.tab + half_w + col + 8 * i, sn[i], sn[i + 1], v32);
   }
 }
 
 __device__ __forceinline__ void tc_tile_prefetch(const WriterParams& p, int t, bool live, bool pair_tile, int n_lo,
-                                                 int n_hi, TileIn& in) {
+                                                 int n_hi, TileIn& in, bool v32) {
   in.tab = nullptr;
   in.dst = nullptr;
   in.rout = (p.reg_out && live) ? p.reg_out + static_cast<int64_t>(t) * p.ro_st : nullptr;
   if (!live) return;
   if (p.reg_in) {
-    const uint4* a = reinterpret_cast<const uint4*>(p.reg_in + static_cast<int64_t>(t) * p.ri_st + n_lo);
-    const uint4* b = reinterpret_cast<const uint4*>(p.reg_in + static_cast<int64_t>(t) * p.ri_st + n_hi);
+    const __nv_bfloat16* a = p.reg_in + static_cast<int64_t>(t) * p.ri_st + n_lo;
+    const __nv_bfloat16* b = p.reg_in + static_cast<int64_t>(t) * p.ri_st + n_hi;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      in.lo[i] = a[i];
-      in.hi[i] = b[i];
+    for (int i = 0; i < 16; i += 2) {
+      ld32(a + 8 * i, in.lo[i], in.lo[i + 1], v32);
+      ld32(b + 8 * i, in.hi[i], in.hi[i + 1], v32);
     }
   }
   if (p.commit) {
@@ -141,7 +164,7 @@ __device__ __forceinline__ void tc_tile_prefetch(const WriterParams& p, int t, b
     const int64_t slot = token_slot(p.qsl, p.R, t, pos, p.bt, p.bt_st, p.max_blocks, p.page, p.num_blocks);
     if (slot >= 0) in.dst = p.cache + (slot / p.page) * p.c_sb + (slot % p.page) * p.c_sr;
     in.tab = p.table + clamp_pos(pos, p.max_pos) * p.tab_st;
-    if (pair_tile && in.dst) tc_load_rope(in, n_lo, in.cs, in.sn, p.w / 2);
+    if (pair_tile && in.dst) tc_load_rope(in, n_lo, in.cs, in.sn, p.w / 2, v32);
   }
 }
 
@@ -160,7 +183,7 @@ __device__ __forceinline__ uint32_t word(const uint4& u, int i) {
 }
 
 __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t tacc, bool live, bool pair_tile, int n_lo,
-                                              int n_hi, TileIn& in) {
+                                              int n_hi, TileIn& in, bool v32) {
 #pragma unroll
   for (int c0 = 0; c0 < 128; c0 += 16) {
     uint32_t rl[16], rh[16];
@@ -189,12 +212,8 @@ __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t ta
       ohi[i] = make_uint4(as_u32(hi[4 * i]), as_u32(hi[4 * i + 1]), as_u32(hi[4 * i + 2]), as_u32(hi[4 * i + 3]));
     }
     if (in.rout) {
-      uint4* r1 = reinterpret_cast<uint4*>(in.rout + clo);
-      uint4* r2 = reinterpret_cast<uint4*>(in.rout + chi);
-      r1[0] = olo[0];
-      r1[1] = olo[1];
-      r2[0] = ohi[0];
-      r2[1] = ohi[1];
+      st32(in.rout + clo, olo[0], olo[1], v32);
+      st32(in.rout + chi, ohi[0], ohi[1], v32);
     }
     if (in.dst) {
       if (pair_tile) {
@@ -202,7 +221,7 @@ __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t ta
         // the next 32 pairs are fetched once this chunk has read its own
         const int q = (c0 % 32) / 8;
         const uint4 cs[2] = {in.cs[q], in.cs[q + 1]}, sn[2] = {in.sn[q], in.sn[q + 1]};
-        if (c0 % 32 == 16 && c0 + 16 < 128) tc_load_rope(in, n_lo + c0 + 16, in.cs, in.sn, p.w / 2);
+        if (c0 % 32 == 16 && c0 + 16 < 128) tc_load_rope(in, n_lo + c0 + 16, in.cs, in.sn, p.w / 2, v32);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const __nv_bfloat162 c = as_bf2(word(cs[i / 4], i % 4)), sv = as_bf2(word(sn[i / 4], i % 4));
@@ -216,12 +235,8 @@ __device__ __forceinline__ void tc_store_tile(const WriterParams& p, uint32_t ta
           ohi[i] = make_uint4(as_u32(hi[4 * i]), as_u32(hi[4 * i + 1]), as_u32(hi[4 * i + 2]), as_u32(hi[4 * i + 3]));
         }
       }
-      uint4* d1 = reinterpret_cast<uint4*>(in.dst + clo);
-      uint4* d2 = reinterpret_cast<uint4*>(in.dst + chi);
-      d1[0] = olo[0];
-      d1[1] = olo[1];
-      d2[0] = ohi[0];
-      d2[1] = ohi[1];
+      st32(in.dst + clo, olo[0], olo[1], v32);
+      st32(in.dst + chi, ohi[0], ohi[1], v32);
     }
   }
 }
@@ -343,7 +358,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int t = m0 + row;
       const bool pair_tile = p.commit && j < p.w / 256;
       TileIn in;
-      tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in);
+      tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in, tp.v32);
       // tcgen05.ld / wait::ld are warp-collective (.sync.aligned): the wait result is made warp-uniform
       // and every lane runs the loads; rows past T only skip their global accesses
       const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1, p.wait_ns));
@@ -353,7 +368,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_store_tile(p, tmem + b * kTcN + (static_cast<uint32_t>(quarter * 32) << 16), t < p.T, pair_tile, n_lo, n_hi,
-                    in);
+                    in, tp.v32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -577,7 +592,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int t = m0 + row;
       const bool pair_tile = p.commit && j < p.w / 256;
       TileIn in;
-      tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in);
+      tc_tile_prefetch(p, t, t < p.T, pair_tile, n_lo, n_hi, in, tp.v32);
       const bool done = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (it >> 1) & 1, p.wait_ns));
       tc_fence_after();
       if (!done) {
@@ -585,7 +600,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_store_tile(p, tmem + b * kTcN + (static_cast<uint32_t>(quarter * 32) << 16), t < p.T, pair_tile, n_lo, n_hi,
-                    in);
+                    in, tp.v32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(peer_smem(&tempty[b], 0));
@@ -653,6 +668,10 @@ int writer_tc(const WriterParams& p, cudaStream_t s) {
   tp.w = p;
   tp.w.wait_ns = wait_limit_ns();
   tp.n_tiles = p.N / kTcN;
+  // 256-bit epilogue accesses need 32-byte aligned rows (column offsets are multiples of 16 elements)
+  auto a32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) % 32) == 0; };
+  tp.v32 = a32(p.reg_in) && (p.ri_st % 16) == 0 && a32(p.reg_out) && (p.ro_st % 16) == 0 &&
+           (!p.commit || (a32(p.cache) && a32(p.table) && p.c_sb % 16 == 0 && p.c_sr % 16 == 0 && p.tab_st % 16 == 0));
   if (p.T >= 2 * kTcM) {
     static unsigned attr2 = 0;
     ensure_smem_limit(writer_tc2_kernel, kT2Smem, attr2);
