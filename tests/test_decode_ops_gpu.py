@@ -363,3 +363,46 @@ def test_probe_latent_rope_checks_the_b200_kernel():
         table = lay.latent_rope_table(4096, inv, w, BF16).to(CUDA)
         assert ops().probe_latent_rope(table, 16) == (False, True)
         assert ops().probe_latent_rope(table) == (False, True)
+
+
+@pytest.mark.parametrize('T', [200, 300])
+def test_writer_epilogue_access_width_does_not_change_results(T):
+    """Rows that are 32-byte aligned take the epilogue's 256-bit loads and stores; rows that are only
+    16-byte aligned (here: every buffer offset by 8 elements, strides 8 elements past a multiple of
+    16) take two 128-bit accesses.  Both write the same register and committed rows, bit for bit."""
+    rng = np.random.default_rng(T + 101)
+    K, page, max_pos, w = 256, 16, 4096, 512
+    N = 2 * w
+    lib = pkg('_lib')
+    h = dev(orc.bf16(rng.standard_normal((T, K), dtype=np.float32)), BF16)
+    E = dev(orc.bf16(rng.standard_normal((N, K), dtype=np.float32) / 16), BF16)
+    reg_np = orc.bf16(rng.standard_normal((T, N), dtype=np.float32))
+    R = T - 3
+    qsl = torch.tensor(list(range(R + 1)), dtype=I32, device=CUDA)
+    pos = torch.from_numpy(rng.integers(0, 2 * page, T)).to(CUDA)
+    nb = 2 * R + 2
+    bt = (torch.randperm(nb - 1, device=CUDA).to(I32)[:2 * R] + 1).view(R, 2)
+    inv = layer().latent_inv_freq(128, 1e6)
+    table = layer().latent_rope_table(max_pos, inv, w, BF16).to(CUDA)
+    st = lib.stream_of(h)
+
+    def run(pad):
+        reg_in = torch.zeros(T, N + pad, dtype=BF16, device=CUDA)[:, pad:]
+        reg_in.copy_(dev(reg_np, BF16))
+        reg_out = torch.full((T, N + pad), float('nan'), dtype=BF16, device=CUDA)[:, pad:]
+        cache = torch.full((nb, 1, page, N + pad), float('nan'), dtype=BF16, device=CUDA)[..., pad:]
+        lib.call('hla_s6_writer_project', lib.ptr(h), h.stride(0), lib.ptr(E), E.stride(0), lib.ptr(reg_in),
+                 reg_in.stride(0), lib.ptr(reg_out), reg_out.stride(0), T, N, K, st)
+        lib.call('hla_s6_writer_commit', lib.ptr(h), h.stride(0), lib.ptr(E), E.stride(0), lib.ptr(reg_in),
+                 reg_in.stride(0), None, 0, T, N, K, lib.ptr(pos), lib.ptr(table), table.stride(0), table.shape[0],
+                 lib.ptr(cache), nb, cache.stride(0), cache.stride(2), page, lib.ptr(bt), bt.stride(0), bt.shape[1],
+                 lib.ptr(qsl), R, st)
+        torch.cuda.synchronize()
+        return reg_out.float().cpu().numpy(), cache.float().cpu().numpy()
+
+    reg32, cache32 = run(0)
+    reg16, cache16 = run(8)
+    assert not np.isnan(reg32).any()
+    np.testing.assert_array_equal(reg16, reg32)
+    np.testing.assert_array_equal(np.isnan(cache16), np.isnan(cache32))
+    np.testing.assert_array_equal(np.nan_to_num(cache16), np.nan_to_num(cache32))
