@@ -119,6 +119,16 @@ def test_latent_rope_is_bit_exact_with_reference(w):
     flat = dev(r[f'x{w}'], BF16).reshape(T, -1).contiguous()
     ops().latent_rope(flat, pos, table, 'b200')
     np.testing.assert_array_equal(flat.view(T, -1, w).float().cpu().numpy(), g[f'rope{w}_bf16'])
+    # the LLA row / query tail: [T, H, 512 + w] rows whose last w columns are rotated in place (head stride
+    # 512 + w, the fourth layout of the reference's test_s6_ops_gpu.py:221-240); the latent head stays untouched
+    H = r[f'x{w}'].shape[1]
+    lla = torch.randn(T, H, 512 + w, dtype=BF16, device=CUDA)
+    lla[..., 512:] = dev(r[f'x{w}'], BF16)
+    head_before = lla[..., :512].clone()
+    y = ops().latent_rope(lla[..., 512:], pos, table, 'b200')
+    assert y.stride() == lla[..., 512:].stride()
+    np.testing.assert_array_equal(lla[..., 512:].float().cpu().numpy(), g[f'rope{w}_bf16'])
+    assert torch.equal(lla[..., :512], head_before)
 
 
 @pytest.mark.parametrize('w', [512, 256])

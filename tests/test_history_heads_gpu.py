@@ -87,3 +87,46 @@ def test_layout_contract():
         ops.history_attention_kv(q, cache, other, table, ctx, 0.1, 4, ws, None, None, 'b200', mla=True)
     with pytest.raises(RuntimeError, match='overflow'):
         ops.history_attention_kv(q, cache, cache[..., :128], table, ctx, 0.1, 64, ws, None, None, 'b200', mla=True)
+
+
+def test_replays_inside_cuda_graph():
+    """Per-head MLA read captured in a CUDA graph, replayed with changing ctx / cache / q contents (the case of the
+    reference's test_s6_ops_gpu.py:78-110): the stream-K plan and slot ranges follow the new lengths on the device."""
+    torch.manual_seed(6)
+    ops = pkg('s6_ops')
+    rank, d_rope, block, batch, splits, num_blocks = 512, 64, 16, 8, 8, 256
+    ws = ops.S6Workspace(16, rank, batch * splits)
+    ws.ensure(CUDA)
+    cache = torch.randn(num_blocks, 16, block, rank + d_rope, dtype=BF16, device=CUDA)
+    table = torch.randint(0, num_blocks, (batch, 64), dtype=torch.int32, device=CUDA)
+    ctx = torch.randint(0, 1000, (batch,), dtype=torch.int32, device=CUDA)
+    q = torch.randn(batch, 16, rank + d_rope, dtype=BF16, device=CUDA)
+    scale = 1 / math.sqrt(128)
+
+    def go():
+        return ops.history_attention_kv(q, cache, cache[..., :rank], table, ctx, scale, splits, ws, None, None, 'b200',
+                                        mla=True)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        go()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o, lse = go()
+    for _ in range(3):
+        ctx.copy_(torch.randint(0, 1000, (batch,), dtype=torch.int32, device=CUDA))
+        ctx[0] = 0
+        cache.copy_(torch.randn_like(cache))
+        q.copy_(torch.randn_like(q))
+        graph.replay()
+        torch.cuda.synchronize()
+        c = cache.float().cpu().numpy()
+        o_ref, lse_ref = orc.history_attention_kv(q.float().cpu().numpy(), c, c[..., :rank], table.cpu().numpy(),
+                                                  ctx.cpu().numpy(), scale)
+        o_np, lse_np = o.float().cpu().numpy(), lse.cpu().numpy()
+        np.testing.assert_allclose(o_np, o_ref, **O_TOL)
+        keep = ctx.cpu().numpy() > 0
+        np.testing.assert_allclose(lse_np[:, keep], lse_ref[:, keep], atol=LSE_ATOL, rtol=0)
+        assert (o_np[0] == 0).all() and (lse_np[:, 0] == -np.inf).all()

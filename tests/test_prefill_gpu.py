@@ -44,7 +44,8 @@ def test_chunk_attention_matches_reference_fixture():
     assert (o[~valid] == 0).all() and (lse[:, ~valid] == -np.inf).all()
 
 
-@pytest.mark.parametrize('qsl', [(0, 300), (0, 64, 65, 200, 257, 257), (0, 1, 2, 3, 70, 130)])
+@pytest.mark.parametrize('qsl', [(0, 300), (0, 64, 65, 200, 257, 257), (0, 1, 2, 3, 70, 130),
+                                 tuple(range(34))])      # the last: uniform decode, one token per request
 def test_chunk_attention_long_and_ragged_chunks(qsl):
     rng = np.random.default_rng(len(qsl))
     T = qsl[-1] + 5
