@@ -13,7 +13,7 @@ import torch
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get('HLA_S6_LIB', _PKG / 'libhla_s6.so'))
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 OK, EINVAL, EOVERFLOW, ECUDA = 0, 1, 2, 3
 # codes a kernel writes to its optional device error word (HLA_S6_ERR_*)
@@ -21,7 +21,8 @@ ERR_WAIT_COPY, ERR_WAIT_STAGE, ERR_RANGE, ERR_WAIT_PEER, ERR_BLOCK = 1, 2, 3, 4,
 COMBINE_AFTER_PARTIALS = 1   # hla_s6_decode_combine flag (include/hla_s6.h)
 PARTIALS_AFTER_QUERY = 1     # hla_s6_history_partials flag
 REDUCE_AFTER_PARTIALS = 1    # hla_s6_history_reduce_exchange flag
-PREPARE_EARLY_LAUNCH = 1     # hla_s6_decode_prepare flag
+PREPARE_EARLY_LAUNCH = 1     # hla_s6_decode_prepare flags
+PREPARE_EXACT_ONLY = 2
 PEER_HANDLE_BYTES = 64       # HLA_S6_PEER_HANDLE_BYTES
 EXCHANGE_WORD_BYTES = 8      # HLA_S6_EXCHANGE_WORD_BYTES: fp32 value | 32-bit tag
 

@@ -205,6 +205,7 @@ int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_strid
   p.R = num_reqs;
   p.slot_out = slot_out;
   p.pdl = (flags & HLA_S6_PREPARE_EARLY_LAUNCH) != 0;
+  p.exact_only = (flags & HLA_S6_PREPARE_EXACT_ONLY) != 0;
   return prepare(p, static_cast<cudaStream_t>(stream));
 }
 

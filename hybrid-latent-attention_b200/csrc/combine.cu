@@ -7,7 +7,9 @@
 //   4. LSE merge, invalid (padding) tokens zeroed                        (merge_states, s6_ops.py:262)
 // CTA = (8 tokens, head h), 8 warps, one token per warp.  All of B[h] ([W, 128] bf16) is put in
 // flight with cp.async before steps 1-2, so its latency hides behind them; step 3 is mma.m16n8k16 with the 8
-// tokens as M (rows 8-15 zero; z from shared memory, B via ldmatrix.trans).  Instead of split partials the kernel
+// tokens as M (rows 8-15 zero; z from shared memory, B via ldmatrix.trans).
+// With an external exact part (chunk_o) and more CTAs than one wave fills, a CTA takes 16 tokens instead
+// (two per warp, every row of the mma tile used): half the CTAs, and B[h] staged once per 16 tokens.  Instead of split partials the kernel
 // can take num_parts reduced (z fp32 [T,H,W], lse [H,T]) pairs and LSE-merge them - how a
 // sequence-split history arrives after its cross-GPU exchange.
 #include "combine.cuh"
@@ -17,37 +19,41 @@
 
 namespace hla {
 
-constexpr int kCTok = 8;       // tokens per CTA (one per warp; the mma M of 16 is zero-padded)
+constexpr int kCTok = 8;       // tokens per CTA with the window inside (one per warp; the mma M of 16 is zero-padded)
+constexpr int kCTokWide = 16;  // tokens per CTA with an external exact part (two per warp)
 constexpr int kCKC = 64;       // k rows of B per chunk
 constexpr int kCChunkBytes = kCKC * 128 * 2;   // 16 KB
 
-template <int W>
+template <int W, int TOK>
 struct CombineSmem {
   static constexpr int Z_BYTES = 16 * W * 2;
   static constexpr int B_OFF = 0;                                // all of B[h]: W/64 chunks
   static constexpr int Z_OFF = (W / kCKC) * kCChunkBytes;
-  static constexpr int OW_OFF = Z_OFF + Z_BYTES;                 // float [16][128] window outputs
-  static constexpr int Q_OFF = OW_OFF + kCTok * 128 * 4;          // float [8 warps][128]
-  static constexpr int L_OFF = Q_OFF + 8 * 128 * 4;               // float lse_h[16], lse_w[16]
-  static constexpr int QSL_OFF = L_OFF + 2 * kCTok * 4;         // int32 query_start_loc copy
+  static constexpr int OW_OFF = Z_OFF + Z_BYTES;                 // float [TOK][128] exact-part outputs
+  static constexpr int Q_OFF = OW_OFF + TOK * 128 * 4;            // float [8 warps][128]
+  static constexpr int L_OFF = Q_OFF + 8 * 128 * 4;               // float lse_h[TOK], lse_w[TOK]
+  static constexpr int QSL_OFF = L_OFF + 2 * TOK * 4;           // int32 query_start_loc copy
   static constexpr int V_OFF = QSL_OFF + kQslCap * 4;            // per warp: the window's V rows
-  static constexpr int BAR_OFF = V_OFF + kCTok * kWindowVBytes;  // mbarrier: all of B[h] landed
+  // the 16-token form takes its exact part from outside and runs no window
+  static constexpr int V_BYTES = TOK == kCTok ? 8 * kWindowVBytes : 0;
+  static constexpr int BAR_OFF = V_OFF + V_BYTES;                // mbarrier: all of B[h] landed
   static constexpr int BYTES = BAR_OFF + 16 + 1024;              // + slack to align the base to 1024 B
 };
 
-template <int W>
+template <int W, int TOK>
 __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_constant__ CUtensorMap tmap_b,
                                                              const CombineParams p) {
-  using S = CombineSmem<W>;
+  static_assert(TOK == kCTok || TOK == kCTokWide, "8 or 16 tokens per CTA");
+  using S = CombineSmem<W, TOK>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // B[h] arrives by TMA with SWIZZLE_128B, whose pattern follows address bits: 1024-byte aligned base
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* ow_s = reinterpret_cast<float*>(smem + S::OW_OFF);
   float* q_s = reinterpret_cast<float*>(smem + S::Q_OFF);
   float* lh_s = reinterpret_cast<float*>(smem + S::L_OFF);
-  float* lw_s = lh_s + kCTok;
+  float* lw_s = lh_s + TOK;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.x, t0 = blockIdx.y * kCTok, T = p.T, H = p.H;
+  const int h = blockIdx.x, t0 = blockIdx.y * TOK, T = p.T, H = p.H;
   constexpr int NK = W / kCKC;
 
   // ---- all of B[h] in flight now (W/64 TMA boxes of 64 rows x 2 slabs of 64 columns, one mbarrier);
@@ -65,10 +71,11 @@ __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_con
   WindowArgs win = p.win;
   win.qsl = stage_qsl(p.win.qsl, p.win.R, reinterpret_cast<int32_t*>(smem + S::QSL_OFF));
 
-  // ---- 1 + 2: warp w owns token t0 + w: exact window first (its inputs precede the history
-  //      kernel), then - after the history grid has completed - the history reduce
-  {
-    const int tt = warp, t = t0 + tt;
+  // ---- 1 + 2: warp w owns tokens t0 + w (+ 8 in the 16-token form): exact window first (its inputs
+  //      precede the history kernel), then - after the history grid has completed - the history reduce
+#pragma unroll 1
+  for (int tt = warp; tt < TOK; tt += 8) {
+    const int t = t0 + tt;
     float o[4], lse_w;
     if (t < T && p.chunk_o) {
       const __nv_bfloat16* src = p.chunk_o + static_cast<int64_t>(t) * p.co_st + static_cast<int64_t>(h) * p.co_sh;
@@ -79,11 +86,11 @@ __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_con
       o[2] = __bfloat162float(b[1].x);
       o[3] = __bfloat162float(b[1].y);
       lse_w = p.chunk_lse[static_cast<int64_t>(h) * T + t];
-    } else if (t < T) {
+    } else if (t < T && S::V_BYTES > 0) {
       if (!win.ctx_tok && win.window <= 32)
         window_warp_short(win, t, h, q_s + warp * 128, smem + S::V_OFF + warp * kWindowVBytes, o, lse_w);
       else window_warp(win, t, h, q_s + warp * 128, o, lse_w);
-    } else {
+    } else {  // past T (the host launches the 16-token form only with an external exact part)
       o[0] = o[1] = o[2] = o[3] = 0.f;
       lse_w = -INFINITY;
     }
@@ -250,7 +257,8 @@ __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_con
       pk.x = pack_bf16(acc[i].x, acc[i].y);
       pk.y = pack_bf16(acc[i].z, acc[i].w);
       *reinterpret_cast<uint2*>(smem + S::Z_OFF + swz(tt, d >> 3, W * 2) + (d & 7) * 2) = pk;
-      *reinterpret_cast<uint2*>(smem + S::Z_OFF + swz(tt + 8, d >> 3, W * 2) + (d & 7) * 2) = make_uint2(0u, 0u);
+      if (TOK == kCTok)  // 8 tokens: rows 8-15 of the mma tile are zero
+        *reinterpret_cast<uint2*>(smem + S::Z_OFF + swz(tt + 8, d >> 3, W * 2) + (d & 7) * 2) = make_uint2(0u, 0u);
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) ow_s[tt * 128 + lane * 4 + e] = bf16_round(o[e]);
@@ -289,11 +297,11 @@ __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_con
     }
   }
 
-  // ---- 4: merge (row g of the mma tile = token t0 + g; columns 16w + 8nt + 2c, +1)
+  // ---- 4: merge (row g (+ 8) of the mma tile = token t0 + g (+ 8); columns 16w + 8nt + 2c, +1)
   const int g = lane >> 2, c = lane & 3;
-  {
-    const int half = 0;
-    const int tt = g, t = t0 + tt;
+#pragma unroll
+  for (int half = 0; half < TOK / 8; ++half) {
+    const int tt = g + 8 * half, t = t0 + tt;
     if (t >= T) return;
     const bool invalid = t >= win.qsl[win.R];
     float w1, w2;
@@ -312,16 +320,16 @@ __global__ void __launch_bounds__(256, 1) decode_combine_kernel(const __grid_con
   }
 }
 
-template <int W>
+template <int W, int TOK>
 static int launch_combine(const CombineParams& p, bool pdl, cudaStream_t s) {
   CUtensorMap tb;
   int rc = combine_b_tmap(&tb, p.B, p.H, W, p.b_sh, p.b_sk);
   if (rc) return rc;
   static unsigned attr_mask = 0;
-  const int smem = CombineSmem<W>::BYTES;
-  ensure_smem_limit(decode_combine_kernel<W>, smem, attr_mask);
+  const int smem = CombineSmem<W, TOK>::BYTES;
+  ensure_smem_limit(decode_combine_kernel<W, TOK>, smem, attr_mask);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.H, (p.T + kCTok - 1) / kCTok);
+  cfg.gridDim = dim3(p.H, (p.T + TOK - 1) / TOK);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -330,14 +338,26 @@ static int launch_combine(const CombineParams& p, bool pdl, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_combine_kernel<W>, tb, p), "decode_combine_kernel launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_combine_kernel<W, TOK>, tb, p), "decode_combine_kernel launch");
+}
+
+// The 16-token form when the exact part comes from outside and the 8-token grid would not fit in one
+// wave (one CTA per SM: its shared memory holds all of B[h])
+static bool combine_wide(const CombineParams& p) {
+  if (!p.chunk_o) return false;
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
+  return static_cast<int64_t>(p.H) * ((p.T + kCTok - 1) / kCTok) > sms[dev];
 }
 
 int decode_combine(const CombineParams& p, int W, bool pdl, cudaStream_t s) {
   if (p.T == 0) return kStatusOk;
+  const bool wide = combine_wide(p);
   switch (W) {
-    case 256: return launch_combine<256>(p, pdl, s);
-    case 512: return launch_combine<512>(p, pdl, s);
+    case 256: return wide ? launch_combine<256, kCTokWide>(p, pdl, s) : launch_combine<256, kCTok>(p, pdl, s);
+    case 512: return wide ? launch_combine<512, kCTokWide>(p, pdl, s) : launch_combine<512, kCTok>(p, pdl, s);
     default: set_error("decode combine width %d unsupported (256 or 512)", W); return kStatusInvalid;
   }
 }

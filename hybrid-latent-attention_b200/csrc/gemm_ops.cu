@@ -142,7 +142,7 @@ int writer(const WriterParams& p, cudaStream_t s) {
 // -------------------------------------------------------------------- prepare
 // CTA x < W/64: latent query columns [32x, 32x+32) and their RoPE partners [W/2 + 32x, ...).
 // CTAs x >= W/64 (when the exact part is enabled): exact RoPE + exact-cache append of head h,
-// 16 tokens each, every load of a thread issued at once.
+// 16 tokens each, every load of a thread issued at once.  With exact_only the grid holds only those.
 template <int W>
 __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
   __shared__ __align__(128) uint8_t qs[64 * 256];   // q tile [64 tokens][128] bf16
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
   __shared__ __align__(16) __nv_bfloat16 cs_s[64][64];  // RoPE rows of the tile: [token][cos 32 | sin 32]
   __shared__ int64_t pos_s[64];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const int x = blockIdx.x, h = blockIdx.y, t0 = blockIdx.z * 64;
+  const int x = blockIdx.x + (p.exact_only ? W / 64 : 0), h = blockIdx.y, t0 = blockIdx.z * 64;
   constexpr int HALF = W / 2;
   // a history split launched as this grid's programmatic dependent may start streaming pages now;
   // it reads q_lat only after this grid has completed.  Launched early itself (PrepareParams::pdl),
@@ -276,7 +276,11 @@ __global__ void __launch_bounds__(128) prepare_kernel(const PrepareParams p) {
 int prepare(const PrepareParams& p, cudaStream_t s) {
   if (p.T == 0) return kStatusOk;
   const int extra = p.k ? 4 : 0;  // exact-part CTAs per (head, 64-token block): 16 tokens each
-  dim3 grid(p.W / 64 + extra, p.H, (p.T + 63) / 64);
+  if (p.exact_only && !p.k) {
+    set_error("prepare: the exact part alone needs k");
+    return kStatusInvalid;
+  }
+  dim3 grid(p.exact_only ? extra : p.W / 64 + extra, p.H, (p.T + 63) / 64);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(128);

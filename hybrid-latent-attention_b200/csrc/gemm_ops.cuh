@@ -61,6 +61,7 @@ struct PrepareParams {
   int R;
   int64_t* slot_out;
   bool pdl;  // launch as a programmatic dependent of the preceding launch (the kernel waits for it)
+  bool exact_only;  // run only the exact part's CTAs (k != NULL): no latent query, q_lat untouched
 };
 
 int writer(const WriterParams& p, cudaStream_t s);

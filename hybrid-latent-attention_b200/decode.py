@@ -86,16 +86,25 @@ class S6DecodeModel:
     (it streams pages while the prepare runs and reads q_lat after it), and the combine (or the
     sequence split's reduce) as one of the history split.  ``pdl=False`` serialises every launch;
     the results are bit-identical.
+
+    ``window_overlap``: the exact window runs as its own kernel on a side stream, beside the history
+    split, and the combine takes it as an external exact part (16 tokens per CTA when its grid
+    exceeds one wave).  ``None`` (default) turns it on when the fused combine's grid (heads x
+    ceil(B / 8) CTAs, one per SM) would not fit in one wave - e.g. 256 requests - and leaves the
+    window inside the combine otherwise.
     """
 
     def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
-                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=False, pdl=True):
+                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=None, pdl=True):
         self.s, self.device = shape, torch.device(device)
-        self.window_overlap = window_overlap
         self.pdl = pdl
         s = shape
         B = len(batch.ctx)
         self.B = B
+        if window_overlap is None:
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            window_overlap = s.heads * -(-B // 8) > sms
+        self.window_overlap = bool(window_overlap)
         g = torch.Generator(device=self.device).manual_seed(seed)
         gen = lambda *shape_, std=1.0, dtype=BF16: (torch.randn(*shape_, generator=g, device=self.device) * std).to(dtype)
         ctx = torch.tensor(batch.ctx, dtype=torch.int64)
@@ -315,17 +324,25 @@ class S6DecodeModel:
         q_lat = self.q_lat[..., :width] if width != s.rank else self.q_lat
         ex = self.exact_logical[layer][loop]
         qr = self.q_rope
-        _lib.call('hla_s6_decode_prepare', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(A), A.stride(0),
-                  A.stride(1), _lib.ptr(self.positions), _lib.ptr(table), table.stride(0), table.shape[0],
-                  _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), B, s.heads, s.head_dim, width, _lib.ptr(qr),
-                  qr.stride(0), qr.stride(1), _lib.ptr(k), k.stride(0), k.stride(1), _lib.ptr(v), v.stride(0),
-                  v.stride(1), _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0], _lib.ptr(ex),
-                  ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
-                  self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B, None,
-                  _lib.PREPARE_EARLY_LAUNCH if self.pdl else 0, stream)
-        # 2b. (window_overlap) exact window on a side stream, beside the history kernel (it needs prepare's
-        #     q_rope and appended row only); the combine then takes it as its external exact part.  Measured
-        #     slower than the window inside the combine (config 2: 18.3 vs 17.2 ms per step), so off by default
+
+        def prepare(kv, flags, strm):
+            k_, v_ = kv
+            _lib.call('hla_s6_decode_prepare', _lib.ptr(q), q.stride(0), q.stride(1), _lib.ptr(A), A.stride(0),
+                      A.stride(1), _lib.ptr(self.positions), _lib.ptr(table), table.stride(0), table.shape[0],
+                      _lib.ptr(q_lat), q_lat.stride(0), q_lat.stride(1), B, s.heads, s.head_dim, width, _lib.ptr(qr),
+                      qr.stride(0), qr.stride(1), _lib.ptr(k_), k.stride(0), k.stride(1), _lib.ptr(v_), v.stride(0),
+                      v.stride(1), _lib.ptr(self.cos_sin), self.cos_sin.stride(0), self.cos_sin.shape[0],
+                      _lib.ptr(ex), ex.shape[0], ex.stride(0), ex.stride(1), ex.stride(2), s.page,
+                      _lib.ptr(self.exact_table), self.exact_table.stride(0), self.exact_table.shape[1],
+                      _lib.ptr(self.qsl), B, None, flags, strm)
+
+        early = _lib.PREPARE_EARLY_LAUNCH if self.pdl else 0
+        # 2b. (window_overlap) the exact part and the exact window on a side stream, beside the history
+        #     kernel: they need only this step's q, k, v and the exact cache, and the combine then takes the
+        #     window as its external exact part.  The side stream forks after the previous combine (which
+        #     was the last reader of q_rope and of the window buffers), so only the latent query stays ahead
+        #     of the history split.  On by default when the fused combine needs more than one wave (config 4's
+        #     256 requests); with one wave it gains nothing (config 2).
         win_done = None
         if self.window_overlap:
             main = torch.cuda.current_stream(self.device)
@@ -334,17 +351,20 @@ class S6DecodeModel:
             fork = torch.cuda.Event()
             fork.record(main)
             self._win_stream.wait_event(fork)
+            side = _lib.ctypes.c_void_p(self._win_stream.cuda_stream)
+            prepare((k, v), _lib.PREPARE_EXACT_ONLY, side)
             _lib.call('hla_s6_window_attention', _lib.ptr(qr), qr.stride(0), qr.stride(1), _lib.ptr(ex), ex.shape[0],
                       ex.stride(0), ex.stride(1), ex.stride(2), s.page, _lib.ptr(self.exact_table),
                       self.exact_table.stride(0), self.exact_table.shape[1], _lib.ptr(self.qsl), B,
                       _lib.ptr(self.seq_lens), s.window, float(self.scale), B, s.heads, s.head_dim,
-                      _lib.ptr(self.win_o), self.win_o.stride(0), self.win_o.stride(1), _lib.ptr(self.win_lse),
-                      _lib.ctypes.c_void_p(self._win_stream.cuda_stream))
+                      _lib.ptr(self.win_o), self.win_o.stride(0), self.win_o.stride(1), _lib.ptr(self.win_lse), side)
             win_done = torch.cuda.Event()
             win_done.record(self._win_stream)
+            prepare((None, None), early, stream)       # the latent query alone
+        else:
+            prepare((k, v), early, stream)
         # 3. history split, a programmatic dependent of the prepare just launched (pages stream meanwhile;
-        #    q_lat is read once the prepare has completed).  The side-stream window, when on, sits between
-        #    them in host order only, on another stream.
+        #    q_lat is read once the prepare has completed).
         self._history(layer, loop, stream, _lib.PARTIALS_AFTER_QUERY if self.pdl else 0)
         # 3b. sequence split: reduce this GPU's slice to (z, lse) and all-gather the parts
         z_in = lse_in = None
@@ -394,9 +414,9 @@ class S6DecodeModel:
 
     def launches_per_step(self):
         """Launches of this library per step (the sequence split adds one reduce per (layer, loop), the
-        side-stream window one window kernel)."""
+        side-stream window an exact-part prepare and a window kernel)."""
         s = self.s
-        return s.layers * s.loops * (4 + (self.exchange is not None) + bool(self.window_overlap))
+        return s.layers * s.loops * (4 + (self.exchange is not None) + 2 * bool(self.window_overlap))
 
     def step(self, overlap_writer=True):
         """One decode step.  With ``overlap_writer`` the writer launches run on a side stream forked from

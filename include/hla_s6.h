@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define HLA_S6_ABI_VERSION 3
+#define HLA_S6_ABI_VERSION 4
 #define HLA_S6_OK 0
 #define HLA_S6_EINVAL 1
 #define HLA_S6_EOVERFLOW 2
@@ -281,8 +281,13 @@ int hla_s6_exact_append(void* q, int64_t q_stride_t, int64_t q_stride_h, const v
  * preceding launch on the stream: its CTAs are staged before that launch completes and wait for it
  * before they read or write memory, which hides the launch gap.  A history split launched after it
  * with HLA_S6_PARTIALS_AFTER_QUERY may then start streaming before that preceding launch has
- * completed, so the block table and ctx the split reads must not be written by it. */
+ * completed, so the block table and ctx the split reads must not be written by it.
+ * HLA_S6_PREPARE_EXACT_ONLY runs the exact part alone (k required; q_lat is not written, A is not
+ * read), so that a caller can put the exact part on another stream than the latent query, e.g.
+ * beside the history split with the window kernel after it; the latent query alone is the same call
+ * with k = NULL. */
 #define HLA_S6_PREPARE_EARLY_LAUNCH 1
+#define HLA_S6_PREPARE_EXACT_ONLY 2
 int hla_s6_decode_prepare(const void* q_pre, int64_t q_stride_t, int64_t q_stride_h, const void* A,
                           int64_t a_stride_h, int64_t a_stride_k, const int64_t* positions, const void* table,
                           int64_t table_stride, int64_t max_position, void* q_lat, int64_t q_lat_stride_t,

@@ -33,6 +33,31 @@ def test_side_stream_window_matches_fused_window():
     assert torch.equal(side.out, eager)
 
 
+def test_many_requests_side_window_and_sixteen_token_combine():
+    """201 requests: the fused combine would need 16 x 26 CTAs (more than one wave), so by default the
+    window runs beside the history kernel and the combine takes 16 tokens per CTA (the last CTA of each
+    head holds 9).  It agrees with the one-wave arrangement (window inside an 8-token combine), eagerly
+    and under graph replay."""
+    dec = pkg('decode')
+    shape = dec.OuroShape(layers=1)
+    ctx = [(37 * i * i + 11 * i) % 3000 for i in range(201)]
+    ctx[:4] = [0, 1, 31, 32]
+    auto = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=13)
+    fused = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=13, window_overlap=False)
+    assert auto.window_overlap and not fused.window_overlap
+    auto.step()
+    fused.step()
+    torch.cuda.synchronize()
+    assert torch.isfinite(auto.out.float()).all()
+    torch.testing.assert_close(auto.out.float(), fused.out.float(), atol=2e-2, rtol=1e-2)
+    eager = auto.out.clone()
+    g = auto.capture()
+    auto.out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(auto.out, eager)
+
+
 def test_programmatic_launches_match_serial_launches():
     """The step's programmatic dependent launches (history split beside the prepare that writes q_lat,
     combine beside the history split) give bit-identical outputs to fully serialised launches, for

@@ -362,6 +362,35 @@ def test_decode_prepare_fuses_latent_query_and_exact_append():
             np.testing.assert_array_equal(flat[want[t], :, d:], v[t])
     untouched = np.setdiff1d(np.arange(nb * page), want[want >= 0])
     assert np.isnan(flat[untouched]).all()
+    # the same work as two launches on two streams - the latent query alone (k = NULL) and the exact part
+    # alone (HLA_S6_PREPARE_EXACT_ONLY) - gives bit-identical q_lat, q_rope, cache rows and slots
+    q_lat2, q_rope2 = torch.full_like(q_lat, float('nan')), torch.full_like(q_rope, float('nan'))
+    cache2 = torch.full_like(cache, float('nan'))
+    logical2 = cache2.transpose(1, 2)
+    slots2 = torch.full_like(slots, -7)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    for kv, flags, strm in (((None, None), 0, lib.stream_of(qd)),
+                            ((kd, vd), lib.PREPARE_EXACT_ONLY, lib.ctypes.c_void_p(side.cuda_stream))):
+        lib.call('hla_s6_decode_prepare', lib.ptr(qd), qd.stride(0), qd.stride(1), lib.ptr(Ad), Ad.stride(0),
+                 Ad.stride(1), lib.ptr(posd), lib.ptr(ltab), ltab.stride(0), ltab.shape[0], lib.ptr(q_lat2),
+                 q_lat2.stride(0), q_lat2.stride(1), T, H, d, W, lib.ptr(q_rope2), q_rope2.stride(0),
+                 q_rope2.stride(1), lib.ptr(kv[0]), kd.stride(0), kd.stride(1), lib.ptr(kv[1]), vd.stride(0),
+                 vd.stride(1), lib.ptr(cos_sin), cos_sin.stride(0), cos_sin.shape[0], lib.ptr(logical2), nb,
+                 logical2.stride(0), logical2.stride(1), logical2.stride(2), page, lib.ptr(btd), btd.stride(0),
+                 btd.shape[1], lib.ptr(qsl), R, lib.ptr(slots2), flags, strm)
+    torch.cuda.synchronize()
+    assert torch.equal(q_lat2, q_lat) and torch.equal(q_rope2, q_rope) and torch.equal(slots2, slots)
+    assert torch.equal(cache2.isnan(), cache.isnan())
+    assert torch.equal(torch.nan_to_num(cache2), torch.nan_to_num(cache))
+    with pytest.raises(ValueError, match='exact part alone needs k'):
+        lib.call('hla_s6_decode_prepare', lib.ptr(qd), qd.stride(0), qd.stride(1), lib.ptr(Ad), Ad.stride(0),
+                 Ad.stride(1), lib.ptr(posd), lib.ptr(ltab), ltab.stride(0), ltab.shape[0], lib.ptr(q_lat2),
+                 q_lat2.stride(0), q_lat2.stride(1), T, H, d, W, lib.ptr(q_rope2), q_rope2.stride(0),
+                 q_rope2.stride(1), None, 0, 0, None, 0, 0, lib.ptr(cos_sin), cos_sin.stride(0), cos_sin.shape[0],
+                 lib.ptr(logical2), nb, logical2.stride(0), logical2.stride(1), logical2.stride(2), page,
+                 lib.ptr(btd), btd.stride(0), btd.shape[1], lib.ptr(qsl), R, None, lib.PREPARE_EXACT_ONLY,
+                 lib.stream_of(qd))
 
 
 def test_probe_latent_rope_checks_the_b200_kernel():

@@ -50,4 +50,4 @@ def test_c_host_compiles_links_and_gets_status_codes():
         assert cc.returncode == 0, cc.stderr
         run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
         assert run.returncode == 0, (run.returncode, run.stdout, run.stderr)
-        assert run.stdout.strip() == 'ok 3'
+        assert run.stdout.strip() == f'ok {pkg("_lib").ABI_VERSION}'
