@@ -56,6 +56,7 @@ METRIC_CONTIG = 'contiguous-layout latent history reader tokens/s and HBM GB/s (
 METRIC_EXPORT = 'rollout cache export rows/s and HBM GB/s (% roofline), one 8192-token request, 24 layers'
 METRIC_HEADS = 'per-head (LLA MLA-style) latent history reader tokens/s and HBM GB/s (% roofline), B=64 ctx 8K'
 FALLBACK_TFLOPS = 1400.0
+WINDOW_MODES = {'auto': None, 'on': True, 'off': False}
 
 
 def dist_env():
@@ -433,7 +434,8 @@ def run_ours(args):
     shape = dec.OuroShape(max_position=max_pos)
     exchange = (rank, world, dist.group.WORLD) if (args.config == 5 and world > 1) else None
     model = dec.S6DecodeModel(shape, dec.DecodeBatch(ctx), device='cuda', seed=args.seed + rank,
-                              latent_rows=latent_rows, exchange=exchange, exchange_mode=args.exchange)
+                              latent_rows=latent_rows, exchange=exchange, exchange_mode=args.exchange,
+                              window_overlap=WINDOW_MODES[args.side_window])
     torch.cuda.synchronize()
     model.step()                       # eager warm-up: descriptor caches, occupancy
     graph = model.capture()
@@ -523,7 +525,8 @@ def run_ours(args):
                                         if args.exchange == 'peer' else
                                         f'sequence-split x{world} (NCCL all_gather per layer x loop)')
                                        if exchange is not None else f'request-partitioned x{world} (no collectives)'),
-                       'l2': 'inputs larger than L2 (latent caches ~40 GB per GPU), no flush'},
+                       'l2': 'inputs larger than L2 (latent caches ~40 GB per GPU), no flush',
+                       'side_window': model.window_overlap},
             'latent_history': {'bytes_per_step': bytes_hist, 'GBps_in_step': bytes_hist / (ms_step / 1e3) / 1e9,
                                'attention_bytes_per_step': attn_bytes,
                                'attention_GBps': attn_bytes / (ms_step / 1e3) / 1e9,
@@ -674,7 +677,7 @@ def run_full(args):
     dec = importlib.import_module(f'{PKG}.decode')
     ctx, scaling, _, max_pos = config_batch(2, rank, world, args.seed)
     model = dec.S6DecodeModel(dec.OuroShape(max_position=max_pos), dec.DecodeBatch(ctx), device='cuda',
-                              seed=args.seed + rank)
+                              seed=args.seed + rank, window_overlap=WINDOW_MODES[args.side_window])
     native_ms = None
     if args.dropin:
         # the native step of the same build first, on the same model and weights, for comparison
@@ -1226,8 +1229,9 @@ def _graph_ms(torch, graph, reps):
 def run_profile(args):
     """--profile CASE: a few eager steps of one workload, small enough for ncu (a few GB on the device).
 
-    decode     the four launches per (layer, loop) of S6DecodeModel.step in order (writer, prepare, history
-               split, combine; loop 0 reads the 256-wide latent, loops 1-3 the 512-wide one), so
+    decode     the launches per (layer, loop) of S6DecodeModel.step in order (writer, prepare, history
+               split, combine, plus the side-stream exact part and window for batches whose fused combine would
+               exceed one wave; loop 0 reads the 256-wide latent, loops 1-3 the 512-wide one), so
                ``ncu -k regex:history_split -s 1 -c 2`` selects one launch of each width (2 layers: ~3 GB)
     prefill    the config-3 prompt-step writer (prefill.PrefillWriter: four writer launches per layer,
                N = 512 at loop 0 and 1024 at loops 1-3, 4096 tokens per prompt; 1 layer x 8 prompts: ~1 GB)
@@ -1336,6 +1340,9 @@ def main():
     ap.add_argument('--exchange', default='peer', choices=['peer', 'nccl'],
                     help='config 5 on several GPUs: how the (z, lse) parts move')
     ap.add_argument('--no-cpu', action='store_true', help='skip the CPU baseline leg')
+    ap.add_argument('--side-window', default='auto', choices=sorted(WINDOW_MODES),
+                    help='decode configs: exact part and window on a side stream beside the history split '
+                         '(S6DecodeModel window_overlap; auto = when the fused combine would exceed one wave)')
     ap.add_argument('--dropin', action='store_true',
                     help='--config full: run the attention through the drop-in mirror of the adapter (ouro_attention)')
     prof = ap.add_argument_group('profiler workloads (--profile CASE; no JSON line, for ncu)')

@@ -87,11 +87,14 @@ class S6DecodeModel:
     sequence split's reduce) as one of the history split.  ``pdl=False`` serialises every launch;
     the results are bit-identical.
 
-    ``window_overlap``: the exact window runs as its own kernel on a side stream, beside the history
-    split, and the combine takes it as an external exact part (16 tokens per CTA when its grid
-    exceeds one wave).  ``None`` (default) turns it on when the fused combine's grid (heads x
-    ceil(B / 8) CTAs, one per SM) would not fit in one wave - e.g. 256 requests - and leaves the
-    window inside the combine otherwise.
+    ``window_overlap``: the exact part of the prepare (exact RoPE, exact-cache append) and the exact
+    window run on a side stream, beside the history split, so that only the latent query stays ahead
+    of the split; the combine takes the window as an external exact part (16 tokens per CTA when its
+    grid exceeds one wave).  ``None`` (default) turns it on when the fused combine's grid (heads x
+    ceil(B / 8) CTAs, one per SM) would exceed one wave, without a sequence split, and keeps the
+    window inside the combine otherwise.  Measured on one GPU: 256 requests (config 4) 51.4 -> 47.1 ms
+    per step, end to end with host copies 4999 -> 5269 tokens/s; 64 requests (config 2) within 0.7%
+    on the device but 3% slower end to end (3963 -> 3850 tokens/s); 4 requests (config 5) unchanged.
     """
 
     def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
@@ -103,7 +106,7 @@ class S6DecodeModel:
         self.B = B
         if window_overlap is None:
             sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-            window_overlap = s.heads * -(-B // 8) > sms
+            window_overlap = exchange is None and s.heads * -(-B // 8) > sms
         self.window_overlap = bool(window_overlap)
         g = torch.Generator(device=self.device).manual_seed(seed)
         gen = lambda *shape_, std=1.0, dtype=BF16: (torch.randn(*shape_, generator=g, device=self.device) * std).to(dtype)
@@ -291,8 +294,9 @@ class S6DecodeModel:
                   width, s.page, float(self.scale), self.splits, _lib.ptr(self.ws), self.ws_floats, None, flags, stream)
 
     def layer_loop(self, layer, loop, stream, wstream=None, io=None):
-        """The four launches of one (layer, loop); the writer goes to ``wstream`` when given (it reads only
-        ``h`` and feeds only the commit and the next loop's writer, so it overlaps the attention chain).
+        """The launches of one (layer, loop) (four, or six with the side-stream exact part and window); the
+        writer goes to ``wstream`` when given (it reads only ``h`` and feeds only the commit and the next
+        loop's writer, so it overlaps the attention chain).
         ``io = (q, k, v, h, out)`` takes the pre-RoPE q, k, v ``[B, H, d]`` (any token / head strides), the
         attention input ``h [B, hidden]`` and the output ``[B, H, d]`` from the caller - a dense body around
         the attention - instead of the resident activation and output buffers."""
@@ -341,8 +345,8 @@ class S6DecodeModel:
         #     kernel: they need only this step's q, k, v and the exact cache, and the combine then takes the
         #     window as its external exact part.  The side stream forks after the previous combine (which
         #     was the last reader of q_rope and of the window buffers), so only the latent query stays ahead
-        #     of the history split.  On by default when the fused combine needs more than one wave (config 4's
-        #     256 requests); with one wave it gains nothing (config 2).
+        #     of the history split.  On by default when the fused combine would exceed one wave (see the class
+        #     notes).
         win_done = None
         if self.window_overlap:
             main = torch.cuda.current_stream(self.device)

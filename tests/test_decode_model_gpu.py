@@ -34,10 +34,10 @@ def test_side_stream_window_matches_fused_window():
 
 
 def test_many_requests_side_window_and_sixteen_token_combine():
-    """201 requests: the fused combine would need 16 x 26 CTAs (more than one wave), so by default the
-    window runs beside the history kernel and the combine takes 16 tokens per CTA (the last CTA of each
-    head holds 9).  It agrees with the one-wave arrangement (window inside an 8-token combine), eagerly
-    and under graph replay."""
+    """201 requests: by default the exact part and the window run beside the history kernel, and the
+    combine, whose 8-token grid (16 x 26 CTAs) would exceed one wave, takes 16 tokens per CTA (the last
+    CTA of each head holds 9).  It agrees with the window inside an 8-token combine, eagerly and under
+    graph replay."""
     dec = pkg('decode')
     shape = dec.OuroShape(layers=1)
     ctx = [(37 * i * i + 11 * i) % 3000 for i in range(201)]
