@@ -667,6 +667,10 @@ __global__ void __launch_bounds__(kReduceThreads, 1) history_reduce_kernel(const
                                                                          float* __restrict__ out_f32,
                                                                          float* __restrict__ lse_out,
                                                                          int64_t lse_st, int64_t lse_sh) {
+  // launched as a programmatic dependent of the split: it waits for the split grid before its first
+  // read, and lets its own dependent (a combine, which waits for this grid before it reads z) start now
+  griddep_launch_dependents();
+  griddep_wait();
   const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   float lse;
   const float4 acc = reduce_row<W>(ws_o, ws_lse, meta, stream_mode, t, h, H, empty, lse);
@@ -1108,19 +1112,31 @@ int history_reduce_strided(const HistoryArgs& a, const HistoryPlan& plan, const 
     }
     return cuda_status(e, "history_reduce_warp_kernel launch");
   }
-  dim3 grid(a.T, a.H, a.W / (4 * kReduceCols));
-#define HLA_REDUCE(WW)                                                                                          \
-  history_reduce_kernel<WW><<<grid, kReduceThreads, 0, stream>>>(plan.ws_o, plan.ws_lse, plan.meta,             \
-                                                                 plan.stream_mode, a.T, a.H, empty,             \
-                                                                 static_cast<__nv_bfloat16*>(out), o_st, o_sh, \
-                                                                 out_f32, lse, lse_st, lse_sh)
+  // many partials per row (a few rows over the whole GPU): block-cooperative, also a programmatic
+  // dependent of the split
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.T, a.H, a.W / (4 * kReduceCols));
+  cfg.blockDim = dim3(kReduceThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  cudaError_t e;
   switch (a.W) {
-    case 256: HLA_REDUCE(256); break;
-    case 512: HLA_REDUCE(512); break;
-    default: HLA_REDUCE(1024); break;
+    case 256: e = cudaLaunchKernelEx(&cfg, history_reduce_kernel<256>, plan.ws_o, plan.ws_lse, plan.meta,
+                                     plan.stream_mode, a.T, a.H, empty, o, o_st, o_sh, out_f32, lse, lse_st, lse_sh);
+      break;
+    case 512: e = cudaLaunchKernelEx(&cfg, history_reduce_kernel<512>, plan.ws_o, plan.ws_lse, plan.meta,
+                                     plan.stream_mode, a.T, a.H, empty, o, o_st, o_sh, out_f32, lse, lse_st, lse_sh);
+      break;
+    default: e = cudaLaunchKernelEx(&cfg, history_reduce_kernel<1024>, plan.ws_o, plan.ws_lse, plan.meta,
+                                    plan.stream_mode, a.T, a.H, empty, o, o_st, o_sh, out_f32, lse, lse_st, lse_sh);
+      break;
   }
-#undef HLA_REDUCE
-  return cuda_status(cudaGetLastError(), "history_reduce_kernel launch");
+  return cuda_status(e, "history_reduce_kernel launch");
 }
 
 int history_reduce_exchange(const HistoryArgs& a, const HistoryPlan& plan, const uint8_t* empty,

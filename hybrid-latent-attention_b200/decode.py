@@ -95,19 +95,28 @@ class S6DecodeModel:
     window inside the combine otherwise.  Measured on one GPU: 256 requests (config 4) 51.4 -> 47.1 ms
     per step, end to end with host copies 4999 -> 5269 tokens/s; 64 requests (config 2) within 0.7%
     on the device but 3% slower end to end (3963 -> 3850 tokens/s); 4 requests (config 5) unchanged.
+
+    ``reduce_first``: the history split's partials are reduced by the block-cooperative reduce kernel
+    into one fp32 part that the combine merges, instead of inside the combine (one warp per (row,
+    head) walking all of the row's partials).  ``None`` (default) turns it on without a sequence split
+    when the split leaves more than about 16 partials per row (fewer than ~18 requests on a B200).
     """
 
     def __init__(self, shape: OuroShape, batch: DecodeBatch, device='cuda', seed=0, split_max_tokens=512,
-                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=None, pdl=True):
+                 latent_rows=None, exchange=None, exchange_mode='peer', window_overlap=None, pdl=True,
+                 reduce_first=None):
         self.s, self.device = shape, torch.device(device)
         self.pdl = pdl
         s = shape
         B = len(batch.ctx)
         self.B = B
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         if window_overlap is None:
-            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
             window_overlap = exchange is None and s.heads * -(-B // 8) > sms
         self.window_overlap = bool(window_overlap)
+        if reduce_first is None:       # more than ~16 stream-K partials per row (the split runs 2 CTAs per SM)
+            reduce_first = exchange is None and 2 * sms > 16 * B
+        self.reduce_first = bool(reduce_first)
         g = torch.Generator(device=self.device).manual_seed(seed)
         gen = lambda *shape_, std=1.0, dtype=BF16: (torch.randn(*shape_, generator=g, device=self.device) * std).to(dtype)
         ctx = torch.tensor(batch.ctx, dtype=torch.int64)
@@ -185,6 +194,8 @@ class S6DecodeModel:
         self.reg = [torch.empty(B, 2 * s.rank, dtype=BF16, device=self.device) for _ in range(s.layers)]
         self.exchange_mode = exchange_mode
         self.x_bases = None
+        if self.reduce_first:          # the reduced history part (z fp32 [B, H, W], lse [H, B]) the combine merges
+            self.zpart = torch.empty(B * s.heads * s.rank + s.heads * B, dtype=torch.float32, device=self.device)
         if exchange is not None and exchange_mode not in ('peer', 'nccl'):
             raise ValueError(f'unknown exchange mode {exchange_mode!r}')
         if exchange is not None and exchange_mode == 'peer':
@@ -390,6 +401,15 @@ class S6DecodeModel:
             lse_in = ctypes.c_void_p(own + B * s.heads * width * wb)
             x_epoch, part_seen = epoch, _lib.ptr(self.x_counters[2 * i + 1])
             parts, flags = world, after   # its producer is the reduce just launched
+        elif self.reduce_first:
+            # few rows over the whole GPU (config 5 on one GPU: ~75 partials per row): the block-cooperative
+            # reduce first, then the combine merges its single part, instead of one warp walking every
+            # partial of a (row, head) inside the combine
+            zf = B * s.heads * width
+            z_in, lse_in = self.zpart[:zf], self.zpart[zf:zf + s.heads * B]
+            _lib.call('hla_s6_history_reduce', B, s.heads, width, s.page, self.splits, _lib.ptr(self.ws),
+                      self.ws_floats, None, None, 0, 0, _lib.ptr(z_in), _lib.ptr(lse_in), stream)
+            parts, part_stride, flags = 1, zf + s.heads * B, after      # its producer is the reduce just launched
         elif self.exchange is not None:
             rank, world, group = self.exchange
             zf = B * s.heads * width
@@ -420,7 +440,8 @@ class S6DecodeModel:
         """Launches of this library per step (the sequence split adds one reduce per (layer, loop), the
         side-stream window an exact-part prepare and a window kernel)."""
         s = self.s
-        return s.layers * s.loops * (4 + (self.exchange is not None) + 2 * bool(self.window_overlap))
+        return s.layers * s.loops * (4 + (self.exchange is not None or self.reduce_first) +
+                                     2 * bool(self.window_overlap))
 
     def step(self, overlap_writer=True):
         """One decode step.  With ``overlap_writer`` the writer launches run on a side stream forked from

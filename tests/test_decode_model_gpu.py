@@ -58,6 +58,29 @@ def test_many_requests_side_window_and_sixteen_token_combine():
     assert torch.equal(auto.out, eager)
 
 
+def test_few_requests_reduce_before_the_combine():
+    """4 long requests (about 75 stream-K partials per row): by default the block-cooperative reduce merges
+    the partials before the combine, which then merges one part.  It agrees with the in-combine reduce
+    (one warp per (row, head) over all partials), eagerly and under graph replay."""
+    dec = pkg('decode')
+    shape = dec.OuroShape(layers=1)
+    batch = dec.DecodeBatch([30000, 17, 12000, 0])
+    first = dec.S6DecodeModel(shape, batch, device='cuda', seed=21)
+    inside = dec.S6DecodeModel(shape, batch, device='cuda', seed=21, reduce_first=False)
+    assert first.reduce_first and not inside.reduce_first
+    first.step()
+    inside.step()
+    torch.cuda.synchronize()
+    assert torch.isfinite(first.out.float()).all()
+    torch.testing.assert_close(first.out.float(), inside.out.float(), atol=2e-2, rtol=1e-2)
+    eager = first.out.clone()
+    g = first.capture()
+    first.out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(first.out, eager)
+
+
 def test_programmatic_launches_match_serial_launches():
     """The step's programmatic dependent launches (history split beside the prepare that writes q_lat,
     combine beside the history split) give bit-identical outputs to fully serialised launches, for
