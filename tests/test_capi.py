@@ -94,3 +94,17 @@ def test_ops_reject_cpu_tensors_and_unknown_backends():
         ops.history_attention(q, cache, bt, ctx, 1.0, 1, ws, None, None, 'torch')
     with pytest.raises(ValueError, match='CUDA'):
         ops.history_attention(q, cache, bt, ctx, 1.0, 1, ws, None, None, 'b200')
+
+
+def test_python_constants_match_the_header_defines():
+    """Every status code, device error code, launch flag and size that _lib.py mirrors from
+    include/hla_s6.h carries the header's value."""
+    _lib = pkg('_lib')
+    defines = {m.group(1): int(m.group(2))
+               for m in re.finditer(r'^#define HLA_S6_(\w+)\s+(\d+)\s*$', HEADER.read_text(), re.M)}
+    mirrored = ['OK', 'EINVAL', 'EOVERFLOW', 'ECUDA', 'ERR_WAIT_COPY', 'ERR_WAIT_STAGE', 'ERR_RANGE', 'ERR_WAIT_PEER',
+                'ERR_BLOCK', 'COMBINE_AFTER_PARTIALS', 'PARTIALS_AFTER_QUERY', 'REDUCE_AFTER_PARTIALS',
+                'PREPARE_EARLY_LAUNCH', 'PREPARE_EXACT_ONLY', 'PEER_HANDLE_BYTES', 'EXCHANGE_WORD_BYTES']
+    for name in mirrored:
+        assert getattr(_lib, name) == defines[name], name
+    assert _lib.ABI_VERSION == defines['ABI_VERSION']
