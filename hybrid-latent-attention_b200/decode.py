@@ -84,8 +84,9 @@ class S6DecodeModel:
 
     ``pdl`` (default on): the history split is launched as a programmatic dependent of the prepare
     (it streams pages while the prepare runs and reads q_lat after it), and the combine (or the
-    sequence split's reduce) as one of the history split.  ``pdl=False`` serialises every launch;
-    the results are bit-identical.
+    sequence split's reduce) as one of the history split.  ``pdl=False`` serialises these launches
+    (the library's stage-2 reduce kernels are always programmatic dependents of the split and wait for
+    it before their first read); the results are bit-identical.
 
     ``window_overlap``: the exact part of the prepare (exact RoPE, exact-cache append) and the exact
     window run on a side stream, beside the history split, so that only the latent query stays ahead
