@@ -345,11 +345,11 @@ static int launch_combine(const CombineParams& p, bool pdl, cudaStream_t s) {
 // wave (one CTA per SM: its shared memory holds all of B[h])
 static bool combine_wide(const CombineParams& p) {
   if (!p.chunk_o) return false;
-  static int sms[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
-  return static_cast<int64_t>(p.H) * ((p.T + kCTok - 1) / kCTok) > sms[dev];
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    return false;
+  return static_cast<int64_t>(p.H) * ((p.T + kCTok - 1) / kCTok) > sms;
 }
 
 int decode_combine(const CombineParams& p, int W, bool pdl, cudaStream_t s) {
