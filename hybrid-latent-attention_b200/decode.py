@@ -48,6 +48,17 @@ class OuroShape:
     max_position: int = 65536
 
 
+def step_arrangement(requests, heads, sms, sequence_split):
+    """Default arrangement of a decode step's launches for ``requests`` rows on a GPU with ``sms`` SMs:
+    ``(window_overlap, reduce_first)``.  The side-stream exact part and window pay when the fused
+    combine's grid (heads x ceil(requests / 8) CTAs, one per SM) would exceed one wave; the reduce before
+    the combine pays when the history split (2 CTAs per SM) leaves more than about 16 partials per row.
+    Neither is used with a sequence split, whose reduce and combine exchange parts between GPUs."""
+    if sequence_split:
+        return False, False
+    return heads * -(-requests // 8) > sms, 2 * sms > 16 * requests
+
+
 def seq_split_rows(latent_rows, page, rank, world):
     """Sequence split of each request's latent history across ``world`` GPUs by whole pages: rank r holds
     pages ``[r * P // world, (r + 1) * P // world)`` of a request with P pages.  Returns, per request,
@@ -112,12 +123,9 @@ class S6DecodeModel:
         B = len(batch.ctx)
         self.B = B
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        if window_overlap is None:
-            window_overlap = exchange is None and s.heads * -(-B // 8) > sms
-        self.window_overlap = bool(window_overlap)
-        if reduce_first is None:       # more than ~16 stream-K partials per row (the split runs 2 CTAs per SM)
-            reduce_first = exchange is None and 2 * sms > 16 * B
-        self.reduce_first = bool(reduce_first)
+        auto_window, auto_reduce = step_arrangement(B, s.heads, sms, exchange is not None)
+        self.window_overlap = bool(auto_window if window_overlap is None else window_overlap)
+        self.reduce_first = bool(auto_reduce if reduce_first is None else reduce_first)
         g = torch.Generator(device=self.device).manual_seed(seed)
         gen = lambda *shape_, std=1.0, dtype=BF16: (torch.randn(*shape_, generator=g, device=self.device) * std).to(dtype)
         ctx = torch.tensor(batch.ctx, dtype=torch.int64)
