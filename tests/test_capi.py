@@ -108,3 +108,14 @@ def test_python_constants_match_the_header_defines():
     for name in mirrored:
         assert getattr(_lib, name) == defines[name], name
     assert _lib.ABI_VERSION == defines['ABI_VERSION']
+
+
+def test_prepare_exact_part_alone_needs_k(lib):
+    """HLA_S6_PREPARE_EXACT_ONLY without k is refused on the host (EINVAL) before any launch."""
+    _lib = pkg('_lib')
+    T, H, d, W = 1, 16, 128, 512
+    rc = lib.hla_s6_decode_prepare(None, 0, 0, None, 0, 0, None, None, W, 1, None, 0, 0, T, H, d, W, None, 0, 0,
+                                   None, 0, 0, None, 0, 0, None, 128, 1, None, 1, 0, 0, 0, 16, None, 0, 1, None, 1,
+                                   None, _lib.PREPARE_EXACT_ONLY, None)
+    assert rc == _lib.EINVAL
+    assert b'exact part alone needs k' in lib.hla_s6_last_error()
