@@ -1277,7 +1277,8 @@ def run_profile(args):
         torch.cuda.synchronize()
         print(f'ok: {args.profile_steps} prefill steps, {model.launches_per_step()} launches each')
         return
-    model = dec.S6DecodeModel(dec.OuroShape(layers=args.layers), dec.DecodeBatch([args.ctx] * args.batch),
+    model = dec.S6DecodeModel(dec.OuroShape(layers=args.layers, max_position=max(65536, args.ctx + 128)),
+                              dec.DecodeBatch([args.ctx] * args.batch),
                               device='cuda', seed=0)
     for _ in range(args.profile_steps):
         model.step(overlap_writer=False)
